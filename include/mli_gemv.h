@@ -1,0 +1,138 @@
+/*
+ * mli_gemv.h -- C ABI of the B200 (sm_100a) INT8 group-64 linear library
+ * (libmli_gemv.so).
+ *
+ * Every pointer is a caller-owned DEVICE pointer unless stated otherwise, and
+ * no entry point allocates or frees memory.  Layouts are the ones the
+ * MiniLlama-Infra weight file and forward pass use (scripts/quantize_int8_group.py:67-71,
+ * src/main_cuda.cpp:364-393, src/model_cuda_v2_shared.cu:384-412):
+ *
+ *   w_q  int8  [d][n]       row-major, one output row per row
+ *   w_s  fp32  [d][n / gs]  one scale per (row, group of gs columns)
+ *   x    fp32  [n]          activation (batch 1)     or [m][n] token-major
+ *   y    fp32  [d]          output                   or [m][d] token-major
+ *
+ * n = in-features (the reference's `n`), d = out-features (`d`), gs = group
+ * size (the reference's `group_size`; 64 everywhere in MiniLlama-Infra).
+ *
+ * Streams: `stream` is a cudaStream_t passed as void*; NULL is the legacy
+ * default stream, which the reference's <<<>>> launches use.
+ *
+ * Errors: every entry point returns MLI_OK (0) or an MLI_ERR_* code; a CUDA
+ * launch error is returned as MLI_ERR_CUDA and its cudaError_t is kept for
+ * mli_last_cuda_error().  The reference launchers (src/model_cuda_v2_shared.cu)
+ * return void and check nothing; the drop-in shim below keeps that signature
+ * and records the status for mli_last_status().
+ */
+#ifndef MLI_GEMV_H
+#define MLI_GEMV_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum mli_status_code {
+  MLI_OK = 0,
+  MLI_ERR_INVALID_ARG = 1, /* null pointer, non-positive size, bad count     */
+  MLI_ERR_UNSUPPORTED = 2, /* shape outside every kernel's limits            */
+  MLI_ERR_CUDA = 3,        /* a CUDA runtime call or launch failed           */
+  MLI_ERR_DEVICE = 4       /* a kernel gave up on a bounded wait (see below) */
+};
+
+/* Launch-option bits for mli_set_launch_flags(). */
+#define MLI_LAUNCH_PDL 1u /* programmatic dependent launch (default on) */
+
+/* ---- library state ------------------------------------------------------ */
+const char* mli_status_string(int status);
+int mli_last_status(void);            /* status of the last call on this thread */
+int mli_last_cuda_error(void);        /* cudaError_t behind the last MLI_ERR_CUDA */
+int mli_version(void);                /* MAJOR*10000 + MINOR*100 + PATCH */
+unsigned mli_get_launch_flags(void);
+void mli_set_launch_flags(unsigned flags);
+/* Reads and clears the device error word of the current device: 0 when no
+ * kernel gave up on a bounded wait since the last call. */
+int mli_device_error(unsigned* code_out);
+
+/* ---- batch-1 linear ops (the reference's matmul launchers) ------------- */
+
+/* y = W x with W = w_q * w_s (dequantised per group), fp32 activations.
+ * Replaces matmul_int8 (include/model.h:62; src/model_cuda_v2_shared.cu:36-69).
+ * fp32 result within max|y - y_ref| / max|y_ref| <= 1e-5 of the reference. */
+int mli_gemv_w8a32(float* y, const float* x, const int8_t* w_q,
+                   const float* w_s, int n, int d, int group_size,
+                   void* stream);
+
+/* Per-token dynamic activation quantisation, bit-identical to the reference:
+ * xs[0] = max(max|x| / 127, 1e-8); xq = clamp(rint(x * (1 / xs[0])), +-127).
+ * Replaces quantize_activation (include/model.h:64;
+ * src/model_cuda_v2_shared.cu:429-460). */
+int mli_quantize_activation(int8_t* xq, float* xs, const float* x, int n,
+                            void* stream);
+
+/* W8A8: y[r] = sum_g ((float)I[r][g] * w_s[r][g]) * xs[0], with I the exact
+ * int32 dot of group g of row r and xq.  Replaces matmul_dp4a
+ * (include/model.h:63; src/model_cuda_v2_shared.cu:462-509). */
+int mli_gemv_w8a8(float* y, const int8_t* xq, const float* xs,
+                  const int8_t* w_q, const float* w_s, int n, int d,
+                  int group_size, void* stream);
+
+/* W8A8 with the activation quantiser fused in as a prologue: every CTA
+ * quantises x itself, so one launch replaces the reference's pair
+ * quantize_activation + matmul_dp4a (src/model_cuda_v2_shared.cu:529-530).
+ * xq_out / xs_out may be NULL; when given they receive the same bytes
+ * mli_quantize_activation writes. */
+int mli_gemv_w8a8_fused(float* y, int8_t* xq_out, float* xs_out,
+                        const float* x, const int8_t* w_q, const float* w_s,
+                        int n, int d, int group_size, void* stream);
+
+/* ---- batched decode (m independent tokens, no reference counterpart) -- */
+
+/* Row-wise activation quantisation of m tokens: xs has m entries.  Each row
+ * is bit-identical to mli_quantize_activation of that row. */
+int mli_quantize_activation_rows(int8_t* xq, float* xs, const float* x, int m,
+                                 int n, void* stream);
+
+/* Y[t][r] = sum_g ((float)I[t][r][g] * w_s[r][g]) * xs[t] for m tokens.
+ * m >= 16 runs on the tcgen05 kind::i8 tensor-core path; smaller m on the
+ * CUDA-core path.  Each token's row is within the W8A8 tolerance of
+ * mli_gemv_w8a8 on that token. */
+int mli_gemm_w8a8(float* y, const int8_t* xq, const float* xs,
+                  const int8_t* w_q, const float* w_s, int m, int n, int d,
+                  int group_size, void* stream);
+
+/* ---- offline weight preparation ---------------------------------------- */
+
+/* Group-wise weight quantisation, bit-identical to
+ * scripts/quantize_int8_group.py:55-71: scale = max(amax, 1e-9) / 127 per
+ * (row, group), q = clip(round_half_even(w / scale), +-127). */
+int mli_quantize_weights(int8_t* w_q, float* w_s, const float* w, int rows,
+                         int cols, int group_size, void* stream);
+
+/* ---- diagnostics --------------------------------------------------------- */
+
+/* Exact int32 group dot products I[r][g] (d x n/gs), the values the W8A8
+ * kernels scale; for bit-exact parity tests. */
+int mli_debug_group_dots(int32_t* out, const int8_t* xq, const int8_t* w_q,
+                         int n, int d, int group_size, void* stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+
+/* ---- drop-in shim (libmli_dropin.so, C++ linkage) --------------------------
+ * Exactly the reference's launch signatures (include/model.h:62-64), so the
+ * reference's forward_cuda / forward_cuda_dp4a (src/model_cuda_v2_shared.cu:370-421,
+ * 514-566) link against this library unchanged once the reference's own
+ * definitions of these three functions are removed.  They launch on the legacy
+ * default stream like the reference and store their status for
+ * mli_last_status(). */
+void matmul_int8(float* xout, float* x, int8_t* w_q, float* w_s, int n, int d,
+                 int group_size);
+void matmul_dp4a(float* xout, const int8_t* x_q, const float* x_s,
+                 const int8_t* w_q, const float* w_s, int n, int d,
+                 int group_size);
+void quantize_activation(int8_t* xq, float* xs, const float* x, int n);
+#endif /* __cplusplus */
+
+#endif /* MLI_GEMV_H */

@@ -1,0 +1,106 @@
+"""Python face of the INT8 group-64 linear library, named like the reference.
+
+The reference launchers (src/model_cuda_v2_shared.cu, declared in
+include/model.h:62-64) take raw device pointers and sizes:
+
+    matmul_int8(xout, x, w_q, w_s, n, d, group_size)
+    matmul_dp4a(xout, x_q, x_s, w_q, w_s, n, d, group_size)
+    quantize_activation(xq, xs, x, n)
+
+These functions keep those names, argument orders and meanings, accept CUDA
+torch tensors (or raw device pointers as ints) and forward to the C ABI on the
+current torch stream.  Unlike the reference, which checks nothing, a failing
+call raises MliError.  torch is used only as a device-memory container.
+"""
+from __future__ import annotations
+
+import ctypes
+
+from ._lib import check, lib
+
+__all__ = [
+    "matmul_int8", "matmul_dp4a", "quantize_activation", "matmul_dp4a_fused",
+    "quantize_activation_rows", "gemm_w8a8", "quantize_weights", "group_dots",
+    "device_error", "set_pdl",
+]
+
+
+def _ptr(t):
+    if t is None:
+        return None
+    if isinstance(t, int):
+        return t
+    if not t.is_cuda:
+        raise ValueError("expected a CUDA tensor (device memory)")
+    if not t.is_contiguous():
+        raise ValueError("expected a contiguous tensor")
+    return t.data_ptr()
+
+
+def _stream(stream):
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+def matmul_int8(xout, x, w_q, w_s, n: int, d: int, group_size: int = 64, stream=None):
+    """W8A32 GEMV, xout[d] = dequant(w_q, w_s)[d][n] @ x[n] (reference :36-69)."""
+    check(lib().mli_gemv_w8a32(_ptr(xout), _ptr(x), _ptr(w_q), _ptr(w_s), n, d, group_size,
+                               _stream(stream)), "matmul_int8")
+
+
+def quantize_activation(xq, xs, x, n: int, stream=None):
+    """Per-token int8 quantisation of x[n] (reference :429-460)."""
+    check(lib().mli_quantize_activation(_ptr(xq), _ptr(xs), _ptr(x), n, _stream(stream)),
+          "quantize_activation")
+
+
+def matmul_dp4a(xout, x_q, x_s, w_q, w_s, n: int, d: int, group_size: int = 64, stream=None):
+    """W8A8 GEMV from an already-quantised activation (reference :462-509)."""
+    check(lib().mli_gemv_w8a8(_ptr(xout), _ptr(x_q), _ptr(x_s), _ptr(w_q), _ptr(w_s), n, d,
+                              group_size, _stream(stream)), "matmul_dp4a")
+
+
+def matmul_dp4a_fused(xout, x, w_q, w_s, n: int, d: int, group_size: int = 64,
+                      xq_out=None, xs_out=None, stream=None):
+    """W8A8 GEMV with the activation quantiser fused in (one launch)."""
+    check(lib().mli_gemv_w8a8_fused(_ptr(xout), _ptr(xq_out), _ptr(xs_out), _ptr(x), _ptr(w_q),
+                                    _ptr(w_s), n, d, group_size, _stream(stream)),
+          "matmul_dp4a_fused")
+
+
+def quantize_activation_rows(xq, xs, x, m: int, n: int, stream=None):
+    check(lib().mli_quantize_activation_rows(_ptr(xq), _ptr(xs), _ptr(x), m, n, _stream(stream)),
+          "quantize_activation_rows")
+
+
+def gemm_w8a8(y, xq, xs, w_q, w_s, m: int, n: int, d: int, group_size: int = 64, stream=None):
+    """Batched W8A8 for m tokens: y[m][d]."""
+    check(lib().mli_gemm_w8a8(_ptr(y), _ptr(xq), _ptr(xs), _ptr(w_q), _ptr(w_s), m, n, d,
+                              group_size, _stream(stream)), "gemm_w8a8")
+
+
+def quantize_weights(w_q, w_s, w, rows: int, cols: int, group_size: int = 64, stream=None):
+    """Group-wise weight quantisation (scripts/quantize_int8_group.py:55-71)."""
+    check(lib().mli_quantize_weights(_ptr(w_q), _ptr(w_s), _ptr(w), rows, cols, group_size,
+                                     _stream(stream)), "quantize_weights")
+
+
+def group_dots(out, xq, w_q, n: int, d: int, group_size: int = 64, stream=None):
+    check(lib().mli_debug_group_dots(_ptr(out), _ptr(xq), _ptr(w_q), n, d, group_size,
+                                     _stream(stream)), "group_dots")
+
+
+def device_error() -> int:
+    code = ctypes.c_uint(0)
+    lib().mli_device_error(ctypes.byref(code))
+    return int(code.value)
+
+
+def set_pdl(enabled: bool) -> None:
+    flags = lib().mli_get_launch_flags()
+    flags = (flags | 1) if enabled else (flags & ~1)
+    lib().mli_set_launch_flags(flags)

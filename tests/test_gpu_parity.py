@@ -1,0 +1,318 @@
+"""GPU parity of the CUDA kernels (through the C ABI) against the CPU oracle.
+
+Tolerances (the ones the path is specified with):
+  * int8 / index outputs (quantised activations, quantised weights, int32
+    group dots): bit-exact.
+  * W8A32 fp32 output: max|y - y_ref| / max|y_ref| <= 1e-5 against the
+    oracle (the reference's own arithmetic order) and the fp64 recompute.
+  * W8A8 fp32 output: <= 1e-6 of the fp64 recompute from the exact int32
+    group dots (sum_g I_g * ws * xs), and of the oracle.
+"""
+import numpy as np
+import pytest
+
+from oracle import oracle as orc
+from minillama_infra_b200 import ops, synth
+from minillama_infra_b200._lib import MliError, lib
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+TOL_W8A32 = 1e-5
+TOL_W8A8 = 1e-6
+GUARD = 64  # guard-band floats before and after every output
+
+
+def dev():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    return torch.device("cuda:0")
+
+
+def up(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev())
+
+
+class Guarded:
+    """Output buffer with canary bands on both sides."""
+
+    def __init__(self, n, dtype=torch.float32):
+        self.n = n
+        fill = float("nan") if dtype.is_floating_point else 0x5A
+        self.buf = torch.full((n + 2 * GUARD,), fill, dtype=dtype, device=dev())
+        self.t = self.buf[GUARD:GUARD + n]
+
+    def check(self):
+        head = self.buf[:GUARD].cpu().numpy()
+        tail = self.buf[GUARD + self.n:].cpu().numpy()
+        if self.buf.dtype.is_floating_point:
+            assert np.all(np.isnan(head)) and np.all(np.isnan(tail)), "guard band overwritten"
+        else:
+            assert np.all(head == 0x5A) and np.all(tail == 0x5A), "guard band overwritten"
+        return self.t.cpu().numpy()
+
+
+def make_case(d, n, seed, outliers=False):
+    w_q, w_s = orc.quantize_weights(synth.weights_np(d, n, seed))
+    x = synth.activation_np(n, seed + 1, outliers=outliers)
+    return w_q, w_s, x
+
+
+# (d, n): config shapes, ragged row counts, single group, fast-path limit,
+# and shapes that take the generic kernels (n % 256 != 0, n > 16384).
+SHAPES = [
+    (2048, 2048), (512, 2048), (8192, 2048), (2048, 8192), (1024, 3072), (3072, 3072),
+    (37, 2048), (1, 256), (300, 512), (5, 16384), (3, 16640), (9, 320), (7, 64),
+]
+
+
+@pytest.mark.parametrize("d,n", SHAPES)
+def test_w8a32_parity(d, n):
+    w_q, w_s, x = make_case(d, n, d * 7 + n)
+    y = Guarded(d)
+    ops.matmul_int8(y.t, up(x), up(w_q), up(w_s), n, d, 64)
+    torch.cuda.synchronize()
+    got = y.check()
+    assert orc.max_abs_rel(got, orc.gemv_w8a32(x, w_q, w_s)) <= TOL_W8A32
+    assert orc.max_abs_rel(got, orc.gemv_w8a32_f64(x, w_q, w_s)) <= TOL_W8A32
+
+
+@pytest.mark.parametrize("d,n", SHAPES)
+def test_w8a8_parity(d, n):
+    w_q, w_s, x = make_case(d, n, d * 11 + n, outliers=True)
+    xq_ref, xs_ref = orc.quantize_activation(x)
+    tx = up(x)
+    xq = Guarded(n, torch.int8)
+    xs = torch.empty(1, dtype=torch.float32, device=dev())
+    ops.quantize_activation(xq.t, xs, tx, n)
+    y = Guarded(d)
+    ops.matmul_dp4a(y.t, xq.t, xs, up(w_q), up(w_s), n, d, 64)
+    torch.cuda.synchronize()
+    assert np.array_equal(xq.check(), xq_ref)
+    assert xs.cpu().numpy().view(np.uint32)[0] == xs_ref.view(np.uint32)[0]
+    got = y.check()
+    assert orc.max_abs_rel(got, orc.gemv_w8a8_f64(xq_ref, xs_ref, w_q, w_s)) <= TOL_W8A8
+    assert orc.max_abs_rel(got, orc.gemv_w8a8(xq_ref, xs_ref, w_q, w_s)) <= TOL_W8A8
+
+
+@pytest.mark.parametrize("d,n", SHAPES)
+def test_w8a8_fused_parity(d, n):
+    w_q, w_s, x = make_case(d, n, d * 13 + n, outliers=True)
+    xq_ref, xs_ref = orc.quantize_activation(x)
+    y = Guarded(d)
+    xq = Guarded(n, torch.int8)
+    xs = torch.empty(1, dtype=torch.float32, device=dev())
+    ops.matmul_dp4a_fused(y.t, up(x), up(w_q), up(w_s), n, d, 64, xq_out=xq.t, xs_out=xs)
+    torch.cuda.synchronize()
+    assert np.array_equal(xq.check(), xq_ref)
+    assert xs.cpu().numpy().view(np.uint32)[0] == xs_ref.view(np.uint32)[0]
+    got = y.check()
+    assert orc.max_abs_rel(got, orc.gemv_w8a8_f64(xq_ref, xs_ref, w_q, w_s)) <= TOL_W8A8
+
+
+def test_w8a8_fused_without_outputs():
+    d, n = 1024, 2048
+    w_q, w_s, x = make_case(d, n, 99, outliers=True)
+    xq_ref, xs_ref = orc.quantize_activation(x)
+    y = Guarded(d)
+    ops.matmul_dp4a_fused(y.t, up(x), up(w_q), up(w_s), n, d, 64)
+    torch.cuda.synchronize()
+    assert orc.max_abs_rel(y.check(), orc.gemv_w8a8_f64(xq_ref, xs_ref, w_q, w_s)) <= TOL_W8A8
+
+
+@pytest.mark.parametrize("gs", [32, 128])
+def test_other_group_sizes(gs):
+    d, n = 64, 1024
+    w = synth.weights_np(d, n, 5)
+    w_q, w_s = orc.quantize_weights(w, gs)
+    x = synth.activation_np(n, 6)
+    y = Guarded(d)
+    ops.matmul_int8(y.t, up(x), up(w_q), up(w_s), n, d, gs)
+    xq_ref, xs_ref = orc.quantize_activation(x)
+    y8 = Guarded(d)
+    ops.matmul_dp4a(y8.t, up(xq_ref), up(xs_ref), up(w_q), up(w_s), n, d, gs)
+    torch.cuda.synchronize()
+    assert orc.max_abs_rel(y.check(), orc.gemv_w8a32(x, w_q, w_s, gs)) <= TOL_W8A32
+    assert orc.max_abs_rel(y8.check(), orc.gemv_w8a8_f64(xq_ref, xs_ref, w_q, w_s, gs)) <= TOL_W8A8
+
+
+def test_misaligned_pointers_take_generic_path():
+    d, n = 40, 2048
+    w_q, w_s, x = make_case(d, n, 17)
+    # shift activation / weights by 4 bytes inside larger buffers
+    xb = torch.zeros(n + 4, dtype=torch.float32, device=dev())
+    xb[1:1 + n] = up(x)
+    wb = torch.zeros(d * n + 4, dtype=torch.int8, device=dev())
+    wb[4:4 + d * n] = up(w_q.reshape(-1))
+    y = Guarded(d)
+    ops.matmul_int8(y.t, xb.data_ptr() + 4, wb.data_ptr() + 4, up(w_s), n, d, 64)
+    torch.cuda.synchronize()
+    assert orc.max_abs_rel(y.check(), orc.gemv_w8a32(x, w_q, w_s)) <= TOL_W8A32
+
+
+def test_zero_activation():
+    d, n = 64, 2048
+    w_q, w_s, _ = make_case(d, n, 3)
+    x = np.zeros(n, np.float32)
+    xq = torch.empty(n, dtype=torch.int8, device=dev())
+    xs = torch.empty(1, dtype=torch.float32, device=dev())
+    y = Guarded(d)
+    ops.matmul_dp4a_fused(y.t, up(x), up(w_q), up(w_s), n, d, 64, xq_out=xq, xs_out=xs)
+    torch.cuda.synchronize()
+    assert np.all(y.check() == 0.0)
+    assert xs.item() == np.float32(1e-8) and int(xq.abs().max()) == 0
+
+
+def test_group_dots_bit_exact():
+    d, n = 300, 8192
+    w_q, _, x = make_case(d, n, 23, outliers=True)
+    xq, _ = orc.quantize_activation(x)
+    out = torch.empty((d, n // 64), dtype=torch.int32, device=dev())
+    ops.group_dots(out, up(xq), up(w_q), n, d, 64)
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy(), orc.group_dots(xq, w_q))
+
+
+def test_weight_quantiser_bit_exact(golden_dir):
+    import os
+    z = np.load(os.path.join(golden_dir, "quant_ref_script.npz"))
+    cases = [(z[f"{k}_w"], z[f"{k}_q"], z[f"{k}_s"]) for k in ["wq", "wk", "w1", "w2"]]
+    w = synth.weights_np(333, 2048, 8)
+    q_ref, s_ref = orc.quantize_weights(w)
+    cases.append((w, q_ref, s_ref))
+    for w, q_ref, s_ref in cases:
+        rows, cols = w.shape
+        q = torch.empty((rows, cols), dtype=torch.int8, device=dev())
+        s = torch.empty((rows, cols // 64), dtype=torch.float32, device=dev())
+        ops.quantize_weights(q, s, up(w), rows, cols, 64)
+        torch.cuda.synchronize()
+        assert np.array_equal(q.cpu().numpy(), q_ref)
+        assert np.array_equal(s.cpu().numpy().view(np.uint32), s_ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("m", [1, 2, 3, 5, 8, 13, 16, 17, 64])
+def test_gemm_w8a8_parity(m):
+    d, n = 640, 3072
+    w_q, w_s = orc.quantize_weights(synth.weights_np(d, n, 31 + m))
+    x = synth.activation_np(n, 32 + m, m=m, outliers=True)
+    xq_ref, xs_ref = orc.quantize_activation(x)
+    xq = torch.empty((m, n), dtype=torch.int8, device=dev())
+    xs = torch.empty(m, dtype=torch.float32, device=dev())
+    ops.quantize_activation_rows(xq, xs, up(x), m, n)
+    y = Guarded(m * d)
+    ops.gemm_w8a8(y.t, xq, xs, up(w_q), up(w_s), m, n, d, 64)
+    torch.cuda.synchronize()
+    assert np.array_equal(xq.cpu().numpy(), xq_ref)
+    assert np.array_equal(xs.cpu().numpy().view(np.uint32), xs_ref.view(np.uint32))
+    got = y.check().reshape(m, d)
+    for t in range(m):
+        ref = orc.gemv_w8a8_f64(xq_ref[t], xs_ref[t:t + 1], w_q, w_s)
+        assert orc.max_abs_rel(got[t], ref) <= TOL_W8A8, t
+
+
+def test_rows_are_independent_of_sharding():
+    """Row r's result is bit-identical whether computed in the full matrix or
+    in any row slice (the property the sharded classifier relies on)."""
+    d, n = 4096, 2048
+    w_q, w_s, x = make_case(d, n, 41)
+    tw, ts, tx = up(w_q), up(w_s), up(x)
+    full = torch.empty(d, dtype=torch.float32, device=dev())
+    ops.matmul_int8(full, tx, tw, ts, n, d, 64)
+    xq = torch.empty(n, dtype=torch.int8, device=dev())
+    xs = torch.empty(1, dtype=torch.float32, device=dev())
+    full8 = torch.empty(d, dtype=torch.float32, device=dev())
+    ops.matmul_dp4a_fused(full8, tx, tw, ts, n, d, 64, xq_out=xq, xs_out=xs)
+    for world in (2, 4, 8):
+        chunk = d // world
+        part = torch.empty(d, dtype=torch.float32, device=dev())
+        part8 = torch.empty(d, dtype=torch.float32, device=dev())
+        for r in range(world):
+            ops.matmul_int8(part[r * chunk:(r + 1) * chunk], tx, tw[r * chunk:(r + 1) * chunk],
+                            ts[r * chunk:(r + 1) * chunk], n, chunk, 64)
+            ops.matmul_dp4a_fused(part8[r * chunk:(r + 1) * chunk], tx, tw[r * chunk:(r + 1) * chunk],
+                                  ts[r * chunk:(r + 1) * chunk], n, chunk, 64)
+        torch.cuda.synchronize()
+        assert torch.equal(part.view(torch.int32), full.view(torch.int32))
+        assert torch.equal(part8.view(torch.int32), full8.view(torch.int32))
+
+
+def test_deterministic_and_stream_pdl_independent():
+    d, n = 2048, 8192
+    w_q, w_s, x = make_case(d, n, 43)
+    tw, ts, tx = up(w_q), up(w_s), up(x)
+    outs = []
+    s = torch.cuda.Stream()
+    for pdl in (True, False):
+        ops.set_pdl(pdl)
+        for stream in (None, s):
+            y = torch.empty(d, dtype=torch.float32, device=dev())
+            with torch.cuda.stream(s if stream is not None else torch.cuda.current_stream()):
+                ops.matmul_int8(y, tx, tw, ts, n, d, 64)
+            torch.cuda.synchronize()
+            outs.append(y.view(torch.int32).clone())
+    ops.set_pdl(True)
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+
+
+def test_dropin_shim_matches_c_abi():
+    from minillama_infra_b200._lib import DROPIN_SYMBOLS, dropin
+    d, n = 512, 2048
+    w_q, w_s, x = make_case(d, n, 47, outliers=True)
+    tw, ts, tx = up(w_q), up(w_s), up(x)
+    sh = dropin()
+    y_shim = torch.empty(d, dtype=torch.float32, device=dev())
+    y_abi = torch.empty(d, dtype=torch.float32, device=dev())
+    getattr(sh, DROPIN_SYMBOLS["matmul_int8"])(y_shim.data_ptr(), tx.data_ptr(), tw.data_ptr(),
+                                               ts.data_ptr(), n, d, 64)
+    ops.matmul_int8(y_abi, tx, tw, ts, n, d, 64)
+    xq = torch.empty(n, dtype=torch.int8, device=dev())
+    xs = torch.empty(1, dtype=torch.float32, device=dev())
+    getattr(sh, DROPIN_SYMBOLS["quantize_activation"])(xq.data_ptr(), xs.data_ptr(), tx.data_ptr(), n)
+    y8_shim = torch.empty(d, dtype=torch.float32, device=dev())
+    getattr(sh, DROPIN_SYMBOLS["matmul_dp4a"])(y8_shim.data_ptr(), xq.data_ptr(), xs.data_ptr(),
+                                               tw.data_ptr(), ts.data_ptr(), n, d, 64)
+    torch.cuda.synchronize()
+    assert lib().mli_last_status() == 0
+    assert torch.equal(y_shim.view(torch.int32), y_abi.view(torch.int32))
+    xq_ref, xs_ref = orc.quantize_activation(x)
+    assert np.array_equal(xq.cpu().numpy(), xq_ref)
+    assert orc.max_abs_rel(y8_shim.cpu().numpy(), orc.gemv_w8a8_f64(xq_ref, xs_ref, w_q, w_s)) <= TOL_W8A8
+
+
+def test_reference_kernels_match_oracle_bit_exact():
+    """Pins the oracle: the reference's own kernels (rebuilt for sm_100a) give
+    exactly the oracle's bits on the same inputs."""
+    if not orc.ref_available():
+        pytest.skip("oracle/_ref not built")
+    ref = orc.ref()
+    for d, n in [(256, 2048), (64, 8192), (48, 3072)]:
+        w_q, w_s, x = make_case(d, n, d + n, outliers=True)
+        tw, ts, tx = up(w_q), up(w_s), up(x)
+        y = torch.empty(d, dtype=torch.float32, device=dev())
+        y8 = torch.empty(d, dtype=torch.float32, device=dev())
+        xq = torch.empty(n, dtype=torch.int8, device=dev())
+        xs = torch.empty(1, dtype=torch.float32, device=dev())
+        torch.cuda.synchronize()
+        ref.ref_matmul_int8(y.data_ptr(), tx.data_ptr(), tw.data_ptr(), ts.data_ptr(), n, d, 64)
+        ref.ref_quantize_activation(xq.data_ptr(), xs.data_ptr(), tx.data_ptr(), n)
+        ref.ref_matmul_dp4a(y8.data_ptr(), xq.data_ptr(), xs.data_ptr(), tw.data_ptr(), ts.data_ptr(), n, d, 64)
+        assert ref.ref_device_synchronize() == 0
+        assert np.array_equal(y.cpu().numpy().view(np.uint32), orc.gemv_w8a32(x, w_q, w_s).view(np.uint32))
+        xq_ref, xs_ref = orc.quantize_activation(x)
+        assert np.array_equal(xq.cpu().numpy(), xq_ref)
+        assert np.array_equal(y8.cpu().numpy().view(np.uint32),
+                              orc.gemv_w8a8(xq_ref, xs_ref, w_q, w_s).view(np.uint32))
+
+
+def test_invalid_arguments_raise():
+    y = torch.empty(8, dtype=torch.float32, device=dev())
+    with pytest.raises(MliError):
+        ops.matmul_int8(y, 0, 0, 0, 64, 8, 64)
+    with pytest.raises(MliError):
+        ops.matmul_int8(y, y, y, y, 0, 8, 64)
+    with pytest.raises(MliError):
+        ops.quantize_activation(y, y, y, -1)
+
+
+def test_no_device_errors_recorded():
+    assert ops.device_error() == 0
