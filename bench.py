@@ -312,6 +312,26 @@ def per_shape(device, form, steps):
     return res
 
 
+def profile_case(device, form, shape_name, launches):
+    """A few back-to-back launches of one shape and nothing else: the command
+    the ncu summaries under profiles/ are captured from."""
+    shapes = {name: (d, n) for name, d, n in list(synth.LLAMA_1B) + [synth.CLASSIFIER_1B]}
+    d, n = shapes[shape_name]
+    q, s = synth.weights_gpu(d, n, seed=77, device=device)
+    x = synth.activation_gpu(n, 5, device, outliers=(form == "w8a8"))
+    y = torch.empty(d, dtype=torch.float32, device=device)
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        for _ in range(launches):
+            if form == "w8a32":
+                ops.matmul_int8(y, x, q, s, n, d, GS)
+            else:
+                ops.matmul_dp4a_fused(y, x, q, s, n, d, GS)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": shape_name, "form": form, "d": d, "n": n,
+                      "launches": launches, "device_error": ops.device_error()}))
+
+
 # ---------------------------------------------------------------------------
 def main():
     ap = argparse.ArgumentParser()
@@ -323,7 +343,19 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--per-shape", action="store_true", help="also time each shape in isolation")
+    ap.add_argument("--profile-shape", default=None,
+                    help="run --launches launches of one shape (wq, wk, ..., wcls) and exit")
+    ap.add_argument("--launches", type=int, default=3)
+    ap.add_argument("--launch-flags", type=int, default=None,
+                    help="override the library's launch flags (MLI_LAUNCH_* bits)")
     args = ap.parse_args()
+    if args.launch_flags is not None:
+        from minillama_infra_b200._lib import lib
+        lib().mli_set_launch_flags(args.launch_flags)
+    if args.profile_shape:
+        torch.cuda.set_device(0)
+        profile_case(torch.device("cuda", 0), args.form, args.profile_shape, args.launches)
+        return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

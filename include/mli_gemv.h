@@ -43,6 +43,10 @@ enum mli_status_code {
 
 /* Launch-option bits for mli_set_launch_flags(). */
 #define MLI_LAUNCH_PDL 1u /* programmatic dependent launch (default on) */
+/* Batch-1 GEMV tuning: by default a matrix of at least two ring stages per SM
+ * runs two CTAs per SM; with this bit only matrices of 16+ stages per SM do,
+ * the others leave the second slot to the next kernel in the stream. */
+#define MLI_LAUNCH_ONE_CTA 2u
 
 /* ---- library state ------------------------------------------------------ */
 const char* mli_status_string(int status);
@@ -116,6 +120,14 @@ int mli_quantize_weights(int8_t* w_q, float* w_s, const float* w, int rows,
  * kernels scale; for bit-exact parity tests. */
 int mli_debug_group_dots(int32_t* out, const int8_t* xq, const int8_t* w_q,
                          int n, int d, int group_size, void* stream);
+
+/* Host-only: the launch plan the batch-1 streaming GEMV would use for this
+ * shape on a device with the given properties.  form: 0 W8A32, 1 W8A8,
+ * 2 fused W8A8.  out[8] = {grid, dynamic smem bytes, slices per row, warps
+ * per slice, rows per stage, stages, ring slots, bytes per stage}.  Returns
+ * MLI_ERR_UNSUPPORTED for shapes that take the generic kernels. */
+int mli_debug_plan_gemv(int form, int n, int d, int sm_count, int smem_per_sm,
+                        int smem_optin, int* out);
 
 #ifdef __cplusplus
 } /* extern "C" */

@@ -43,6 +43,7 @@ SIGNATURES = {
     "mli_gemm_w8a8": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P]),
     "mli_quantize_weights": (_I, [_P, _P, _P, _I, _I, _I, _P]),
     "mli_debug_group_dots": (_I, [_P, _P, _P, _I, _I, _I, _P]),
+    "mli_debug_plan_gemv": (_I, [_I, _I, _I, _I, _I, _I, ctypes.POINTER(_I)]),
 }
 
 # The drop-in shim's C++ symbols (include/mli_gemv.h, reference include/model.h:62-64).

@@ -5,29 +5,43 @@
 //   W8A8   y[r] = sum_g ((float)I[r][g] * s[r][g]) * xs     (:465-501)
 //          I[r][g] = exact int32 dot of group g of row r with the int8 x.
 //
-// Design (HBM-bound: ~1 byte of weight per 2 flops):
-//  * Every warp owns one "slice" of 2048 columns (32 groups).  Lane l covers
-//    the 16-byte quarter (l & 3) of the four consecutive groups
-//    4*(l >> 2) .. +3 of its slice, so one row costs each lane four 16-byte
-//    streaming loads (64 bytes apart) plus one load of its scales.  Every
-//    32-byte sector a warp touches is fully used.
-//  * The activation slice a lane needs never changes from row to row, so it
-//    lives in registers for the whole kernel: the CTA stages x once into
-//    shared memory with one bulk (TMA-engine) copy, each warp then loads its
-//    slice into registers.  Rows stream through a two-deep register pipeline.
-//  * W8A32 converts int8 -> fp32 exactly with a byte-permute under a 2^23
-//    exponent and packed fp32x2 subtract / FMA (two values per instruction).
+// The op is HBM-bound (one weight byte per two flops), so the kernel is built
+// to keep HBM streaming across the whole chain of GEMVs of a decode step:
+//
+//  * Bulk-copy streaming.  "Stages" of whole weight rows (and their scale
+//    rows) move from HBM into a ring of shared-memory slots with 1-D bulk
+//    copies (the TMA engine, completion on an mbarrier); eight warps compute
+//    from shared memory.  A stage is ~32 KB of contiguous int8 rows, the ring
+//    holds 2-6 stages per CTA.  Whichever warp is last to finish with a slot
+//    refills it, so no warp ever waits for another to drain a slot.
+//  * Programmatic dependent launch.  Every CTA triggers its dependents as it
+//    starts and fills its ring *before* griddepcontrol.wait (weights never
+//    depend on the previous kernel).  One CTA per SM uses half of the SM's
+//    registers and at most half of its shared memory, so the next GEMV's CTA
+//    is resident alongside and fills its ring while this one drains.
+//  * Consumers: warp w owns one slice of a row -- 1024 columns for W8A32,
+//    2048 for W8A8 (split-K when n is wider) -- and takes 4 (W8A32) or 2
+//    (W8A8) rows of it per stage, reduced across lanes together.  In read k
+//    of a row, lane l takes the 16 bytes at 16*(l + 32k) of its slice, so a
+//    warp read is 512 contiguous bytes (conflict-free), and the slice of x it
+//    needs is the same for every row: it lives in registers for the whole
+//    kernel.
+//  * The activation is read only after griddepcontrol.wait, straight from
+//    global memory (it was just written, so it sits in L2), and prepared once
+//    per CTA in shared memory:
+//      W8A32: split exactly enough for fp32 parity into four int8 digit planes
+//      under a per-group power of two (see x_digits_prologue), so every
+//      weight chunk is 16 dp4a of exact int32 partials plus three fp32 ops
+//      instead of 16 int8->fp32 conversions and 16 FMAs;
+//      W8A8 fused: quantised in the prologue, bit-identical to
+//      quantize_activation.
 //  * W8A8 does four dp4a per 16 bytes, a 3-shuffle quad reduce-scatter that
 //    leaves each lane with one whole group's int32 dot, then the reference's
-//    per-group fp32 term ((float)I * ws) * xs.  The fused variant quantises x
-//    in every CTA's prologue, bit-identical to quantize_activation.
-//  * Rows with more than one slice (n > 2048: split-K) are combined through
-//    shared memory in slice order.  The arithmetic of one row depends only on
-//    n: never on d, the tile, the grid or the GPU count, so a row-sharded
-//    classifier returns bit-identical logits on any number of GPUs.
-//  * Programmatic dependent launch: the first row's weights are requested
-//    before griddepcontrol.wait, so a chain of GEMVs keeps HBM busy across
-//    kernel boundaries.
+//    per-group term ((float)I * ws) * xs.
+//  * Slices of one row are combined in slice order by the last consumer warp
+//    to finish the stage.  A row's arithmetic depends only on n: never on d,
+//    the stage, the grid or the GPU count, so a row-sharded classifier gives
+//    bit-identical logits on any number of GPUs.
 #include <utility>
 
 #include "mli_common.cuh"
@@ -36,227 +50,156 @@
 namespace mli {
 
 constexpr int kGroup = 64;
-constexpr int kSliceCols = 2048;
-constexpr int kWarps = 8;
-constexpr int kThreads = kWarps * 32;
+constexpr int kConsumerWarps = 8;
+constexpr int kConsumerThreads = kConsumerWarps * 32;
+constexpr int kThreads = kConsumerThreads;
 constexpr int kMaxSlices = 8;
-constexpr int kMaxCols = kSliceCols * kMaxSlices;  // fast-path limit on n
-constexpr int kSmemHeader = 128;                   // mbarrier + reduction scratch
+constexpr int kMaxRing = 6;
+constexpr int kHeader = 256;
 
-struct GemvArgs {
+// Shared-memory header: full[6] @0, reduction scratch (8 floats) @128,
+// per-slot completion counters (6 ints) @160.
+struct Smem {
+  uint64_t* full;
+  float* red;
+  int* counters;
+  __device__ explicit Smem(unsigned char* base)
+      : full(reinterpret_cast<uint64_t*>(base)),
+        red(reinterpret_cast<float*>(base + 128)),
+        counters(reinterpret_cast<int*>(base + 160)) {}
+};
+
+enum class Form : int { kW8A32 = 0, kW8A8 = 1, kW8A8Fused = 2 };
+
+// 16-byte chunks per lane per row slice: a slice is 512 * K columns (8 * K
+// groups).  W8A32 keeps its fp32 slice of x in 2 * 16 registers per lane,
+// W8A8 its int8 slice in 4 * 4.
+__host__ __device__ constexpr int chunks_per_lane(Form f) { return f == Form::kW8A32 ? 2 : 4; }
+__host__ __device__ constexpr int slice_cols(Form f) { return 512 * chunks_per_lane(f); }
+// Rows each consumer warp takes per stage (reduced together, see
+// warp_sum_rows): enough independent work per pass to hide latency with only
+// eight consumer warps per SM.
+__host__ __device__ constexpr int rows_per_warp(Form f) { return f == Form::kW8A32 ? 4 : 2; }
+
+struct StreamArgs {
   float* y;
-  const float* x;     // fp32 activation (W8A32, fused W8A8)
-  const int8_t* xq;   // int8 activation (W8A8)
-  const float* xs;    // activation scale (W8A8)
-  int8_t* xq_out;     // fused W8A8: optional copy of the quantised x
-  float* xs_out;      //             and of its scale
+  const float* x;   // fp32 activation (W8A32, fused W8A8)
+  const int8_t* xq; // int8 activation (W8A8)
+  const float* xs;  // activation scale (W8A8)
+  int8_t* xq_out;   // fused W8A8: optional copy of the quantised x ...
+  float* xs_out;    // ... and of its scale
   const int8_t* w;
   const float* s;
-  int n, d;
-  int S;        // slices per row = ceil(n / 2048)
-  int wps;      // warps per slice = 8 / S
-  int rpw;      // rows per warp per tile
-  int R;        // rows per tile = wps * rpw
-  int n_tiles;  // ceil(d / R)
+  int n, d, G;      // G = n / 64 groups per row
+  int S, wps;       // slices per row, consumer warps per slice (8 / S)
+  int R;            // rows per stage
+  int n_stages;     // ceil(d / R)
+  int ring;         // ring slots
+  uint32_t stage_bytes;  // R * n + R * G * 4
+  uint32_t x_off, ring_off, part_off;
 };
-
-// Work split of one CTA: which warp handles which slice / rows.
-struct WarpRole {
-  int sl, wj;
-  bool warp_on, lane_on;
-  int g0;    // first of the lane's four groups (row-relative group index)
-  int col0;  // first column of the lane's chunk 0
-  __device__ WarpRole(const GemvArgs& a) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    sl = warp % a.S;
-    wj = warp / a.S;
-    warp_on = wj < a.wps;
-    g0 = sl * 32 + (lane >> 2) * 4;
-    lane_on = warp_on && g0 < (a.n >> 6);
-    col0 = g0 * kGroup + (lane & 3) * 16;
-  }
-};
-
-__device__ __forceinline__ int my_tile_count(const GemvArgs& a) {
-  return blockIdx.x < static_cast<unsigned>(a.n_tiles)
-             ? (a.n_tiles - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
-             : 0;
-}
-
-// Row handled by this warp at flattened position idx (tile-major).
-__device__ __forceinline__ int row_at(const GemvArgs& a, int wj, int idx) {
-  const int t = idx / a.rpw;
-  const int i = idx - t * a.rpw;
-  return (static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x)) * a.R + wj + i * a.wps;
-}
-
-// Stage `bytes` from global into shared memory with one bulk copy.  Returns
-// false (on every thread) if the copy did not land within the wait limit.
-__device__ __forceinline__ bool stage_to_smem(void* dst, const void* src,
-                                              uint32_t bytes, uint64_t* bar) {
-  if (threadIdx.x == 0) {
-    mbar_init(bar, 1);
-    fence_barrier_init();
-    mbar_arrive_expect_tx(bar, bytes);
-    bulk_copy_g2s(dst, src, bytes, bar);
-  }
-  __syncthreads();
-  const bool ok = mbar_wait_bounded(bar, 0, kWaitLimitNs);
-  if (__syncthreads_or(!ok)) {
-    if (threadIdx.x == 0) {
-      record_device_error(kDevStageTimeout);
-      mbar_wait_bounded(bar, 0, kWaitLimitNs);  // let an in-flight copy drain
-    }
-    return false;
-  }
-  return true;
-}
-
-// Combine the per-slice partial sums of one tile in slice order.
-__device__ __forceinline__ void combine_slices(const GemvArgs& a,
-                                               const float* part, int row0) {
-  for (int r = threadIdx.x; r < a.R; r += kThreads) {
-    const int row = row0 + r;
-    if (row < a.d) {
-      float v = part[r * a.S];
-      for (int s = 1; s < a.S; ++s) v += part[r * a.S + s];
-      a.y[row] = v;
-    }
-  }
-}
 
 // ---------------------------------------------------------------------------
-// W8A32
+// Activation prologues (consumer threads, once per CTA)
 // ---------------------------------------------------------------------------
-struct RowW8A32 {
-  uint4 w[4];
-  float4 s;
-};
+// W8A32 represents each 64-column group of the fp32 activation exactly enough
+// for fp32 parity as four signed 7-bit int8 "digit planes" under a per-group
+// power of two:  x~ = 2^-E (d1 + d2 2^-7 + d3 2^-14 + d4 2^-21),
+// with E chosen so that max|x_g| * 2^E lies in [32, 64).  Every digit is in
+// [-64, 64] and |x - x~| <= 2^-27 max|x_g| (well below the fp32 rounding of
+// the dot product itself).  A weight chunk then costs 16 dp4a of exact int32
+// partials P1..P4, combined as Q = 128 P1 + P2 and R = 128 P3 + P4 (both
+// below 2^24, so exact in fp32):  sum_j w_j x~_j = 2^-(E+7) (Q + 2^-14 R).
+//
+// rint(u) for |u| <= 64 is (u + 1.5*2^23) - 1.5*2^23 (ties to even), and the
+// low byte of the bits of u + 1.5*2^23 is the digit's two's-complement byte.
+constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
 
-__device__ __forceinline__ void load_row_w8a32(const GemvArgs& a,
-                                               const WarpRole& role, int row,
-                                               RowW8A32& r) {
-  if (role.lane_on && row < a.d) {
-    const int8_t* p = a.w + static_cast<size_t>(row) * a.n + role.col0;
-    r.w[0] = ldg_stream_u4(p);
-    r.w[1] = ldg_stream_u4(p + 64);
-    r.w[2] = ldg_stream_u4(p + 128);
-    r.w[3] = ldg_stream_u4(p + 192);
-    r.s = ldg_f4(a.s + static_cast<size_t>(row) * (a.n >> 6) + role.g0);
-  } else {
-    r.w[0] = r.w[1] = r.w[2] = r.w[3] = make_uint4(0, 0, 0, 0);
-    r.s = make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-}
-
-// Dot of one lane's 64 weights with its register-resident activations.
-// Per 16-byte chunk: sum_j w_j x_j in two interleaved fp32 lanes, then one
-// FMA with the group scale.
-__device__ __forceinline__ float dot_w8a32(const RowW8A32& r,
-                                           const float2 (&xr)[4][8]) {
-  const float2 m = make_float2(-kI8Magic, -kI8Magic);
-  const float sv[4] = {r.s.x, r.s.y, r.s.z, r.s.w};
-  float acc = 0.f;
+// Digit bytes of one value; `u` is the value already scaled by 2^E.
+__device__ __forceinline__ void digits4(float u, uint32_t (&t)[4]) {
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const uint32_t u0 = r.w[k].x ^ 0x80808080u;
-    const uint32_t u1 = r.w[k].y ^ 0x80808080u;
-    const uint32_t u2 = r.w[k].z ^ 0x80808080u;
-    const uint32_t u3 = r.w[k].w ^ 0x80808080u;
-    float2 p = mul2(add2(biased_pair<0>(u0), m), xr[k][0]);
-    p = fma2(add2(biased_pair<1>(u0), m), xr[k][1], p);
-    p = fma2(add2(biased_pair<0>(u1), m), xr[k][2], p);
-    p = fma2(add2(biased_pair<1>(u1), m), xr[k][3], p);
-    p = fma2(add2(biased_pair<0>(u2), m), xr[k][4], p);
-    p = fma2(add2(biased_pair<1>(u2), m), xr[k][5], p);
-    p = fma2(add2(biased_pair<0>(u3), m), xr[k][6], p);
-    p = fma2(add2(biased_pair<1>(u3), m), xr[k][7], p);
-    acc = fmaf(p.x + p.y, sv[k], acc);
+  for (int p = 0; p < 4; ++p) {
+    const float r = u + kRoundMagic;
+    t[p] = __float_as_uint(r);
+    if (p < 3) u = (u - (r - kRoundMagic)) * 128.0f;
   }
-  return acc;
 }
 
-__global__ void __launch_bounds__(kThreads, 2)
-    gemv_w8a32_g64_kernel(const GemvArgs a) {
-  extern __shared__ __align__(128) unsigned char smem[];
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
-  float* xsm = reinterpret_cast<float*>(smem + kSmemHeader);
-  float* part = xsm + a.n;  // [R][S] slice partials (S > 1)
-
-  const WarpRole role(a);
+// Writes the digit planes [4][n] int8 and the per-group factors 2^-(E+7)
+// [n/64] of x into shared memory.  Thread t handles columns 4t + 1024j, so
+// each half-warp holds one whole 64-column group.
+__device__ __forceinline__ void x_digits_prologue(const float* x, int n, int8_t* planes,
+                                                  float* fac) {
   const int lane = threadIdx.x & 31;
-  const int my_tiles = my_tile_count(a);
-  const int total = my_tiles * a.rpw;
-
-  // Weights do not depend on the previous kernel: request the first row now.
-  RowW8A32 cur;
-  load_row_w8a32(a, role, total > 0 && role.warp_on ? row_at(a, role.wj, 0) : a.d, cur);
-
-  griddep_wait();
-  if (!stage_to_smem(xsm, a.x, static_cast<uint32_t>(a.n) * 4u, bar)) return;
-  griddep_launch_dependents();
-
-  float2 xr[4][8];
+  for (int c0 = 0; c0 < n; c0 += 4 * kConsumerThreads) {
+    const int c = c0 + 4 * threadIdx.x;
+    const bool valid = c < n;
+    const float4 v = valid ? *reinterpret_cast<const float4*>(x + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-#pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (role.lane_on) v = *reinterpret_cast<const float4*>(xsm + role.col0 + 64 * k + 4 * p);
-      xr[k][2 * p] = make_float2(v.x, v.y);
-      xr[k][2 * p + 1] = make_float2(v.z, v.w);
+    for (int off = 1; off < 16; off <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    const int e = static_cast<int>(__float_as_uint(m) >> 23);  // biased exponent of max|x_g|
+    float scale_up, factor;
+    if (e >= 13 && e <= 254) {
+      scale_up = __uint_as_float(static_cast<uint32_t>(259 - e) << 23);  // 2^E, E = 132 - e
+      factor = __uint_as_float(static_cast<uint32_t>(e - 12) << 23);    // 2^-(E + 7)
+    } else if (e == 255) {  // inf / nan in the group: propagate
+      scale_up = 0.f;
+      factor = __uint_as_float(0x7fc00000u);
+    } else {  // max|x_g| < 2^-114: the group contributes nothing measurable
+      scale_up = 0.f;
+      factor = 0.f;
     }
-  }
-
-  int idx = 0;
-  for (int t = 0; t < my_tiles; ++t) {
-    const int row0 = (static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x)) * a.R;
-    for (int i = 0; i < a.rpw; ++i, ++idx) {
-      const int row = row0 + role.wj + i * a.wps;
-      RowW8A32 nxt;
-      load_row_w8a32(a, role, (idx + 1 < total && role.warp_on) ? row_at(a, role.wj, idx + 1) : a.d, nxt);
-      if (role.warp_on && row < a.d) {
-        float acc = role.lane_on ? dot_w8a32(cur, xr) : 0.f;
-        acc = warp_sum(acc);
-        if (lane == 0) {
-          if (a.S == 1) a.y[row] = acc;
-          else part[(role.wj + i * a.wps) * a.S + role.sl] = acc;
-        }
+    uint32_t t0[4], t1[4], t2[4], t3[4];
+    digits4(v.x * scale_up, t0);
+    digits4(v.y * scale_up, t1);
+    digits4(v.z * scale_up, t2);
+    digits4(v.w * scale_up, t3);
+    if (valid) {
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        const uint32_t lo = __byte_perm(t0[p], t1[p], 0x0040);
+        const uint32_t hi = __byte_perm(t2[p], t3[p], 0x0040);
+        *reinterpret_cast<uint32_t*>(planes + p * n + c) = __byte_perm(lo, hi, 0x5410);
       }
-      cur = nxt;
-    }
-    if (a.S > 1) {
-      __syncthreads();
-      combine_slices(a, part, row0);
-      __syncthreads();
+      if ((lane & 15) == 0) fac[c >> 6] = factor;
     }
   }
 }
 
-// ---------------------------------------------------------------------------
-// W8A8 (dp4a)
-// ---------------------------------------------------------------------------
-struct RowW8A8 {
-  uint4 w[4];
-  float s;
-};
-
-__device__ __forceinline__ void load_row_w8a8(const GemvArgs& a,
-                                              const WarpRole& role, int row,
-                                              RowW8A8& r) {
-  if (role.lane_on && row < a.d) {
-    const int8_t* p = a.w + static_cast<size_t>(row) * a.n + role.col0;
-    r.w[0] = ldg_stream_u4(p);
-    r.w[1] = ldg_stream_u4(p + 64);
-    r.w[2] = ldg_stream_u4(p + 128);
-    r.w[3] = ldg_stream_u4(p + 192);
-    r.s = ldg_f1(a.s + static_cast<size_t>(row) * (a.n >> 6) + role.g0 + (threadIdx.x & 3));
-  } else {
-    r.w[0] = r.w[1] = r.w[2] = r.w[3] = make_uint4(0, 0, 0, 0);
-    r.s = 0.f;
+// Fused W8A8: quantises x into shared int8 [n], bit-identical to
+// quantize_activation_kernel (src/model_cuda_v2_shared.cu:429-455).
+// Returns the activation scale.
+__device__ __forceinline__ float x_quant_prologue(const float* x, int n, int8_t* xq, float* red) {
+  float m = 0.f;
+  for (int c = 4 * threadIdx.x; c < n; c += 4 * kConsumerThreads) {
+    const float4 v = *reinterpret_cast<const float4*>(x + c);
+    m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
   }
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  float amax = red[0];
+#pragma unroll
+  for (int w = 1; w < kConsumerWarps; ++w) amax = fmaxf(amax, red[w]);
+  float scale = amax / 127.0f;
+  if (scale < 1e-8f) scale = 1e-8f;
+  const float inv = 1.0f / scale;
+  for (int c = 4 * threadIdx.x; c < n; c += 4 * kConsumerThreads) {
+    const float4 v = *reinterpret_cast<const float4*>(x + c);
+    const int q0 = max(-127, min(127, __float2int_rn(v.x * inv)));
+    const int q1 = max(-127, min(127, __float2int_rn(v.y * inv)));
+    const int q2 = max(-127, min(127, __float2int_rn(v.z * inv)));
+    const int q3 = max(-127, min(127, __float2int_rn(v.w * inv)));
+    *reinterpret_cast<uint32_t*>(xq + c) = (q0 & 0xff) | ((q1 & 0xff) << 8) | ((q2 & 0xff) << 16) |
+                                           (static_cast<uint32_t>(q3 & 0xff) << 24);
+  }
+  return scale;
 }
 
+// ---------------------------------------------------------------------------
+// Consumer row kernels (one warp, one slice of RB consecutive rows)
+// ---------------------------------------------------------------------------
 __device__ __forceinline__ int dp4a_chunk(const uint4 w, const uint4 x) {
   int acc = __dp4a(static_cast<int>(w.x), static_cast<int>(x.x), 0);
   acc = __dp4a(static_cast<int>(w.y), static_cast<int>(x.y), acc);
@@ -265,8 +208,43 @@ __device__ __forceinline__ int dp4a_chunk(const uint4 w, const uint4 x) {
   return acc;
 }
 
-// Lane q of each quad holds int32 partials p[k] (its 16 columns of group k);
-// afterwards it holds group q's full 64-column dot.  Integer sums: exact.
+// Per-lane W8A32 partials of RB consecutive rows (row stride n bytes in the
+// stage, scale-row stride G floats).  Per 16-byte chunk k (group lane/4 + 8k):
+// four digit-plane dots, combined exactly into Q, R, then one rounding into
+// fp32 and one FMA with the group scale; chunks in order k = 0, 1.
+template <int RB>
+__device__ __forceinline__ void rows_w8a32(const int8_t* wr, const float* sr, int n, int G,
+                                           int nvalid, const uint4 (&xd)[2][4],
+                                           const float (&fac)[2], unsigned vmask, int lane,
+                                           float (&out)[RB]) {
+  uint4 w[RB][2];
+  float sc[RB][2];
+#pragma unroll
+  for (int r = 0; r < RB; ++r) {
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const bool v = r < nvalid && ((vmask >> k) & 1u);
+      w[r][k] = v ? *reinterpret_cast<const uint4*>(wr + r * n + 16 * (lane + 32 * k))
+                  : make_uint4(0, 0, 0, 0);
+      sc[r][k] = v ? sr[r * G + (lane >> 2) + 8 * k] : 0.f;
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < RB; ++r) {
+    float acc = 0.f;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int q = dp4a_chunk(w[r][k], xd[k][0]) * 128 + dp4a_chunk(w[r][k], xd[k][1]);
+      const int rr = dp4a_chunk(w[r][k], xd[k][2]) * 128 + dp4a_chunk(w[r][k], xd[k][3]);
+      const float v = fmaf(static_cast<float>(rr), 0x1p-14f, static_cast<float>(q));
+      acc = fmaf(v * fac[k], sc[r][k], acc);
+    }
+    out[r] = acc;
+  }
+}
+
+// Lane q of each quad holds int32 partials p[k] of group (lane/4 + 8k);
+// afterwards it holds the quad's total of p[q].  Integer sums: exact.
 __device__ __forceinline__ int quad_reduce_scatter(int p0, int p1, int p2, int p3) {
   const int q = threadIdx.x & 3;
   const bool b0 = q & 1;
@@ -280,105 +258,189 @@ __device__ __forceinline__ int quad_reduce_scatter(int p0, int p1, int p2, int p
   return keep;
 }
 
-// Per-token quantisation of the staged fp32 x into shared int8, bit-identical
-// to quantize_activation_kernel (src/model_cuda_v2_shared.cu:429-455).
-// Returns the activation scale.
-__device__ __forceinline__ float quantize_staged(const float* xf, int8_t* xq, int n,
-                                 float* red) {
-  float m = 0.f;
-  for (int i = threadIdx.x; i < n; i += kThreads) m = fmaxf(m, fabsf(xf[i]));
-  m = warp_max(m);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
-  __syncthreads();
-  float amax = red[0];
+// Per-lane W8A8 terms of RB consecutive rows: lane q of each quad ends with
+// group (lane/4 + 8q)'s exact int32 dot and forms ((float)I * ws) * xs.
+template <int RB>
+__device__ __forceinline__ void rows_w8a8(const int8_t* wr, const float* sr, int n, int G,
+                                          int nvalid, const uint4 (&xv)[4], unsigned vmask,
+                                          int lane, float xscale, float (&out)[RB]) {
+  uint4 w[RB][4];
 #pragma unroll
-  for (int w = 1; w < kWarps; ++w) amax = fmaxf(amax, red[w]);
-  float scale = amax / 127.0f;
-  if (scale < 1e-8f) scale = 1e-8f;
-  const float inv = 1.0f / scale;
-  for (int i = threadIdx.x * 4; i < n; i += kThreads * 4) {
-    const float4 v = *reinterpret_cast<const float4*>(xf + i);
-    const int q0 = max(-127, min(127, __float2int_rn(v.x * inv)));
-    const int q1 = max(-127, min(127, __float2int_rn(v.y * inv)));
-    const int q2 = max(-127, min(127, __float2int_rn(v.z * inv)));
-    const int q3 = max(-127, min(127, __float2int_rn(v.w * inv)));
-    const uint32_t packed = (q0 & 0xff) | ((q1 & 0xff) << 8) | ((q2 & 0xff) << 16) |
-                            (static_cast<uint32_t>(q3 & 0xff) << 24);
-    *reinterpret_cast<uint32_t*>(xq + i) = packed;
+  for (int r = 0; r < RB; ++r)
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      w[r][k] = (r < nvalid && ((vmask >> k) & 1u))
+                    ? *reinterpret_cast<const uint4*>(wr + r * n + 16 * (lane + 32 * k))
+                    : make_uint4(0, 0, 0, 0);
+  const int q = lane & 3;
+  const bool gvalid = (vmask >> q) & 1u;  // group lane/4 + 8q exists
+#pragma unroll
+  for (int r = 0; r < RB; ++r) {
+    const int I = quad_reduce_scatter(dp4a_chunk(w[r][0], xv[0]), dp4a_chunk(w[r][1], xv[1]),
+                                      dp4a_chunk(w[r][2], xv[2]), dp4a_chunk(w[r][3], xv[3]));
+    const bool v = gvalid && r < nvalid;
+    const float ws = v ? sr[r * G + (lane >> 2) + 8 * q] : 0.f;
+    out[r] = v ? (static_cast<float>(I) * ws) * xscale : 0.f;
   }
-  return scale;
 }
 
-template <bool kFused>
-__global__ void __launch_bounds__(kThreads, 2)
-    gemv_w8a8_g64_kernel(const GemvArgs a) {
-  extern __shared__ __align__(128) unsigned char smem[];
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
-  float* red = reinterpret_cast<float*>(smem + 16);
-  float* xf = reinterpret_cast<float*>(smem + kSmemHeader);
-  int8_t* xqs = reinterpret_cast<int8_t*>(smem + kSmemHeader) + (kFused ? 4 * a.n : 0);
-  float* part = reinterpret_cast<float*>(xqs + a.n);
+// ---------------------------------------------------------------------------
+// The streaming kernel
+// ---------------------------------------------------------------------------
+// Issues the bulk copies of stage `st` (rows st*R .. +R-1 and their scales)
+// into ring slot `slot`, completing on full[slot].
+__device__ __forceinline__ void issue_stage(const StreamArgs& a, unsigned char* ring, uint64_t* full,
+                                            int st, int slot) {
+  const int row0 = st * a.R;
+  const int rows = min(a.R, a.d - row0);
+  const uint32_t wb = static_cast<uint32_t>(rows) * a.n;
+  const uint32_t sb = static_cast<uint32_t>(rows) * a.G * 4u;
+  unsigned char* dst = ring + static_cast<size_t>(slot) * a.stage_bytes;
+  mbar_arrive_expect_tx(&full[slot], wb + sb);
+  bulk_copy_g2s(dst, a.w + static_cast<size_t>(row0) * a.n, wb, &full[slot]);
+  bulk_copy_g2s(dst + static_cast<size_t>(a.R) * a.n, a.s + static_cast<size_t>(row0) * a.G, sb,
+                &full[slot]);
+}
 
-  const WarpRole role(a);
-  const int lane = threadIdx.x & 31;
-  const int my_tiles = my_tile_count(a);
-  const int total = my_tiles * a.rpw;
+template <Form F>
+__global__ void __launch_bounds__(kThreads, 2) gemv_stream_kernel(const StreamArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem[];
+  Smem sm(smem);
+  unsigned char* ring = smem + a.ring_off;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long T = a.n_stages;
+  const int begin = static_cast<int>((blockIdx.x * T) / gridDim.x);
+  const int cnt = static_cast<int>(((blockIdx.x + 1) * T) / gridDim.x) - begin;
 
-  RowW8A8 cur;
-  load_row_w8a8(a, role, total > 0 && role.warp_on ? row_at(a, role.wj, 0) : a.d, cur);
+  // Fill the ring before waiting on the previous kernel: weights never
+  // depend on it.
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < a.ring; ++i) {
+      mbar_init(&sm.full[i], 1);
+      sm.counters[i] = 0;
+    }
+    fence_barrier_init();
+    for (int i = 0; i < a.ring && i < cnt; ++i) issue_stage(a, ring, sm.full, begin + i, i);
+  }
+  __syncthreads();
+  griddep_launch_dependents();
 
+  constexpr int K = chunks_per_lane(F);
+  constexpr int kSlice = slice_cols(F);
+  constexpr int RB = rows_per_warp(F);
+  const int S = a.S;
+  const int sl = warp % S, wj = warp / S;
+  const bool warp_on = wj < a.wps;
+  const int g_slice = min(8 * K, a.G - sl * 8 * K);
+  unsigned vmask = 0;
+#pragma unroll
+  for (int k = 0; k < K; ++k)
+    if (warp_on && (lane >> 2) + 8 * k < g_slice) vmask |= 1u << k;
+  const int col0 = sl * kSlice + 16 * lane;  // first column of this lane's chunk 0
+
+  // The activation is the previous kernel's output: read it only now.
   griddep_wait();
-  float xscale;
-  if (kFused) {
-    if (!stage_to_smem(xf, a.x, static_cast<uint32_t>(a.n) * 4u, bar)) return;
-    xscale = quantize_staged(xf, xqs, a.n, red);
+  float xscale = 0.f;
+  uint4 xd[2][4];  // W8A32 digit planes of chunks 0, 1
+  float fac[2];
+  uint4 xv[4];     // W8A8 int8 chunks 0..3
+  if constexpr (F == Form::kW8A32) {
+    int8_t* planes = reinterpret_cast<int8_t*>(smem + a.x_off);
+    float* facs = reinterpret_cast<float*>(planes + 4 * a.n);
+    x_digits_prologue(a.x, a.n, planes, facs);
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const bool v = (vmask >> k) & 1u;
+#pragma unroll
+      for (int p = 0; p < 4; ++p)
+        xd[k][p] = v ? *reinterpret_cast<const uint4*>(planes + p * a.n + col0 + 512 * k)
+                     : make_uint4(0, 0, 0, 0);
+      fac[k] = v ? facs[(col0 + 512 * k) >> 6] : 0.f;
+    }
+  } else if constexpr (F == Form::kW8A8Fused) {
+    int8_t* q8 = reinterpret_cast<int8_t*>(smem + a.x_off);
+    xscale = x_quant_prologue(a.x, a.n, q8, sm.red);
     __syncthreads();
     if (blockIdx.x == 0) {
       if (a.xq_out != nullptr) {
         if ((reinterpret_cast<uintptr_t>(a.xq_out) & 15) == 0) {
-          for (int i = threadIdx.x * 16; i < a.n; i += kThreads * 16)
-            *reinterpret_cast<uint4*>(a.xq_out + i) = *reinterpret_cast<const uint4*>(xqs + i);
+          for (int i = threadIdx.x * 16; i < a.n; i += kConsumerThreads * 16)
+            *reinterpret_cast<uint4*>(a.xq_out + i) = *reinterpret_cast<const uint4*>(q8 + i);
         } else {
-          for (int i = threadIdx.x; i < a.n; i += kThreads) a.xq_out[i] = xqs[i];
+          for (int i = threadIdx.x; i < a.n; i += kConsumerThreads) a.xq_out[i] = q8[i];
         }
       }
       if (a.xs_out != nullptr && threadIdx.x == 0) *a.xs_out = xscale;
     }
-  } else {
-    if (!stage_to_smem(xqs, a.xq, static_cast<uint32_t>(a.n), bar)) return;
-    xscale = *a.xs;
-  }
-  griddep_launch_dependents();
-
-  uint4 xv[4];
 #pragma unroll
-  for (int k = 0; k < 4; ++k)
-    xv[k] = role.lane_on ? *reinterpret_cast<const uint4*>(xqs + role.col0 + 64 * k)
-                         : make_uint4(0, 0, 0, 0);
+    for (int k = 0; k < 4; ++k)
+      xv[k] = ((vmask >> k) & 1u) ? *reinterpret_cast<const uint4*>(q8 + col0 + 512 * k)
+                                  : make_uint4(0, 0, 0, 0);
+  } else {
+    xscale = *a.xs;
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      xv[k] = ((vmask >> k) & 1u) ? *reinterpret_cast<const uint4*>(a.xq + col0 + 512 * k)
+                                  : make_uint4(0, 0, 0, 0);
+  }
 
-  int idx = 0;
-  for (int t = 0; t < my_tiles; ++t) {
-    const int row0 = (static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x)) * a.R;
-    for (int i = 0; i < a.rpw; ++i, ++idx) {
-      const int row = row0 + role.wj + i * a.wps;
-      RowW8A8 nxt;
-      load_row_w8a8(a, role, (idx + 1 < total && role.warp_on) ? row_at(a, role.wj, idx + 1) : a.d, nxt);
-      if (role.warp_on && row < a.d) {
-        const int I = quad_reduce_scatter(dp4a_chunk(cur.w[0], xv[0]), dp4a_chunk(cur.w[1], xv[1]),
-                                          dp4a_chunk(cur.w[2], xv[2]), dp4a_chunk(cur.w[3], xv[3]));
-        float term = role.lane_on ? (static_cast<float>(I) * cur.s) * xscale : 0.f;
-        term = warp_sum(term);
-        if (lane == 0) {
-          if (a.S == 1) a.y[row] = term;
-          else part[(role.wj + i * a.wps) * a.S + role.sl] = term;
+  for (int i = 0; i < cnt; ++i) {
+    const int slot = i % a.ring;
+    if (!mbar_wait_bounded(&sm.full[slot], (i / a.ring) & 1, kWaitLimitNs)) {
+      record_device_error(kDevStageTimeout);
+      // give a copy still in flight the same time to land, then leave
+      mbar_wait_bounded(&sm.full[slot], (i / a.ring) & 1, kWaitLimitNs);
+      break;
+    }
+    const int row0 = (begin + i) * a.R;
+    const int rows = min(a.R, a.d - row0);
+    const int8_t* wst = reinterpret_cast<const int8_t*>(ring + static_cast<size_t>(slot) * a.stage_bytes);
+    const float* sst = reinterpret_cast<const float*>(wst + static_cast<size_t>(a.R) * a.n);
+    float* part = reinterpret_cast<float*>(smem + a.part_off) + slot * a.R * S;
+    if (warp_on) {
+      const int j0 = wj * RB;  // this warp's rows of the stage: j0 .. j0 + RB - 1
+      const int nvalid = rows - j0;
+      if (nvalid > 0) {
+        const int8_t* wr = wst + static_cast<size_t>(j0) * a.n + sl * kSlice;
+        const float* sr = sst + j0 * a.G + sl * 8 * K;
+        float v[RB];
+        if constexpr (F == Form::kW8A32)
+          rows_w8a32<RB>(wr, sr, a.n, a.G, nvalid, xd, fac, vmask, lane, v);
+        else
+          rows_w8a8<RB>(wr, sr, a.n, a.G, nvalid, xv, vmask, lane, xscale, v);
+        const float total = warp_sum_rows<RB>(v, lane);
+        constexpr int kLanesPerRow = 32 / RB;
+        const int r = lane / kLanesPerRow;
+        if ((lane & (kLanesPerRow - 1)) == 0 && r < nvalid) {
+          if (S == 1) a.y[row0 + j0 + r] = total;
+          else part[(j0 + r) * S + sl] = total;
         }
       }
-      cur = nxt;
     }
-    if (a.S > 1) {
-      __syncthreads();
-      combine_slices(a, part, row0);
-      __syncthreads();
+    // The last warp to finish with this slot sums the slices of its rows and
+    // refills the slot with stage i + ring.
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) {
+      __threadfence_block();
+      last = atomicAdd(&sm.counters[slot], 1) == kConsumerWarps - 1;
+      if (last) sm.counters[slot] = 0;
+      __threadfence_block();
+    }
+    if (__shfl_sync(0xffffffffu, last, 0)) {
+      if (S > 1) {
+        for (int rr = lane; rr < rows; rr += 32) {
+          float v = part[rr * S];
+          for (int s2 = 1; s2 < S; ++s2) v += part[rr * S + s2];
+          a.y[row0 + rr] = v;
+        }
+      }
+      if (lane == 0 && i + a.ring < cnt) {
+        fence_proxy_async_smem();  // this CTA's reads of the slot precede the copy's writes
+        issue_stage(a, ring, sm.full, begin + i + a.ring, slot);
+      }
+      __syncwarp();
     }
   }
 }
@@ -455,85 +517,84 @@ __global__ void __launch_bounds__(256)
 // ---------------------------------------------------------------------------
 namespace {
 
-enum class Form { kW8A32, kW8A8, kW8A8Fused };
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-size_t smem_bytes(Form f, int n, int R, int S) {
-  size_t stage = 0;
-  switch (f) {
-    case Form::kW8A32: stage = 4u * n; break;
-    case Form::kW8A8: stage = n; break;
-    case Form::kW8A8Fused: stage = 5u * n; break;
+// Stage geometry and shared-memory layout.  Returns false if the shape does
+// not fit the streaming kernel.
+bool plan_stream(Form f, const DeviceInfo& dev, int n, int d, StreamArgs* a, size_t* smem_out,
+                 int* grid_out) {
+  a->n = n;
+  a->d = d;
+  a->G = n / kGroup;
+  a->S = (n + slice_cols(f) - 1) / slice_cols(f);
+  if (a->S > kMaxSlices) return false;
+  a->wps = kConsumerWarps / a->S;
+  const int R = rows_per_warp(f) * a->wps;
+  a->R = R;
+  a->n_stages = (d + R - 1) / R;
+  a->stage_bytes = static_cast<uint32_t>(R) * n + static_cast<uint32_t>(R) * a->G * 4u;
+  // W8A32: four digit planes + per-group factors; fused W8A8: the int8 x.
+  const size_t xbytes =
+      (f == Form::kW8A32) ? 4u * n + (n / kGroup) * 4u : (f == Form::kW8A8 ? 0u : static_cast<size_t>(n));
+  a->x_off = kHeader;
+  a->ring_off = static_cast<uint32_t>(align_up(kHeader + xbytes, 128));
+  const size_t part_bytes = a->S > 1 ? static_cast<size_t>(R) * a->S * 4u : 0;
+  // Half of the SM's shared memory (minus the per-CTA reservation) lets the
+  // next kernel's CTA co-reside; fall back to a whole SM for huge rows.
+  const size_t half = static_cast<size_t>(dev.smem_per_sm) / 2 - 1024;
+  const size_t whole = static_cast<size_t>(dev.smem_optin_per_cta);
+  int ring = 0;
+  for (size_t budget : {half, whole}) {
+    if (budget <= a->ring_off) continue;
+    ring = static_cast<int>((budget - a->ring_off) / (a->stage_bytes + part_bytes + 16));
+    if (ring >= 2) break;
   }
-  const size_t part = (S > 1) ? static_cast<size_t>(R) * S * 4u : 0;
-  return kSmemHeader + ((stage + 15) & ~size_t(15)) + part;
+  if (ring < 2) return false;
+  if (ring > kMaxRing) ring = kMaxRing;
+  a->ring = ring;
+  a->part_off = static_cast<uint32_t>(align_up(a->ring_off + static_cast<size_t>(ring) * a->stage_bytes, 16));
+  *smem_out = a->part_off + ring * part_bytes;
+  // Two CTAs per SM (16 warps computing) once the matrix has two stages per
+  // SM; smaller ones take one slot and leave the second to the next kernel in
+  // the stream, which then fills its ring while this one runs.
+  const int min_stages_two = (launch_flags() & MLI_LAUNCH_ONE_CTA) ? 16 : 2;
+  const int per_sm = (a->n_stages >= min_stages_two * dev.sm_count &&
+                      2 * (*smem_out + 1024) <= static_cast<size_t>(dev.smem_per_sm)) ? 2 : 1;
+  *grid_out = a->n_stages < per_sm * dev.sm_count ? a->n_stages : per_sm * dev.sm_count;
+  return true;
 }
 
-// Tiles sized so that one wave of resident CTAs covers the matrix.
-GemvArgs plan(Form f, const DeviceInfo& dev, int n, int d, size_t* smem_out,
-              int* grid_out) {
-  GemvArgs a = {};
-  a.n = n;
-  a.d = d;
-  a.S = (n + kSliceCols - 1) / kSliceCols;
-  a.wps = kWarps / a.S;
-  const size_t smem0 = smem_bytes(f, n, 0, 1);
-  int ctas_per_sm = 2;
-  while (ctas_per_sm > 1 && static_cast<size_t>(ctas_per_sm) * (smem0 + 1024 + 8192) >
-                                static_cast<size_t>(dev.smem_per_sm))
-    --ctas_per_sm;
-  const int grid_cap = dev.sm_count * ctas_per_sm;
-  const long long warps_cap = static_cast<long long>(grid_cap) * a.wps;
-  int rpw = static_cast<int>((d + warps_cap - 1) / warps_cap);
-  if (rpw < 1) rpw = 1;
-  if (rpw > 64) rpw = 64;
-  a.rpw = rpw;
-  a.R = a.wps * rpw;
-  a.n_tiles = (d + a.R - 1) / a.R;
-  *grid_out = a.n_tiles < grid_cap ? a.n_tiles : grid_cap;
-  *smem_out = smem_bytes(f, n, a.R, a.S);
-  return a;
-}
+bool fast_path_ok(int n, int group_size) { return group_size == kGroup && n % 256 == 0; }
 
-bool fast_path_ok(int n, int group_size) {
-  return group_size == kGroup && n % 256 == 0 && n <= kMaxCols;
-}
-
-template <typename K>
-cudaError_t ensure_smem_attr(K kernel, size_t smem) {
-  return ensure_dynamic_smem(reinterpret_cast<const void*>(kernel), smem);
-}
-
-int launch_fast(Form f, GemvArgs args, cudaStream_t stream) {
+// Launches the streaming kernel; returns MLI_ERR_UNSUPPORTED (without
+// launching) when the shape does not fit, so the caller can fall back.
+int launch_stream(Form f, StreamArgs args, int n, int d, cudaStream_t stream) {
   cudaError_t err = cudaSuccess;
   const DeviceInfo& dev = current_device(&err);
   if (err != cudaSuccess) return set_status(MLI_ERR_CUDA, err);
   size_t smem = 0;
   int grid = 0;
-  GemvArgs p = plan(f, dev, args.n, args.d, &smem, &grid);
-  p.y = args.y;
-  p.x = args.x;
-  p.xq = args.xq;
-  p.xs = args.xs;
-  p.xq_out = args.xq_out;
-  p.xs_out = args.xs_out;
-  p.w = args.w;
-  p.s = args.s;
-  if (smem > static_cast<size_t>(dev.smem_optin_per_cta)) return set_status(MLI_ERR_UNSUPPORTED);
+  if (!plan_stream(f, dev, n, d, &args, &smem, &grid)) return MLI_ERR_UNSUPPORTED;
+  const void* kfn = nullptr;
+  switch (f) {
+    case Form::kW8A32: kfn = reinterpret_cast<const void*>(gemv_stream_kernel<Form::kW8A32>); break;
+    case Form::kW8A8: kfn = reinterpret_cast<const void*>(gemv_stream_kernel<Form::kW8A8>); break;
+    case Form::kW8A8Fused:
+      kfn = reinterpret_cast<const void*>(gemv_stream_kernel<Form::kW8A8Fused>);
+      break;
+  }
+  err = ensure_dynamic_smem(kfn, smem);
+  if (err != cudaSuccess) return check_cuda(err);
   switch (f) {
     case Form::kW8A32:
-      err = ensure_smem_attr(gemv_w8a32_g64_kernel, smem);
-      if (err == cudaSuccess)
-        err = launch(gemv_w8a32_g64_kernel, dim3(grid), dim3(kThreads), smem, stream, true, p);
+      err = launch(gemv_stream_kernel<Form::kW8A32>, dim3(grid), dim3(kThreads), smem, stream, true, args);
       break;
     case Form::kW8A8:
-      err = ensure_smem_attr(gemv_w8a8_g64_kernel<false>, smem);
-      if (err == cudaSuccess)
-        err = launch(gemv_w8a8_g64_kernel<false>, dim3(grid), dim3(kThreads), smem, stream, true, p);
+      err = launch(gemv_stream_kernel<Form::kW8A8>, dim3(grid), dim3(kThreads), smem, stream, true, args);
       break;
     case Form::kW8A8Fused:
-      err = ensure_smem_attr(gemv_w8a8_g64_kernel<true>, smem);
-      if (err == cudaSuccess)
-        err = launch(gemv_w8a8_g64_kernel<true>, dim3(grid), dim3(kThreads), smem, stream, true, p);
+      err = launch(gemv_stream_kernel<Form::kW8A8Fused>, dim3(grid), dim3(kThreads), smem, stream, true,
+                   args);
       break;
   }
   return check_cuda(err);
@@ -543,7 +604,7 @@ dim3 warp_per_row_grid(int d) { return dim3(static_cast<unsigned>((d + 7) / 8));
 
 }  // namespace
 
-// Launches the quantiser of one token (quant.cu).
+// Launches the quantiser of m tokens (quant.cu).
 int launch_quantize_rows(int8_t* xq, float* xs, const float* x, int m, int n,
                          cudaStream_t stream);
 
@@ -559,9 +620,10 @@ int mli_gemv_w8a32(float* y, const float* x, const int8_t* w_q, const float* w_s
     return set_status(MLI_ERR_INVALID_ARG);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (fast_path_ok(n, group_size) && aligned(x, 16) && aligned(w_q, 16) && aligned(w_s, 16)) {
-    GemvArgs a = {};
-    a.y = y; a.x = x; a.w = w_q; a.s = w_s; a.n = n; a.d = d;
-    return launch_fast(Form::kW8A32, a, st);
+    StreamArgs a = {};
+    a.y = y; a.x = x; a.w = w_q; a.s = w_s;
+    const int rc = launch_stream(Form::kW8A32, a, n, d, st);
+    if (rc != MLI_ERR_UNSUPPORTED) return rc;
   }
   return check_cuda(launch(gemv_w8a32_generic_kernel, warp_per_row_grid(d), dim3(256), 0, st,
                            true, y, x, w_q, w_s, n, d, group_size));
@@ -572,10 +634,11 @@ int mli_gemv_w8a8(float* y, const int8_t* xq, const float* xs, const int8_t* w_q
   if (!y || !xq || !xs || !w_q || !w_s || n <= 0 || d <= 0 || group_size <= 0)
     return set_status(MLI_ERR_INVALID_ARG);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (fast_path_ok(n, group_size) && aligned(xq, 16) && aligned(w_q, 16) && aligned(w_s, 4)) {
-    GemvArgs a = {};
-    a.y = y; a.xq = xq; a.xs = xs; a.w = w_q; a.s = w_s; a.n = n; a.d = d;
-    return launch_fast(Form::kW8A8, a, st);
+  if (fast_path_ok(n, group_size) && aligned(xq, 16) && aligned(w_q, 16) && aligned(w_s, 16)) {
+    StreamArgs a = {};
+    a.y = y; a.xq = xq; a.xs = xs; a.w = w_q; a.s = w_s;
+    const int rc = launch_stream(Form::kW8A8, a, n, d, st);
+    if (rc != MLI_ERR_UNSUPPORTED) return rc;
   }
   return check_cuda(launch(gemv_w8a8_generic_kernel, warp_per_row_grid(d), dim3(256), 0, st,
                            true, y, xq, xs, w_q, w_s, n, d, group_size));
@@ -588,17 +651,43 @@ int mli_gemv_w8a8_fused(float* y, int8_t* xq_out, float* xs_out, const float* x,
     return set_status(MLI_ERR_INVALID_ARG);
   if ((xq_out == nullptr) != (xs_out == nullptr)) return set_status(MLI_ERR_INVALID_ARG);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (fast_path_ok(n, group_size) && aligned(x, 16) && aligned(w_q, 16) && aligned(w_s, 4)) {
-    GemvArgs a = {};
+  if (fast_path_ok(n, group_size) && aligned(x, 16) && aligned(w_q, 16) && aligned(w_s, 16)) {
+    StreamArgs a = {};
     a.y = y; a.x = x; a.xq_out = xq_out; a.xs_out = xs_out; a.w = w_q; a.s = w_s;
-    a.n = n; a.d = d;
-    return launch_fast(Form::kW8A8Fused, a, st);
+    const int rc = launch_stream(Form::kW8A8Fused, a, n, d, st);
+    if (rc != MLI_ERR_UNSUPPORTED) return rc;
   }
-  // Unfused fallback for shapes outside the fast path: needs caller buffers.
+  // Unfused path for shapes outside the streaming kernel: needs caller buffers.
   if (xq_out == nullptr) return set_status(MLI_ERR_UNSUPPORTED);
   int rc = launch_quantize_rows(xq_out, xs_out, x, 1, n, st);
   if (rc != MLI_OK) return rc;
   return mli_gemv_w8a8(y, xq_out, xs_out, w_q, w_s, n, d, group_size, stream);
+}
+
+int mli_debug_plan_gemv(int form, int n, int d, int sm_count, int smem_per_sm,
+                        int smem_optin, int* out) {
+  if (!out || form < 0 || form > 2 || n <= 0 || d <= 0 || sm_count <= 0 || smem_per_sm <= 0 ||
+      smem_optin <= 0)
+    return set_status(MLI_ERR_INVALID_ARG);
+  if (!fast_path_ok(n, kGroup)) return set_status(MLI_ERR_UNSUPPORTED);
+  DeviceInfo dev;
+  dev.sm_count = sm_count;
+  dev.smem_per_sm = smem_per_sm;
+  dev.smem_optin_per_cta = smem_optin;
+  StreamArgs a = {};
+  size_t smem = 0;
+  int grid = 0;
+  if (!plan_stream(static_cast<Form>(form), dev, n, d, &a, &smem, &grid))
+    return set_status(MLI_ERR_UNSUPPORTED);
+  out[0] = grid;
+  out[1] = static_cast<int>(smem);
+  out[2] = a.S;
+  out[3] = a.wps;
+  out[4] = a.R;
+  out[5] = a.n_stages;
+  out[6] = a.ring;
+  out[7] = static_cast<int>(a.stage_bytes);
+  return set_status(MLI_OK);
 }
 
 int mli_debug_group_dots(int32_t* out, const int8_t* xq, const int8_t* w_q, int n,
@@ -606,8 +695,9 @@ int mli_debug_group_dots(int32_t* out, const int8_t* xq, const int8_t* w_q, int 
   if (!out || !xq || !w_q || n <= 0 || d <= 0 || group_size <= 0)
     return set_status(MLI_ERR_INVALID_ARG);
   const size_t total = static_cast<size_t>(d) * (n / group_size);
-  const unsigned blocks = static_cast<unsigned>((total + 255) / 256 < 65535 ? (total + 255) / 256 : 65535);
-  return check_cuda(launch(group_dots_kernel, dim3(blocks > 0 ? blocks : 1), dim3(256), 0,
+  const size_t want = (total + 255) / 256;
+  const unsigned blocks = static_cast<unsigned>(want < 65535 ? (want > 0 ? want : 1) : 65535);
+  return check_cuda(launch(group_dots_kernel, dim3(blocks), dim3(256), 0,
                            static_cast<cudaStream_t>(stream), false, out, xq, w_q, n, d,
                            group_size));
 }

@@ -71,6 +71,17 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar,
       : "memory");
 }
 
+// Orders this thread's earlier generic-proxy accesses of shared memory
+// before later async-proxy (bulk copy) accesses.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
 // Global -> shared bulk copy of `bytes` (multiple of 16, both addresses
 // 16-byte aligned), completion signalled on `bar` as transaction bytes.
 __device__ __forceinline__ void bulk_copy_g2s(void* dst_smem, const void* src,
@@ -180,11 +191,60 @@ __device__ __forceinline__ float2 biased_pair(uint32_t u_flipped) {
   return r;
 }
 
+// Named barrier 1 over the first `kCount` threads of the CTA (the consumer
+// warps of a warp-specialised kernel; the producer warp never joins it).
+template <int kCount>
+__device__ __forceinline__ void named_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kCount) : "memory");
+}
+// Same barrier, returning whether `pred` held on any participating thread.
+template <int kCount>
+__device__ __forceinline__ bool named_sync_or(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n.reg .pred p, q;\n"
+      "setp.ne.u32 p, %1, 0;\n"
+      "bar.red.or.pred q, 1, %2, p;\n"
+      "selp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred)), "n"(kCount)
+      : "memory");
+  return r != 0;
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
   return v;
 }
+// Sums RB per-lane values (one per row) across the warp at once: a
+// transposed butterfly halves the rows held per lane at offsets 16, 8, ...
+// and finishes with a plain butterfly.  Row r's total ends up in lane
+// r * (32 / RB) (among others).  Every row is summed with the same tree as
+// warp_sum -- pairs across lane bit 4 first, then bits 3, 2, 1, 0 -- so the
+// result is bit-identical to warp_sum of that row alone.
+template <int RB>
+__device__ __forceinline__ float warp_sum_rows(const float (&v)[RB], int lane) {
+  static_assert(RB == 1 || RB == 2 || RB == 4 || RB == 8, "RB must be 1, 2, 4 or 8");
+  float cur[RB];
+#pragma unroll
+  for (int i = 0; i < RB; ++i) cur[i] = v[i];
+  int off = 16;
+#pragma unroll
+  for (int width = RB; width > 1; width >>= 1, off >>= 1) {
+    const bool upper = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < width / 2; ++i) {
+      const float keep = upper ? cur[i + width / 2] : cur[i];
+      const float send = upper ? cur[i] : cur[i + width / 2];
+      cur[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+#pragma unroll
+  for (; off > 0; off >>= 1) cur[0] += __shfl_xor_sync(0xffffffffu, cur[0], off);
+  return cur[0];
+}
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1)

@@ -58,10 +58,12 @@ def make_case(d, n, seed, outliers=False):
 
 
 # (d, n): config shapes, ragged row counts, single group, fast-path limit,
-# and shapes that take the generic kernels (n % 256 != 0, n > 16384).
+# partial slices, and shapes that take the generic kernels (n % 256 != 0,
+# more than eight slices).
 SHAPES = [
     (2048, 2048), (512, 2048), (8192, 2048), (2048, 8192), (1024, 3072), (3072, 3072),
     (37, 2048), (1, 256), (300, 512), (5, 16384), (3, 16640), (9, 320), (7, 64),
+    (129, 6144), (40, 1280), (16, 12288),
 ]
 
 
@@ -252,6 +254,60 @@ def test_deterministic_and_stream_pdl_independent():
     ops.set_pdl(True)
     for o in outs[1:]:
         assert torch.equal(o, outs[0])
+
+
+@pytest.mark.parametrize("form", ["w8a32", "w8a8"])
+def test_dependent_chain_under_pdl(form):
+    """A chain where every GEMV consumes the previous one's output, launched
+    back to back on a side stream with programmatic dependent launch and
+    captured into a CUDA graph, equals the same chain run without PDL, and its
+    first link equals the oracle."""
+    dims = [2048, 8192, 2048, 512, 2048, 2048, 8192, 2048]
+    mats = []
+    for i in range(len(dims) - 1):
+        n, d = dims[i], dims[i + 1]
+        w_q, w_s = orc.quantize_weights(synth.weights_np(d, n, 500 + i, std=0.05))
+        mats.append((n, d, up(w_q), up(w_s), w_q, w_s))
+    x0 = synth.activation_np(dims[0], 9)
+    s = torch.cuda.Stream()
+
+    def run(pdl, graph):
+        ops.set_pdl(pdl)
+        bufs = [up(x0)] + [torch.empty(d, dtype=torch.float32, device=dev()) for d in dims[1:]]
+
+        def issue():
+            for i, (n, d, tw, ts, _, _) in enumerate(mats):
+                if form == "w8a32":
+                    ops.matmul_int8(bufs[i + 1], bufs[i], tw, ts, n, d, 64)
+                else:
+                    ops.matmul_dp4a_fused(bufs[i + 1], bufs[i], tw, ts, n, d, 64)
+
+        with torch.cuda.stream(s):
+            if graph:
+                issue()  # warm-up
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=s):
+                    issue()
+                for b in bufs[1:]:
+                    b.fill_(float("nan"))
+                g.replay()
+            else:
+                issue()
+        torch.cuda.synchronize()
+        ops.set_pdl(True)
+        return [b.cpu().numpy() for b in bufs]
+
+    ref = run(False, False)
+    for graph in (False, True):
+        got = run(True, graph)
+        for a, b in zip(got[1:], ref[1:]):
+            assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    n, d, _, _, w_q, w_s = mats[0]
+    if form == "w8a32":
+        assert orc.max_abs_rel(ref[1], orc.gemv_w8a32(x0, w_q, w_s)) <= TOL_W8A32
+    else:
+        xq, xs = orc.quantize_activation(x0)
+        assert orc.max_abs_rel(ref[1], orc.gemv_w8a8_f64(xq, xs, w_q, w_s)) <= TOL_W8A8
 
 
 def test_dropin_shim_matches_c_abi():
