@@ -27,6 +27,7 @@
 #ifndef MLI_GEMV_H
 #define MLI_GEMV_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -105,6 +106,58 @@ int mli_quantize_activation_rows(int8_t* xq, float* xs, const float* x, int m,
 int mli_gemm_w8a8(float* y, const int8_t* xq, const float* xs,
                   const int8_t* w_q, const float* w_s, int m, int n, int d,
                   int group_size, void* stream);
+
+/* ---- row-sharded linear layer across GPUs (one process per GPU) --------- */
+
+/* Peer buffers: device memory this process allocates and exports through a
+ * CUDA IPC handle (64 bytes), and opens from the other ranks' handles.  These
+ * set-up calls allocate; the step calls below do not.  The buffer is zeroed. */
+int mli_peer_alloc(size_t bytes, void** ptr, unsigned char* ipc_handle);
+int mli_peer_open(const unsigned char* ipc_handle, void** ptr);
+int mli_peer_close(void* ptr);
+int mli_peer_free(void* ptr);
+
+/* One rank's share of a row-sharded GEMV fused with the all-gather of its
+ * output (no reference counterpart: the reference runs its classifier,
+ * src/model_cuda_v2_shared.cu:418 / :564, on one GPU).  Rows
+ * [row_offset, row_offset + rows) of the d_total-row layer are computed from
+ * this rank's weight shard and stored over NVLink into every rank's logits
+ * buffer peer_logits[p] (each [2][d_total] fp32; the half is *step & 1);
+ * every CTA then adds its row count to peer_rows[p][rank] (uint64).
+ * peer_logits / peer_rows are HOST arrays of `world` device pointers (this
+ * rank's own buffers at index `rank`).  form: 0 W8A32, 2 fused W8A8. */
+int mli_gemv_rowshard(int form, float* const* peer_logits,
+                      unsigned long long* const* peer_rows, const unsigned* step,
+                      const float* x, const int8_t* w_q, const float* w_s, int n,
+                      int rows, int row_offset, int d_total, int rank, int world,
+                      int group_size, void* stream);
+
+/* Bytes of one rank's peer block for a d_total-row layer:
+ *   [0, 64)    uint64 row counters, one per source rank
+ *   [128, 132) uint32 step counter
+ *   [256, ...) fp32 logits [2][d_total], then (at the next 16-byte boundary)
+ *              the CTAs' (max, first index) partials int2 [2][8][512].
+ * mli_gemv_rowshard's peer_logits[p] and mli_rowshard_wait_argmax's logits
+ * point at offset 256 of a block, peer_rows[p] / rows_ctr at offset 0. */
+size_t mli_rowshard_block_bytes(int d_total);
+
+/* Completes a row-sharded step on this rank: waits until rank r's counter
+ * rows_ctr[r] reaches (*step + 1) * shard_rows[r] for every r (bounded by
+ * timeout_us; on expiry *out = -1 and the device error word is set), then
+ * reduces every rank's CTA partials of this step to the first maximum of the
+ * full logits (the reference's host argmax rule), writes its index to *out and
+ * increments *step.  form and n are the GEMV's (they fix each rank's CTA
+ * count); shard_rows is a HOST array of `world` row counts summing to
+ * d_total. */
+int mli_rowshard_wait_argmax(int form, int n, const float* logits,
+                             const unsigned long long* rows_ctr, unsigned* step,
+                             const int* shard_rows, int world, int d_total,
+                             long long* out, int timeout_us, void* stream);
+
+/* Index of the first maximum of x[0..n), on the device (replaces the
+ * reference's logits copy to the host and host argmax, src/main_cuda.cpp:96-98,
+ * src/model_cuda_v2_shared.cu:571-575).  NaN never wins; -0.0 equals +0.0. */
+int mli_argmax(const float* x, int n, long long* out, void* stream);
 
 /* ---- offline weight preparation ---------------------------------------- */
 

@@ -44,6 +44,15 @@ SIGNATURES = {
     "mli_quantize_weights": (_I, [_P, _P, _P, _I, _I, _I, _P]),
     "mli_debug_group_dots": (_I, [_P, _P, _P, _I, _I, _I, _P]),
     "mli_debug_plan_gemv": (_I, [_I, _I, _I, _I, _I, _I, ctypes.POINTER(_I)]),
+    "mli_peer_alloc": (_I, [ctypes.c_size_t, ctypes.POINTER(_P), ctypes.c_char_p]),
+    "mli_peer_open": (_I, [ctypes.c_char_p, ctypes.POINTER(_P)]),
+    "mli_peer_close": (_I, [_P]),
+    "mli_peer_free": (_I, [_P]),
+    "mli_gemv_rowshard": (_I, [_I, ctypes.POINTER(_P), ctypes.POINTER(_P), _P, _P, _P, _P, _I, _I, _I,
+                               _I, _I, _I, _I, _P]),
+    "mli_rowshard_wait_argmax": (_I, [_I, _I, _P, _P, _P, ctypes.POINTER(_I), _I, _I, _P, _I, _P]),
+    "mli_rowshard_block_bytes": (ctypes.c_size_t, [_I]),
+    "mli_argmax": (_I, [_P, _I, _P, _P]),
 }
 
 # The drop-in shim's C++ symbols (include/mli_gemv.h, reference include/model.h:62-64).

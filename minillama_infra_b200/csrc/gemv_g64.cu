@@ -58,15 +58,20 @@ constexpr int kMaxRing = 6;
 constexpr int kHeader = 256;
 
 // Shared-memory header: full[6] @0, reduction scratch (8 floats) @128,
-// per-slot completion counters (6 ints) @160.
+// per-slot completion counters (6 ints) @160, reduction indices (8 ints)
+// @192, CTA flags @224.
 struct Smem {
   uint64_t* full;
   float* red;
   int* counters;
+  int* red_i;
+  int* broken;
   __device__ explicit Smem(unsigned char* base)
       : full(reinterpret_cast<uint64_t*>(base)),
         red(reinterpret_cast<float*>(base + 128)),
-        counters(reinterpret_cast<int*>(base + 160)) {}
+        counters(reinterpret_cast<int*>(base + 160)),
+        red_i(reinterpret_cast<int*>(base + 192)),
+        broken(reinterpret_cast<int*>(base + 224)) {}
 };
 
 enum class Form : int { kW8A32 = 0, kW8A8 = 1, kW8A8Fused = 2 };
@@ -97,6 +102,15 @@ struct StreamArgs {
   int ring;         // ring slots
   uint32_t stage_bytes;  // R * n + R * G * 4
   uint32_t x_off, ring_off, part_off;
+  // Row-sharded output (world > 0): row r of this launch is global row
+  // row_offset + r; its value is stored into every rank's logits buffer
+  // peer_y[p] ([2][d_total], the half chosen by *step & 1), and every CTA
+  // then adds the number of rows it produced to peer_rows[p][rank].
+  int world, rank, row_offset, d_total;
+  uint32_t out_off;  // shared-memory staging of this CTA's output rows
+  const unsigned* step;
+  float* peer_y[kMaxPeers];
+  unsigned long long* peer_rows[kMaxPeers];
 };
 
 // ---------------------------------------------------------------------------
@@ -287,6 +301,48 @@ __device__ __forceinline__ void rows_w8a8(const int8_t* wr, const float* sr, int
 // ---------------------------------------------------------------------------
 // The streaming kernel
 // ---------------------------------------------------------------------------
+// Stores one finished output row: locally, or (row-sharded) into every rank's
+// logits buffer over NVLink.
+// Row-sharded launches stage the CTA's rows (a contiguous range) in shared
+// memory and publish them once at the end of the CTA.
+template <bool kPeer>
+__device__ __forceinline__ void store_row(const StreamArgs& a, int row, float v, float* staged,
+                                          int cta_row0) {
+  if constexpr (!kPeer) {
+    a.y[row] = v;
+  } else {
+    staged[row - cta_row0] = v;
+  }
+}
+
+// (max, first index) over v[0..n) by the CTA's 256 threads, scanning each
+// thread's elements in index order with a strict `>` and combining with the
+// first-maximum rule (larger value, then smaller index).  Result on thread 0.
+__device__ __forceinline__ void cta_first_max(const float* v, int n, int idx0, float* red_v,
+                                              int* red_i, float* out_v, int* out_i) {
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < n; i += kConsumerThreads)
+    if (v[i] > bv) { bv = v[i]; bi = idx0 + i; }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+  }
+  if ((threadIdx.x & 31) == 0) {
+    red_v[threadIdx.x >> 5] = bv;
+    red_i[threadIdx.x >> 5] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < kConsumerWarps; ++w)
+      if (red_v[w] > bv || (red_v[w] == bv && red_i[w] < bi)) { bv = red_v[w]; bi = red_i[w]; }
+    *out_v = bv;
+    *out_i = bi;
+  }
+}
+
 // Issues the bulk copies of stage `st` (rows st*R .. +R-1 and their scales)
 // into ring slot `slot`, completing on full[slot].
 __device__ __forceinline__ void issue_stage(const StreamArgs& a, unsigned char* ring, uint64_t* full,
@@ -302,7 +358,7 @@ __device__ __forceinline__ void issue_stage(const StreamArgs& a, unsigned char* 
                 &full[slot]);
 }
 
-template <Form F>
+template <Form F, bool kPeer>
 __global__ void __launch_bounds__(kThreads, 2) gemv_stream_kernel(const StreamArgs a) {
   extern __shared__ __align__(1024) unsigned char smem[];
   Smem sm(smem);
@@ -319,6 +375,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_stream_kernel(const StreamAr
       mbar_init(&sm.full[i], 1);
       sm.counters[i] = 0;
     }
+    *sm.broken = 0;
     fence_barrier_init();
     for (int i = 0; i < a.ring && i < cnt; ++i) issue_stage(a, ring, sm.full, begin + i, i);
   }
@@ -340,6 +397,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_stream_kernel(const StreamAr
 
   // The activation is the previous kernel's output: read it only now.
   griddep_wait();
+  const unsigned parity = kPeer ? (*a.step & 1u) : 0u;
+  float* staged = reinterpret_cast<float*>(smem + a.out_off);
+  const int cta_row0 = begin * a.R;
   float xscale = 0.f;
   uint4 xd[2][4];  // W8A32 digit planes of chunks 0, 1
   float fac[2];
@@ -385,10 +445,13 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_stream_kernel(const StreamAr
                                   : make_uint4(0, 0, 0, 0);
   }
 
+  if constexpr (kPeer) __syncthreads();  // x region becomes the output staging area
+
   for (int i = 0; i < cnt; ++i) {
     const int slot = i % a.ring;
     if (!mbar_wait_bounded(&sm.full[slot], (i / a.ring) & 1, kWaitLimitNs)) {
       record_device_error(kDevStageTimeout);
+      *sm.broken = 1;
       // give a copy still in flight the same time to land, then leave
       mbar_wait_bounded(&sm.full[slot], (i / a.ring) & 1, kWaitLimitNs);
       break;
@@ -413,7 +476,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_stream_kernel(const StreamAr
         constexpr int kLanesPerRow = 32 / RB;
         const int r = lane / kLanesPerRow;
         if ((lane & (kLanesPerRow - 1)) == 0 && r < nvalid) {
-          if (S == 1) a.y[row0 + j0 + r] = total;
+          if (S == 1) store_row<kPeer>(a, row0 + j0 + r, total, staged, cta_row0);
           else part[(j0 + r) * S + sl] = total;
         }
       }
@@ -433,7 +496,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_stream_kernel(const StreamAr
         for (int rr = lane; rr < rows; rr += 32) {
           float v = part[rr * S];
           for (int s2 = 1; s2 < S; ++s2) v += part[rr * S + s2];
-          a.y[row0 + rr] = v;
+          store_row<kPeer>(a, row0 + rr, v, staged, cta_row0);
         }
       }
       if (lane == 0 && i + a.ring < cnt) {
@@ -441,6 +504,36 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_stream_kernel(const StreamAr
         issue_stage(a, ring, sm.full, begin + i + a.ring, slot);
       }
       __syncwarp();
+    }
+  }
+  if constexpr (kPeer) {
+    // Publish the CTA's rows to every rank as one coalesced burst, with the
+    // rows' (max, first index) in this CTA's partial slot, then raise every
+    // rank's counter for this rank by the rows produced.
+    __syncthreads();
+    if (*sm.broken) return;  // never raise the counters for rows that were not produced
+    const int cta_rows = max(0, min((begin + cnt) * a.R, a.d) - cta_row0);
+    __shared__ float s_best_v;
+    __shared__ int s_best_i;
+    cta_first_max(staged, cta_rows, a.row_offset + cta_row0, sm.red, sm.red_i, &s_best_v, &s_best_i);
+    __syncthreads();
+    const size_t off = static_cast<size_t>(parity) * a.d_total + a.row_offset + cta_row0;
+    for (int p = 0; p < a.world; ++p) {
+      float* dst = a.peer_y[p] + off;
+      for (int i = threadIdx.x; i < cta_rows; i += kConsumerThreads) dst[i] = staged[i];
+      if (threadIdx.x == 0) {
+        int2* slot = rowshard_partials(a.peer_y[p], a.d_total) +
+                     (static_cast<size_t>(parity) * kMaxPeers + a.rank) * kMaxRankCtas + blockIdx.x;
+        *slot = make_int2(__float_as_int(s_best_v), s_best_i);
+      }
+    }
+    // The barrier orders every thread's stores before thread 0's system-scope
+    // fence, which (being cumulative) publishes them before the increments.
+    __syncthreads();
+    if (threadIdx.x == 0 && cta_rows > 0) {
+      __threadfence_system();
+      for (int p = 0; p < a.world; ++p)
+        atomicAdd_system(a.peer_rows[p] + a.rank, static_cast<unsigned long long>(cta_rows));
     }
   }
 }
@@ -521,8 +614,8 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // Stage geometry and shared-memory layout.  Returns false if the shape does
 // not fit the streaming kernel.
-bool plan_stream(Form f, const DeviceInfo& dev, int n, int d, StreamArgs* a, size_t* smem_out,
-                 int* grid_out) {
+bool plan_stream(Form f, const DeviceInfo& dev, int n, int d, bool peer, StreamArgs* a,
+                 size_t* smem_out, int* grid_out) {
   a->n = n;
   a->d = d;
   a->G = n / kGroup;
@@ -534,11 +627,20 @@ bool plan_stream(Form f, const DeviceInfo& dev, int n, int d, StreamArgs* a, siz
   a->n_stages = (d + R - 1) / R;
   a->stage_bytes = static_cast<uint32_t>(R) * n + static_cast<uint32_t>(R) * a->G * 4u;
   // W8A32: four digit planes + per-group factors; fused W8A8: the int8 x.
-  const size_t xbytes =
+  size_t xbytes =
       (f == Form::kW8A32) ? 4u * n + (n / kGroup) * 4u : (f == Form::kW8A8 ? 0u : static_cast<size_t>(n));
+  // Row-sharded launches stage a CTA's output rows (at most
+  // ceil(stages / min(stages, SMs)) stages of R rows) in the same region.
+  if (peer) {
+    const int g1 = a->n_stages < dev.sm_count ? a->n_stages : dev.sm_count;
+    const size_t out_bytes = static_cast<size_t>((a->n_stages + g1 - 1) / g1) * R * 4u;
+    if (out_bytes > 64 * 1024) return false;
+    if (out_bytes > xbytes) xbytes = out_bytes;
+  }
   a->x_off = kHeader;
   a->ring_off = static_cast<uint32_t>(align_up(kHeader + xbytes, 128));
   const size_t part_bytes = a->S > 1 ? static_cast<size_t>(R) * a->S * 4u : 0;
+
   // Half of the SM's shared memory (minus the per-CTA reservation) lets the
   // next kernel's CTA co-reside; fall back to a whole SM for huge rows.
   const size_t half = static_cast<size_t>(dev.smem_per_sm) / 2 - 1024;
@@ -553,6 +655,9 @@ bool plan_stream(Form f, const DeviceInfo& dev, int n, int d, StreamArgs* a, siz
   if (ring > kMaxRing) ring = kMaxRing;
   a->ring = ring;
   a->part_off = static_cast<uint32_t>(align_up(a->ring_off + static_cast<size_t>(ring) * a->stage_bytes, 16));
+  // Output rows are staged where the activation was prepared: every warp has
+  // copied its slice of x into registers before the first row is stored.
+  a->out_off = a->x_off;
   *smem_out = a->part_off + ring * part_bytes;
   // Two CTAs per SM (16 warps computing) once the matrix has two stages per
   // SM; smaller ones take one slot and leave the second to the next kernel in
@@ -574,31 +679,45 @@ int launch_stream(Form f, StreamArgs args, int n, int d, cudaStream_t stream) {
   if (err != cudaSuccess) return set_status(MLI_ERR_CUDA, err);
   size_t smem = 0;
   int grid = 0;
-  if (!plan_stream(f, dev, n, d, &args, &smem, &grid)) return MLI_ERR_UNSUPPORTED;
-  const void* kfn = nullptr;
-  switch (f) {
-    case Form::kW8A32: kfn = reinterpret_cast<const void*>(gemv_stream_kernel<Form::kW8A32>); break;
-    case Form::kW8A8: kfn = reinterpret_cast<const void*>(gemv_stream_kernel<Form::kW8A8>); break;
-    case Form::kW8A8Fused:
-      kfn = reinterpret_cast<const void*>(gemv_stream_kernel<Form::kW8A8Fused>);
-      break;
-  }
-  err = ensure_dynamic_smem(kfn, smem);
-  if (err != cudaSuccess) return check_cuda(err);
+  if (!plan_stream(f, dev, n, d, args.world > 0, &args, &smem, &grid)) return MLI_ERR_UNSUPPORTED;
+  if (args.world > 0 && grid > kMaxRankCtas) return set_status(MLI_ERR_UNSUPPORTED);
+  const bool peer = args.world > 0;
+  void (*kfn)(const StreamArgs) = nullptr;
   switch (f) {
     case Form::kW8A32:
-      err = launch(gemv_stream_kernel<Form::kW8A32>, dim3(grid), dim3(kThreads), smem, stream, true, args);
+      kfn = peer ? gemv_stream_kernel<Form::kW8A32, true> : gemv_stream_kernel<Form::kW8A32, false>;
       break;
     case Form::kW8A8:
-      err = launch(gemv_stream_kernel<Form::kW8A8>, dim3(grid), dim3(kThreads), smem, stream, true, args);
+      kfn = peer ? gemv_stream_kernel<Form::kW8A8, true> : gemv_stream_kernel<Form::kW8A8, false>;
       break;
     case Form::kW8A8Fused:
-      err = launch(gemv_stream_kernel<Form::kW8A8Fused>, dim3(grid), dim3(kThreads), smem, stream, true,
-                   args);
+      kfn = peer ? gemv_stream_kernel<Form::kW8A8Fused, true> : gemv_stream_kernel<Form::kW8A8Fused, false>;
       break;
   }
+  err = ensure_dynamic_smem(reinterpret_cast<const void*>(kfn), smem);
+  if (err != cudaSuccess) return check_cuda(err);
+  err = launch(kfn, dim3(grid), dim3(kThreads), smem, stream, true, args);
   return check_cuda(err);
 }
+
+}  // namespace
+
+// Grid of the row-sharded streaming GEMV for `rows` rows of width n on the
+// current device (0 if the launch would not fit), for the waiting side.
+int rowshard_grid(int form, int n, int rows) {
+  if (rows <= 0) return 0;
+  cudaError_t err = cudaSuccess;
+  const DeviceInfo& dev = current_device(&err);
+  if (err != cudaSuccess) return -1;
+  StreamArgs a = {};
+  size_t smem = 0;
+  int grid = 0;
+  if (!plan_stream(form == 0 ? Form::kW8A32 : Form::kW8A8Fused, dev, n, rows, true, &a, &smem, &grid))
+    return -1;
+  return grid;
+}
+
+namespace {
 
 dim3 warp_per_row_grid(int d) { return dim3(static_cast<unsigned>((d + 7) / 8)); }
 
@@ -664,6 +783,31 @@ int mli_gemv_w8a8_fused(float* y, int8_t* xq_out, float* xs_out, const float* x,
   return mli_gemv_w8a8(y, xq_out, xs_out, w_q, w_s, n, d, group_size, stream);
 }
 
+int mli_gemv_rowshard(int form, float* const* peer_logits, unsigned long long* const* peer_rows,
+                      const unsigned* step, const float* x, const int8_t* w_q, const float* w_s,
+                      int n, int rows, int row_offset, int d_total, int rank, int world,
+                      int group_size, void* stream) {
+  if (!peer_logits || !peer_rows || !step || !x || world <= 0 || world > kMaxPeers || rank < 0 ||
+      rank >= world || rows < 0 || row_offset < 0 || row_offset + rows > d_total || n <= 0 ||
+      group_size <= 0 || (form != 0 && form != 2))
+    return set_status(MLI_ERR_INVALID_ARG);
+  for (int p = 0; p < world; ++p)
+    if (!peer_logits[p] || !peer_rows[p]) return set_status(MLI_ERR_INVALID_ARG);
+  if (rows == 0) return set_status(MLI_OK);
+  if (!w_q || !w_s) return set_status(MLI_ERR_INVALID_ARG);
+  if (!fast_path_ok(n, group_size) || !aligned(x, 16) || !aligned(w_q, 16) || !aligned(w_s, 16))
+    return set_status(MLI_ERR_UNSUPPORTED);
+  StreamArgs a = {};
+  a.x = x; a.w = w_q; a.s = w_s;
+  a.world = world; a.rank = rank; a.row_offset = row_offset; a.d_total = d_total; a.step = step;
+  for (int p = 0; p < world; ++p) {
+    a.peer_y[p] = peer_logits[p];
+    a.peer_rows[p] = peer_rows[p];
+  }
+  return launch_stream(form == 0 ? Form::kW8A32 : Form::kW8A8Fused, a, n, rows,
+                       static_cast<cudaStream_t>(stream));
+}
+
 int mli_debug_plan_gemv(int form, int n, int d, int sm_count, int smem_per_sm,
                         int smem_optin, int* out) {
   if (!out || form < 0 || form > 2 || n <= 0 || d <= 0 || sm_count <= 0 || smem_per_sm <= 0 ||
@@ -677,7 +821,7 @@ int mli_debug_plan_gemv(int form, int n, int d, int sm_count, int smem_per_sm,
   StreamArgs a = {};
   size_t smem = 0;
   int grid = 0;
-  if (!plan_stream(static_cast<Form>(form), dev, n, d, &a, &smem, &grid))
+  if (!plan_stream(static_cast<Form>(form), dev, n, d, false, &a, &smem, &grid))
     return set_status(MLI_ERR_UNSUPPORTED);
   out[0] = grid;
   out[1] = static_cast<int>(smem);

@@ -18,8 +18,28 @@ enum DeviceError : unsigned int {
   kDevOk = 0,
   kDevStageTimeout = 1,  // bulk copy of the activation vector never landed
   kDevMmaTimeout = 2,    // tensor-core pipeline barrier never completed
+  kDevPeerTimeout = 3,   // rows of a row-sharded step never arrived from a rank
 };
 extern __device__ unsigned int g_device_error;
+
+// Row-sharded layers (gemv_g64.cu, rowshard.cu): at most this many ranks and
+// CTAs per rank.  Each rank's logits buffer ([2][d_total] fp32) is followed,
+// at the next 16-byte boundary, by the (max, first index) partials of every
+// CTA of every rank, int2 [2][kMaxPeers][kMaxRankCtas].
+constexpr int kMaxPeers = 8;
+constexpr int kMaxRankCtas = 512;
+
+__host__ __device__ __forceinline__ int2* rowshard_partials(float* logits, int d_total) {
+  const size_t bytes = (static_cast<size_t>(d_total) * 8u + 15u) & ~static_cast<size_t>(15);
+  return reinterpret_cast<int2*>(reinterpret_cast<char*>(logits) + bytes);
+}
+__host__ __device__ __forceinline__ const int2* rowshard_partials(const float* logits, int d_total) {
+  return rowshard_partials(const_cast<float*>(logits), d_total);
+}
+__host__ __device__ constexpr size_t rowshard_block_bytes(int d_total) {
+  return 256 + ((static_cast<size_t>(d_total) * 8u + 15u) & ~static_cast<size_t>(15)) +
+         sizeof(int2) * 2 * kMaxPeers * kMaxRankCtas;
+}
 
 __device__ __forceinline__ void record_device_error(unsigned int code) {
   atomicCAS(&g_device_error, 0u, code);

@@ -21,7 +21,7 @@ from ._lib import check, lib
 __all__ = [
     "matmul_int8", "matmul_dp4a", "quantize_activation", "matmul_dp4a_fused",
     "quantize_activation_rows", "gemm_w8a8", "quantize_weights", "group_dots",
-    "device_error", "set_pdl",
+    "device_error", "set_pdl", "copy_from_ptr",
 ]
 
 
@@ -98,6 +98,23 @@ def device_error() -> int:
     code = ctypes.c_uint(0)
     lib().mli_device_error(ctypes.byref(code))
     return int(code.value)
+
+
+def copy_from_ptr(dst, src_ptr: int, nbytes: int) -> None:
+    """Synchronous device-to-device copy from a raw device pointer (e.g. a peer
+    block of the row-sharded layer) into the CUDA tensor `dst`."""
+    lib()
+    for name in ("libcudart.so.12", "libcudart.so"):
+        try:
+            rt = ctypes.CDLL(name)
+            break
+        except OSError:
+            rt = None
+    if rt is None:
+        raise OSError("libcudart not found")
+    rc = rt.cudaMemcpy(ctypes.c_void_p(dst.data_ptr()), ctypes.c_void_p(src_ptr), ctypes.c_size_t(nbytes), 3)
+    if rc != 0:
+        raise RuntimeError(f"cudaMemcpy failed: {rc}")
 
 
 def set_pdl(enabled: bool) -> None:

@@ -1,0 +1,199 @@
+"""Row-sharded INT8 group-64 linear layer across the GPUs of one node.
+
+The 128256x2048 tied-embedding classifier of Llama-3.2-1B (src/model_cuda_v2_shared.cu:418,
+:564 in the reference, where it is a single-GPU fp32 matmul) and the FFN gate/up/down
+projections shard naturally by output rows: every row is an independent full-K dot, so no
+reduction crosses GPUs.  Rank r owns rows [r*chunk, min(d, (r+1)*chunk)) with
+chunk = ceil(d / world); after the local GEMV the fp32 outputs are all-gathered so every
+rank holds the full vector.  Because the GEMV's per-row arithmetic depends only on n, the
+gathered logits are bit-identical to the single-GPU result for any world size, and so is
+their argmax.
+
+One process per GPU; torch.distributed carries the collective (NCCL on GPUs, gloo in the
+CPU tests).  `compute` is pluggable so the same host logic runs over the CUDA kernels or,
+in the CPU tests, over the oracle.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+
+@dataclass(frozen=True)
+class RowShard:
+    d: int          # total rows
+    world: int
+    rank: int
+
+    @property
+    def chunk(self) -> int:
+        return math.ceil(self.d / self.world)
+
+    @property
+    def r0(self) -> int:
+        return min(self.d, self.rank * self.chunk)
+
+    @property
+    def r1(self) -> int:
+        return min(self.d, (self.rank + 1) * self.chunk)
+
+    @property
+    def rows(self) -> int:
+        return self.r1 - self.r0
+
+
+def row_shard(d: int, world: int, rank: int) -> RowShard:
+    if world <= 0 or not (0 <= rank < world) or d <= 0:
+        raise ValueError(f"bad shard request d={d} world={world} rank={rank}")
+    return RowShard(d, world, rank)
+
+
+class ShardedLinear:
+    """One rank's share of a row-sharded INT8 group-64 linear layer.
+
+    w_q / w_s hold only this rank's rows (int8 [rows][n], fp32 [rows][n/64]).
+    forward(x) computes the local rows into a padded chunk buffer and all-gathers the
+    chunks into `full`, whose first d entries are the layer's output in row order.
+    """
+
+    def __init__(self, w_q, w_s, d: int, n: int, rank: int, world: int, form: str = "w8a32",
+                 group=None, compute=None, device=None):
+        import torch
+
+        self.shard = row_shard(d, world, rank)
+        if w_q.shape[0] != self.shard.rows or w_q.shape[1] != n:
+            raise ValueError(f"weight shard {tuple(w_q.shape)} != ({self.shard.rows}, {n})")
+        if form not in ("w8a32", "w8a8"):
+            raise ValueError(f"unknown form {form}")
+        self.w_q, self.w_s, self.d, self.n, self.form = w_q, w_s, d, n, form
+        self.group = group
+        self.device = w_q.device if device is None else device
+        self.local = torch.zeros(self.shard.chunk, dtype=torch.float32, device=self.device)
+        self.full = torch.zeros(self.shard.chunk * world, dtype=torch.float32, device=self.device)
+        self.compute = compute if compute is not None else self._compute_cuda
+
+    def _compute_cuda(self, y, x):
+        from . import ops
+
+        if self.shard.rows == 0:
+            return
+        if self.form == "w8a32":
+            ops.matmul_int8(y, x, self.w_q, self.w_s, self.n, self.shard.rows, 64)
+        else:
+            ops.matmul_dp4a_fused(y, x, self.w_q, self.w_s, self.n, self.shard.rows, 64)
+
+    def forward(self, x):
+        import torch.distributed as dist
+
+        self.compute(self.local[: self.shard.rows], x)
+        if dist.get_backend(self.group) == "nccl":
+            dist.all_gather_into_tensor(self.full, self.local, group=self.group)
+        else:
+            parts = list(self.full.view(self.shard.world, self.shard.chunk).unbind(0))
+            dist.all_gather(parts, self.local, group=self.group)
+        return self.full[: self.d]
+
+
+class PeerShardedLinear:
+    """Row-sharded layer whose all-gather is fused into the GEMV.
+
+    Every rank allocates one peer block (CUDA IPC, no multicast; layout in
+    include/mli_gemv.h, mli_rowshard_block_bytes):
+        [0, 64)    uint64 row counters, one per source rank (raised over NVLink)
+        [128, 132) uint32 step counter (local)
+        [256, ...) fp32 logits [2][d] (the half is the step's parity), then the
+                   CTAs' (max, first index) partials
+    and opens every other rank's block.  A step is two launches on the current
+    stream: mli_gemv_rowshard (this rank's rows, stored into every rank's logits
+    with the CTAs' partials, then the counters raised) and
+    mli_rowshard_wait_argmax (bounded wait for all ranks' rows, argmax from the
+    partials, step + 1).  The handles travel through torch.distributed (any
+    backend); no collective runs on the data path.  world == 1 needs no
+    process group (the single GPU then gets the fused GEMV + argmax).
+    """
+
+    HEADER = 256
+
+    def __init__(self, w_q, w_s, d: int, n: int, rank: int, world: int, form: str = "w8a32",
+                 group=None, timeout_us: int = 2_000_000):
+        import ctypes
+
+        import torch
+        import torch.distributed as dist
+
+        from ._lib import check, lib
+
+        self.shard = row_shard(d, world, rank)
+        if form not in ("w8a32", "w8a8"):
+            raise ValueError(f"unknown form {form}")
+        if world > 8:
+            raise ValueError("at most 8 ranks")
+        self.w_q, self.w_s, self.d, self.n, self.rank, self.world = w_q, w_s, d, n, rank, world
+        self.form_code = 0 if form == "w8a32" else 2
+        self.timeout_us = timeout_us
+        self.lib = lib()
+        nbytes = self.lib.mli_rowshard_block_bytes(d)
+        self._own = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(64)
+        check(self.lib.mli_peer_alloc(nbytes, ctypes.byref(self._own), handle), "mli_peer_alloc")
+        handles = [handle.raw]
+        if world > 1:
+            handles = [None] * world
+            dist.all_gather_object(handles, handle.raw, group=group)
+        self._opened = []
+        bases = []
+        for p in range(world):
+            if p == rank:
+                bases.append(self._own.value)
+                continue
+            ptr = ctypes.c_void_p()
+            check(self.lib.mli_peer_open(handles[p], ctypes.byref(ptr)), "mli_peer_open")
+            self._opened.append(ptr.value)
+            bases.append(ptr.value)
+        P = ctypes.c_void_p
+        self._peer_logits = (P * world)(*[b + self.HEADER for b in bases])
+        self._peer_rows = (P * world)(*bases)
+        self._shard_rows = (ctypes.c_int * world)(*[row_shard(d, world, r).rows for r in range(world)])
+        self.base = self._own.value
+        self.out = torch.zeros((), dtype=torch.int64, device=w_q.device)
+        self.steps = 0
+        self.group = group
+        if world > 1:
+            dist.barrier(group=group)  # every rank has opened every block before any step
+
+    def logits(self, half: int):
+        """fp32 view of this rank's logits half (0 or 1) -- a device pointer wrapper."""
+        return self.base + self.HEADER + half * self.d * 4
+
+    def forward(self, x, stream=None):
+        import torch
+
+        from ._lib import check
+
+        st = torch.cuda.current_stream().cuda_stream if stream is None else stream
+        check(self.lib.mli_gemv_rowshard(self.form_code, self._peer_logits, self._peer_rows,
+                                         self.base + 128, x.data_ptr(), self.w_q.data_ptr(),
+                                         self.w_s.data_ptr(), self.n, self.shard.rows, self.shard.r0,
+                                         self.d, self.rank, self.world, 64, st), "mli_gemv_rowshard")
+        check(self.lib.mli_rowshard_wait_argmax(self.form_code, self.n, self.base + self.HEADER, self.base,
+                                                self.base + 128, self._shard_rows, self.world, self.d,
+                                                self.out.data_ptr(), self.timeout_us, st),
+              "mli_rowshard_wait_argmax")
+        self.steps += 1
+        return self.out
+
+    def close(self):
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.synchronize()
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        for p in self._opened:
+            self.lib.mli_peer_close(p)
+        self._opened = []
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        if self._own.value:
+            self.lib.mli_peer_free(self._own.value)
+            self._own.value = None
