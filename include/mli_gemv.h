@@ -99,13 +99,24 @@ int mli_gemv_w8a8_fused(float* y, int8_t* xq_out, float* xs_out,
 int mli_quantize_activation_rows(int8_t* xq, float* xs, const float* x, int m,
                                  int n, void* stream);
 
-/* Y[t][r] = sum_g ((float)I[t][r][g] * w_s[r][g]) * xs[t] for m tokens.
- * m >= 16 runs on the tcgen05 kind::i8 tensor-core path; smaller m on the
- * CUDA-core path.  Each token's row is within the W8A8 tolerance of
- * mli_gemv_w8a8 on that token. */
+/* Y[t][r] = xs[t] * sum_g w_s[r][g] * I[t][r][g] for m tokens (Y [m][d]).
+ * m >= 16 with n % 128 == 0 runs on the tcgen05 kind::i8 tensor-core path
+ * (tiles of 128 weight rows x up to 128 tokens); smaller m, or other shapes,
+ * on the CUDA-core path.  Each token's row is within the W8A8 tolerance of
+ * mli_gemv_w8a8 on that token.  `workspace` (device, may be NULL) lets the
+ * tensor-core path split K over CTAs to fill the GPU: it needs
+ * mli_gemm_w8a8_workspace_bytes(m, n, d) bytes, zeroed once before its first
+ * use (the kernel leaves it zeroed again); without it K is not split.  Calls
+ * that share a workspace must not overlap on the GPU. */
+size_t mli_gemm_w8a8_workspace_bytes(int m, int n, int d);
 int mli_gemm_w8a8(float* y, const int8_t* xq, const float* xs,
                   const int8_t* w_q, const float* w_s, int m, int n, int d,
-                  int group_size, void* stream);
+                  int group_size, void* workspace, size_t workspace_bytes,
+                  void* stream);
+/* The CUDA-core batched path alone, any m (for comparisons). */
+int mli_gemm_w8a8_cuda_core(float* y, const int8_t* xq, const float* xs,
+                            const int8_t* w_q, const float* w_s, int m, int n,
+                            int d, int group_size, void* stream);
 
 /* ---- row-sharded linear layer across GPUs (one process per GPU) --------- */
 

@@ -191,16 +191,34 @@ int gemm_w8a8_cuda_core(float* y, const int8_t* xq, const float* xs, const int8_
   return set_status(MLI_OK);
 }
 
+size_t gemm_tc_workspace_bytes(int m, int n, int d, int sm_count);
+int gemm_w8a8_tc(float* y, const int8_t* xq, const float* xs, const int8_t* w_q, const float* w_s,
+                 int m, int n, int d, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
 }  // namespace mli
 
 using namespace mli;
 
-extern "C" int mli_gemm_w8a8(float* y, const int8_t* xq, const float* xs,
-                             const int8_t* w_q, const float* w_s, int m, int n,
-                             int d, int group_size, void* stream) {
+extern "C" {
+
+size_t mli_gemm_w8a8_workspace_bytes(int m, int n, int d) {
+  if (m <= 0 || n <= 0 || d <= 0) return 0;
+  cudaError_t err = cudaSuccess;
+  const DeviceInfo& dev = current_device(&err);
+  if (err != cudaSuccess) return 0;
+  return gemm_tc_workspace_bytes(m, n, d, dev.sm_count);
+}
+
+int mli_gemm_w8a8(float* y, const int8_t* xq, const float* xs, const int8_t* w_q,
+                  const float* w_s, int m, int n, int d, int group_size, void* workspace,
+                  size_t workspace_bytes, void* stream) {
   if (!y || !xq || !xs || !w_q || !w_s || m <= 0 || n <= 0 || d <= 0 || group_size <= 0)
     return set_status(MLI_ERR_INVALID_ARG);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (group_size == 64 && m >= 16) {
+    const int rc = gemm_w8a8_tc(y, xq, xs, w_q, w_s, m, n, d, workspace, workspace_bytes, st);
+    if (rc != MLI_ERR_UNSUPPORTED) return rc;
+  }
   if (group_size == 64 && n % 256 == 0 && n <= 16384 && aligned(xq, 16) && aligned(w_q, 16) &&
       aligned(w_s, 4))
     return gemm_w8a8_cuda_core(y, xq, xs, w_q, w_s, m, n, d, st);
@@ -212,3 +230,15 @@ extern "C" int mli_gemm_w8a8(float* y, const int8_t* xq, const float* xs,
   }
   return set_status(MLI_OK);
 }
+
+/* The CUDA-core batched path alone (any m), for comparisons with the
+ * tensor-core path. */
+int mli_gemm_w8a8_cuda_core(float* y, const int8_t* xq, const float* xs, const int8_t* w_q,
+                            const float* w_s, int m, int n, int d, int group_size, void* stream) {
+  if (!y || !xq || !xs || !w_q || !w_s || m <= 0 || n <= 0 || d <= 0 || group_size != 64 ||
+      n % 256 != 0 || n > 16384 || !aligned(xq, 16) || !aligned(w_q, 16))
+    return set_status(MLI_ERR_INVALID_ARG);
+  return gemm_w8a8_cuda_core(y, xq, xs, w_q, w_s, m, n, d, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -20,7 +20,8 @@ from ._lib import check, lib
 
 __all__ = [
     "matmul_int8", "matmul_dp4a", "quantize_activation", "matmul_dp4a_fused",
-    "quantize_activation_rows", "gemm_w8a8", "quantize_weights", "group_dots",
+    "quantize_activation_rows", "gemm_w8a8", "gemm_w8a8_cuda_core", "gemm_workspace_bytes",
+    "quantize_weights", "group_dots",
     "device_error", "set_pdl", "copy_from_ptr",
 ]
 
@@ -77,10 +78,22 @@ def quantize_activation_rows(xq, xs, x, m: int, n: int, stream=None):
           "quantize_activation_rows")
 
 
-def gemm_w8a8(y, xq, xs, w_q, w_s, m: int, n: int, d: int, group_size: int = 64, stream=None):
-    """Batched W8A8 for m tokens: y[m][d]."""
+def gemm_workspace_bytes(m: int, n: int, d: int) -> int:
+    return int(lib().mli_gemm_w8a8_workspace_bytes(m, n, d))
+
+
+def gemm_w8a8(y, xq, xs, w_q, w_s, m: int, n: int, d: int, group_size: int = 64, workspace=None,
+              stream=None):
+    """Batched W8A8 for m tokens: y[m][d].  `workspace`: a zero-initialised
+    uint8 CUDA tensor of gemm_workspace_bytes(m, n, d) bytes (optional)."""
+    ws_ptr, ws_bytes = (None, 0) if workspace is None else (_ptr(workspace), workspace.numel())
     check(lib().mli_gemm_w8a8(_ptr(y), _ptr(xq), _ptr(xs), _ptr(w_q), _ptr(w_s), m, n, d,
-                              group_size, _stream(stream)), "gemm_w8a8")
+                              group_size, ws_ptr, ws_bytes, _stream(stream)), "gemm_w8a8")
+
+
+def gemm_w8a8_cuda_core(y, xq, xs, w_q, w_s, m: int, n: int, d: int, group_size: int = 64, stream=None):
+    check(lib().mli_gemm_w8a8_cuda_core(_ptr(y), _ptr(xq), _ptr(xs), _ptr(w_q), _ptr(w_s), m, n, d,
+                                        group_size, _stream(stream)), "gemm_w8a8_cuda_core")
 
 
 def quantize_weights(w_q, w_s, w, rows: int, cols: int, group_size: int = 64, stream=None):

@@ -191,17 +191,19 @@ def test_weight_quantiser_bit_exact(golden_dir):
         assert np.array_equal(s.cpu().numpy().view(np.uint32), s_ref.view(np.uint32))
 
 
-@pytest.mark.parametrize("m", [1, 2, 3, 5, 8, 13, 16, 17, 64])
-def test_gemm_w8a8_parity(m):
-    d, n = 640, 3072
-    w_q, w_s = orc.quantize_weights(synth.weights_np(d, n, 31 + m))
-    x = synth.activation_np(n, 32 + m, m=m, outliers=True)
+def _gemm_case(m, n, d, seed, workspace):
+    w_q, w_s = orc.quantize_weights(synth.weights_np(d, n, seed))
+    x = synth.activation_np(n, seed + 1, m=m, outliers=True)
     xq_ref, xs_ref = orc.quantize_activation(x)
     xq = torch.empty((m, n), dtype=torch.int8, device=dev())
     xs = torch.empty(m, dtype=torch.float32, device=dev())
     ops.quantize_activation_rows(xq, xs, up(x), m, n)
+    ws = None
+    if workspace:
+        ws = torch.zeros(ops.gemm_workspace_bytes(m, n, d), dtype=torch.uint8, device=dev())
     y = Guarded(m * d)
-    ops.gemm_w8a8(y.t, xq, xs, up(w_q), up(w_s), m, n, d, 64)
+    tw, ts = up(w_q), up(w_s)
+    ops.gemm_w8a8(y.t, xq, xs, tw, ts, m, n, d, 64, workspace=ws)
     torch.cuda.synchronize()
     assert np.array_equal(xq.cpu().numpy(), xq_ref)
     assert np.array_equal(xs.cpu().numpy().view(np.uint32), xs_ref.view(np.uint32))
@@ -209,6 +211,28 @@ def test_gemm_w8a8_parity(m):
     for t in range(m):
         ref = orc.gemv_w8a8_f64(xq_ref[t], xs_ref[t:t + 1], w_q, w_s)
         assert orc.max_abs_rel(got[t], ref) <= TOL_W8A8, t
+    return got, (xq, xs, tw, ts, ws)
+
+
+@pytest.mark.parametrize("m", [1, 2, 3, 5, 8, 13])
+def test_gemm_w8a8_cuda_core_parity(m):
+    _gemm_case(m, 3072, 640, 31 + m, workspace=False)
+
+
+# m >= 16 takes the tcgen05 kind::i8 path: token tiles of 16/32/64/128 (padded
+# tokens), partial weight tiles, with and without split-K workspace.
+@pytest.mark.parametrize("m,n,d", [(16, 256, 128), (16, 3072, 640), (17, 3072, 1024), (64, 1024, 300),
+                                   (100, 2048, 384), (128, 8192, 256), (256, 3072, 512), (300, 1024, 200)])
+@pytest.mark.parametrize("workspace", [False, True], ids=["no_ws", "splitk"])
+def test_gemm_w8a8_tensor_core_parity(m, n, d, workspace):
+    got, (xq, xs, tw, ts, ws) = _gemm_case(m, n, d, 7 * m + d, workspace)
+    if ws is not None:
+        assert int(ws.view(torch.int32)[:64].abs().sum()) == 0  # counters restored
+        y2 = torch.empty(m * d, dtype=torch.float32, device=dev())
+        ops.gemm_w8a8(y2, xq, xs, tw, ts, m, n, d, 64, workspace=ws)
+        torch.cuda.synchronize()
+        assert np.array_equal(y2.cpu().numpy().reshape(m, d).view(np.uint32), got.view(np.uint32))
+    assert ops.device_error() == 0
 
 
 def test_rows_are_independent_of_sharding():
