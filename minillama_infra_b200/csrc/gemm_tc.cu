@@ -37,7 +37,12 @@ constexpr int kChunk = 128;          // K bytes per stage (one 128-byte swizzle 
 constexpr int kStages = 6;
 constexpr int kThreads = 320;        // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
 constexpr int kEpiWarps = 8;
-constexpr int kAccBufs = 2;
+constexpr int kMaxAccBufs = 8;
+
+// Accumulator buffers per tile width: as many as tensor memory holds (512
+// columns), at most 8, so the MMAs run up to that many groups ahead of the
+// epilogue.
+__host__ __device__ constexpr int acc_bufs(int bn) { return 512 / bn < kMaxAccBufs ? 512 / bn : kMaxAccBufs; }
 
 struct Args {
   float* y;
@@ -143,7 +148,7 @@ struct Smem {
 
 __host__ __device__ constexpr uint32_t stage_bytes(int bn) { return 16384u + static_cast<uint32_t>(bn) * 128u; }
 __host__ __device__ constexpr uint32_t smem_bytes(int bn) {
-  return 1024u /* alignment slack */ + kStages * stage_bytes(bn) + 256u;
+  return 1024u /* alignment slack */ + kStages * stage_bytes(bn) + 512u;
 }
 
 __device__ __forceinline__ Smem carve(unsigned char* raw, int bn) {
@@ -156,8 +161,8 @@ __device__ __forceinline__ Smem carve(unsigned char* raw, int bn) {
   s.full = bars;
   s.empty = bars + kStages;
   s.acc_full = bars + 2 * kStages;
-  s.acc_empty = bars + 2 * kStages + kAccBufs;
-  s.tmem_base = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 2 * kAccBufs);
+  s.acc_empty = bars + 2 * kStages + kMaxAccBufs;
+  s.tmem_base = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 2 * kMaxAccBufs);
   s.flag = reinterpret_cast<int*>(s.tmem_base + 1);
   return s;
 }
@@ -187,7 +192,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int c_end = static_cast<int>((static_cast<long long>(split + 1) * a.chunks) / a.splits);
   const int nchunks = c_end - c_begin;
   const int ngroups = 2 * nchunks;
-  constexpr uint32_t kTmemCols = (2 * kBN <= 32) ? 32 : (2 * kBN <= 64 ? 64 : (2 * kBN <= 128 ? 128 : 256));
+  constexpr int kAccBufs = acc_bufs(kBN);
+  constexpr uint32_t kTmemCols = kAccBufs * kBN;  // 128, 256 or 512: a power of two
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
@@ -302,23 +308,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * quad) << 16) +
                              static_cast<uint32_t>(buf * kBN + half * kCols);
       if constexpr (kCols >= 32) {
+        uint32_t r[kCols / 32][32];
 #pragma unroll
-        for (int j0 = 0; j0 < kCols; j0 += 32) {
-          uint32_t r[32];
-          tmem_ld32(taddr + j0, r);
-          tmem_wait_ld();
+        for (int q = 0; q < kCols / 32; ++q) tmem_ld32(taddr + 32 * q, r[q]);
+        tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 32; ++j) acc[j0 + j] = fmaf(static_cast<float>(static_cast<int>(r[j])), wsc, acc[j0 + j]);
-        }
+        for (int q = 0; q < kCols / 32; ++q)
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            acc[32 * q + j] = fmaf(static_cast<float>(static_cast<int>(r[q][j])), wsc, acc[32 * q + j]);
       } else {
+        uint32_t r[kCols / 8][8];
 #pragma unroll
-        for (int j0 = 0; j0 < kCols; j0 += 8) {
-          uint32_t r[8];
-          tmem_ld8(taddr + j0, r);
-          tmem_wait_ld();
+        for (int q = 0; q < kCols / 8; ++q) tmem_ld8(taddr + 8 * q, r[q]);
+        tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 8; ++j) acc[j0 + j] = fmaf(static_cast<float>(static_cast<int>(r[j])), wsc, acc[j0 + j]);
-        }
+        for (int q = 0; q < kCols / 8; ++q)
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            acc[8 * q + j] = fmaf(static_cast<float>(static_cast<int>(r[q][j])), wsc, acc[8 * q + j]);
       }
       tmem_fence_before();
       __syncwarp();
@@ -359,16 +367,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       epi_sync();
       if (*sm.flag == 2 && row_ok) {
+        // Sum the splits in split order.  The split loop is outermost so the
+        // loads of all columns of one split are independent and in flight
+        // together.
         __threadfence();
+        float v[kCols];
+#pragma unroll
+        for (int j = 0; j < kCols; ++j) v[j] = 0.f;
+        for (int s2 = 0; s2 < a.splits; ++s2) {
+          if (s2 == split) {
+#pragma unroll
+            for (int j = 0; j < kCols; ++j) v[j] += acc[j];
+          } else {
+            const float* src = a.partial + static_cast<size_t>(s2) * a.m * a.d + row;
+            float pv[kCols];
+#pragma unroll
+            for (int j = 0; j < kCols; ++j) {
+              const int t = t_base + j < a.m ? t_base + j : a.m - 1;
+              pv[j] = __ldcg(src + static_cast<size_t>(t) * a.d);
+            }
+#pragma unroll
+            for (int j = 0; j < kCols; ++j) v[j] += pv[j];
+          }
+        }
 #pragma unroll
         for (int j = 0; j < kCols; ++j) {
           const int t = t_base + j;
-          if (t >= a.m) continue;
-          const size_t off = static_cast<size_t>(t) * a.d + row;
-          float v = 0.f;
-          for (int s2 = 0; s2 < a.splits; ++s2)
-            v += (s2 == split) ? acc[j] : __ldcg(a.partial + static_cast<size_t>(s2) * a.m * a.d + off);
-          a.y[off] = v * a.xs[t];
+          if (t < a.m) a.y[static_cast<size_t>(t) * a.d + row] = v[j] * a.xs[t];
         }
       }
     }
@@ -424,9 +449,11 @@ Plan plan(int m, int n, int d, int sm_count, bool have_ws) {
   p.tiles_m = (d + kBM - 1) / kBM;
   p.tiles_n = (m + p.bn - 1) / p.bn;
   p.chunks = n / kChunk;
+  // Split K so the tiles fill the SMs in one wave, keeping at least two
+  // 128-byte chunks (four groups) per split.
   const int tiles = p.tiles_m * p.tiles_n;
-  int splits = have_ws ? (sm_count + tiles - 1) / tiles : 1;
-  if (splits > p.chunks) splits = p.chunks;
+  int splits = have_ws ? sm_count / tiles : 1;
+  if (splits > p.chunks / 2) splits = p.chunks / 2;
   if (splits < 1) splits = 1;
   p.splits = splits;
   return p;
