@@ -113,6 +113,23 @@ int mli_gemm_w8a8(float* y, const int8_t* xq, const float* xs,
                   const int8_t* w_q, const float* w_s, int m, int n, int d,
                   int group_size, void* workspace, size_t workspace_bytes,
                   void* stream);
+/* Allocation-free variant of mli_gemm_w8a8 (no counterpart in the reference,
+ * which has no batched path).  For callers that cannot allocate device memory
+ * for a workspace -- a plugin whose host framework owns all device memory
+ * through its own pool, or a serving loop that must not allocate on the
+ * request path -- the split-K scratch lives in a fixed 12 MiB array inside
+ * the library, which every GPU that loads the library holds until the process
+ * exits.  Same results as mli_gemm_w8a8 with a large enough workspace.
+ * Accepts only the tensor-core shapes (m >= 16, n % 128 == 0, group_size 64,
+ * 16-byte aligned xq and w_q) and shapes whose workspace
+ * (mli_gemm_w8a8_workspace_bytes) fits 12 MiB -- every shape on a 148-SM
+ * B200 -- and returns MLI_ERR_UNSUPPORTED otherwise.  The first call on a
+ * device looks up the array's device address (make it before any stream
+ * capture).  All calls share the array and every call resets its counters:
+ * calls that overlap on the GPU race, so issue them in one stream order. */
+int mli_gemm_w8a8_noalloc(float* y, const int8_t* xq, const float* xs,
+                          const int8_t* w_q, const float* w_s, int m, int n,
+                          int d, int group_size, void* stream);
 /* The CUDA-core batched path alone, any m (for comparisons). */
 int mli_gemm_w8a8_cuda_core(float* y, const int8_t* xq, const float* xs,
                             const int8_t* w_q, const float* w_s, int m, int n,

@@ -43,6 +43,7 @@ SIGNATURES = {
     "mli_gemm_w8a8": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P, ctypes.c_size_t, _P]),
     "mli_gemm_w8a8_workspace_bytes": (ctypes.c_size_t, [_I, _I, _I]),
     "mli_gemm_w8a8_cuda_core": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P]),
+    "mli_gemm_w8a8_noalloc": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P]),
     "mli_quantize_weights": (_I, [_P, _P, _P, _I, _I, _I, _P]),
     "mli_debug_group_dots": (_I, [_P, _P, _P, _I, _I, _I, _P]),
     "mli_debug_plan_gemv": (_I, [_I, _I, _I, _I, _I, _I, ctypes.POINTER(_I)]),

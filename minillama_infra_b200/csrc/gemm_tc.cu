@@ -522,3 +522,67 @@ int gemm_w8a8_tc(float* y, const int8_t* xq, const float* xs, const int8_t* w_q,
 }
 
 }  // namespace mli
+
+// ---------------------------------------------------------------------------
+// Allocation-free batched W8A8 (mli_gemm_w8a8_noalloc)
+// ---------------------------------------------------------------------------
+// Some callers cannot allocate device memory for a workspace: a plugin whose
+// host framework owns every byte of device memory through its own pool, or a
+// serving loop whose policy forbids allocations on the request path.  This
+// entry point gives them the split-K tensor-core path anyway, with its scratch
+// (the per-tile counters and the per-split partial sums) in a fixed array
+// compiled into the library.  Every GPU that loads the library holds the array
+// until the process exits.  The array is sized for the largest split-K
+// workspace a B200 (148 SMs) can need: split-K never runs more partial tiles
+// than there are SMs, and a partial tile is at most 128 rows x 128 tokens of
+// fp32 (64 KiB), so 148 x 64 KiB plus the counters fits in 12 MiB.
+namespace mli {
+namespace {
+
+constexpr size_t kNoAllocWorkspaceBytes = 12u << 20;
+static __device__ __align__(256) unsigned char g_noalloc_workspace[kNoAllocWorkspaceBytes];
+
+constexpr int kMaxDevicesNoAlloc = 64;
+std::once_flag g_noalloc_once[kMaxDevicesNoAlloc];
+void* g_noalloc_ptr[kMaxDevicesNoAlloc];
+cudaError_t g_noalloc_err[kMaxDevicesNoAlloc];
+
+}  // namespace
+}  // namespace mli
+
+extern "C" int mli_gemm_w8a8_noalloc(float* y, const int8_t* xq, const float* xs,
+                                     const int8_t* w_q, const float* w_s, int m, int n, int d,
+                                     int group_size, void* stream) {
+  using namespace mli;
+  if (!y || !xq || !xs || !w_q || !w_s || m <= 0 || n <= 0 || d <= 0 || group_size <= 0)
+    return set_status(MLI_ERR_INVALID_ARG);
+  // Only the tensor-core shapes use scratch; everything else is rejected
+  // rather than silently run elsewhere.
+  if (group_size != 64 || m < 16 || n % tc::kChunk != 0 || !aligned(xq, 16) || !aligned(w_q, 16))
+    return set_status(MLI_ERR_UNSUPPORTED);
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return set_status(MLI_ERR_CUDA, err);
+  if (dev < 0 || dev >= kMaxDevicesNoAlloc) return set_status(MLI_ERR_UNSUPPORTED);
+  // Once per device, with that device current: the array's device address.
+  // In host code g_noalloc_workspace only names a host-side stand-in, so the
+  // kernel must be given this address, never the symbol itself.
+  std::call_once(g_noalloc_once[dev], [dev]() {
+    g_noalloc_err[dev] = cudaGetSymbolAddress(&g_noalloc_ptr[dev], g_noalloc_workspace);
+  });
+  if (g_noalloc_err[dev] != cudaSuccess) return set_status(MLI_ERR_CUDA, g_noalloc_err[dev]);
+  const DeviceInfo& info = current_device(&err);
+  if (err != cudaSuccess) return set_status(MLI_ERR_CUDA, err);
+  const size_t need = gemm_tc_workspace_bytes(m, n, d, info.sm_count);
+  if (need > kNoAllocWorkspaceBytes) return set_status(MLI_ERR_UNSUPPORTED);
+  // The array keeps the previous call's contents: the tile counters must
+  // start at zero, the partial sums are always written before they are read.
+  const tc::Plan p = tc::plan(m, n, d, info.sm_count, true);
+  if (p.splits > 1) {
+    const size_t cbytes = static_cast<size_t>(p.tiles_m) * p.tiles_n * sizeof(unsigned);
+    err = cudaMemsetAsync(g_noalloc_ptr[dev], 0, cbytes, static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return set_status(MLI_ERR_CUDA, err);
+  }
+  return gemm_w8a8_tc(y, xq, xs, w_q, w_s, m, n, d, g_noalloc_ptr[dev], kNoAllocWorkspaceBytes,
+                      static_cast<cudaStream_t>(stream));
+}
