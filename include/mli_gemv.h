@@ -3,7 +3,8 @@
  * (libmli_gemv.so).
  *
  * Every pointer is a caller-owned DEVICE pointer unless stated otherwise, and
- * no entry point allocates or frees memory.  Layouts are the ones the
+ * no compute entry point allocates or frees memory (the setup calls
+ * mli_peer_alloc and mli_chain_create do, and say so).  Layouts are the ones the
  * MiniLlama-Infra weight file and forward pass use (scripts/quantize_int8_group.py:67-71,
  * src/main_cuda.cpp:364-393, src/model_cuda_v2_shared.cu:384-412):
  *
@@ -57,7 +58,10 @@ int mli_version(void);                /* MAJOR*10000 + MINOR*100 + PATCH */
 unsigned mli_get_launch_flags(void);
 void mli_set_launch_flags(unsigned flags);
 /* Reads and clears the device error word of the current device: 0 when no
- * kernel gave up on a bounded wait since the last call. */
+ * kernel gave up on a bounded wait since the last call; otherwise the first
+ * code recorded: 1 a weight stage never landed in shared memory, 2 the
+ * tensor-core pipeline stalled, 3 a rank's rows of a row-sharded layer never
+ * arrived, 4 a chained GEMV's inputs were never completed. */
 int mli_device_error(unsigned* code_out);
 
 /* ---- batch-1 linear ops (the reference's matmul launchers) ------------- */
@@ -91,6 +95,55 @@ int mli_gemv_w8a8(float* y, const int8_t* xq, const float* xs,
 int mli_gemv_w8a8_fused(float* y, int8_t* xq_out, float* xs_out,
                         const float* x, const int8_t* w_q, const float* w_s,
                         int n, int d, int group_size, void* stream);
+
+/* ---- chained decode step (no reference counterpart) -------------------- */
+
+/* One GEMV of a chain: the arguments of mli_gemv_w8a32 (form 0),
+ * mli_gemv_w8a8 (form 1) or mli_gemv_w8a8_fused without xq_out/xs_out
+ * (form 2), plus `wait`: ops [0, wait) of the chain are complete before this
+ * op reads its activation or writes its output (0 <= wait <= own index).  A
+ * decode layer q, k, v, o, gate, up, down at chain index b..b+6 uses waits
+ * b, b, b, b+3, b+4, b+4, b+6 (o after the attention of q/k/v, gate/up after
+ * o, down after gate/up, the next layer after down). */
+typedef struct mli_gemv_op {
+  int form;       /* 0 W8A32, 1 W8A8 (xq, xs given), 2 W8A8 quantising x */
+  int n;          /* in-features: a multiple of 256 */
+  int d;          /* out-features */
+  int group_size; /* 64 */
+  int wait;       /* ops [0, wait) complete first */
+  int reserved;   /* 0 */
+  float* y;
+  const float* x;    /* forms 0 and 2 */
+  const int8_t* xq;  /* form 1 */
+  const float* xs;   /* form 1 */
+  const int8_t* w_q;
+  const float* w_s;
+} mli_gemv_op;
+
+typedef struct mli_chain mli_chain; /* opaque */
+
+/* Plans a chain of `count` GEMVs of one form for the current device: checks
+ * every op (MLI_ERR_INVALID_ARG / MLI_ERR_UNSUPPORTED as the single calls
+ * would; n % 256 == 0, 16-byte aligned x/xq, w_q, w_s), allocates a small
+ * device block (the op table and one counter per op) and copies the table
+ * with synchronous runtime calls: make it before any stream capture.  The
+ * op's pointers are baked in; the buffers they name must outlive the chain. */
+int mli_chain_create(const mli_gemv_op* ops, int count, mli_chain** chain);
+
+/* Runs the whole chain as one cooperative launch (one CTA per SM) on
+ * `stream`: every op's y is bit-identical to its single call.  A chain's runs
+ * must not overlap on the GPU (they share the counters); run it in one stream
+ * order.  Must be called with the chain's device current. */
+int mli_chain_run(mli_chain* chain, void* stream);
+
+/* Frees the chain's device block (synchronising like cudaFree). */
+int mli_chain_destroy(mli_chain* chain);
+
+/* Test hook: the chain plan on a hypothetical device without touching any
+ * GPU.  out[6] = grid, shared bytes per CTA, ring slots, slot bytes, work
+ * units (weight stages), activation epochs. */
+int mli_debug_plan_chain(const mli_gemv_op* ops, int count, int sm_count,
+                         int smem_optin, int* out);
 
 /* ---- batched decode (m independent tokens, no reference counterpart) -- */
 

@@ -27,6 +27,16 @@ MLI_LAUNCH_PDL = 1
 _P = ctypes.c_void_p
 _I = ctypes.c_int
 _U = ctypes.c_uint
+
+
+class GemvOp(ctypes.Structure):
+    """struct mli_gemv_op (include/mli_gemv.h): one GEMV of a chain."""
+    _fields_ = [("form", _I), ("n", _I), ("d", _I), ("group_size", _I), ("wait", _I),
+                ("reserved", _I), ("y", _P), ("x", _P), ("xq", _P), ("xs", _P), ("w_q", _P),
+                ("w_s", _P)]
+
+
+_OPS = ctypes.POINTER(GemvOp)
 SIGNATURES = {
     "mli_status_string": (ctypes.c_char_p, [_I]),
     "mli_last_status": (_I, []),
@@ -56,6 +66,10 @@ SIGNATURES = {
     "mli_rowshard_wait_argmax": (_I, [_I, _I, _P, _P, _P, ctypes.POINTER(_I), _I, _I, _P, _I, _P]),
     "mli_rowshard_block_bytes": (ctypes.c_size_t, [_I]),
     "mli_argmax": (_I, [_P, _I, _P, _P]),
+    "mli_chain_create": (_I, [_OPS, _I, ctypes.POINTER(_P)]),
+    "mli_chain_run": (_I, [_P, _P]),
+    "mli_chain_destroy": (_I, [_P]),
+    "mli_debug_plan_chain": (_I, [_OPS, _I, _I, _I, ctypes.POINTER(_I)]),
 }
 
 # The drop-in shim's C++ symbols (include/mli_gemv.h, reference include/model.h:62-64).

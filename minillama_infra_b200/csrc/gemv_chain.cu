@@ -1,0 +1,837 @@
+// gemv_chain.cu -- a decode step's chain of batch-1 INT8 group-64 GEMVs in one
+// persistent launch (sm_100a).
+//
+// A Llama decode step is a chain of small GEMVs (per layer: q, k, v, o, gate,
+// up, down) whose activations depend on one another: o reads the attention
+// output of q/k/v, gate/up the normalised residual after o, down the SwiGLU of
+// gate/up, the next layer's q/k/v the residual after down.  Launched one by
+// one, every GEMV pays a kernel boundary (the previous grid drains, the next
+// one fills its pipeline), and a 1-4 MB GEMV streams for well under a
+// microsecond, so the boundaries, not HBM, set the step time.
+//
+// Here one CTA per SM streams the weights of the whole chain without a
+// kernel boundary:
+//
+//  * Work units.  Every GEMV is cut into stages of whole rows (64 row slices
+//    of 1024 columns for W8A32, 32 of 2048 for W8A8: 64 KB of weights plus
+//    their scales), the stages of all GEMVs are numbered in chain order, and
+//    CTA c takes units c, c + G, c + 2G, ... (G = CTAs).  Each CTA moves its
+//    units through a ring of shared-memory slots with 1-D bulk copies;
+//    weights never depend on an activation, so the ring runs ahead across
+//    GEMV boundaries and across dependency waits.
+//  * Dependencies.  Op i names a prefix of the chain, ops [0, wait), that must
+//    be complete before it reads its activation (and before it writes its
+//    output).  Each op has a device counter of finished rows; a CTA adds its
+//    rows of an op once it has passed its last unit of that op (gpu-scope
+//    fence, atomic add), and before the first unit of an op whose prefix is
+//    not yet known to be complete it polls the counters with acquire loads,
+//    bounded by a time limit.  Units are processed in chain order by every
+//    CTA, so the earliest unfinished op never waits: with all CTAs resident
+//    (cooperative launch) the chain cannot deadlock.
+//  * Activations.  When the activation changes (a new "epoch": another
+//    vector, or the same vector after a dependency wait), the consumers read
+//    it with L2-coherent loads and prepare it: W8A32 as four int8 digit
+//    planes (digit_quad), fused W8A8 quantised (quant_quad) -- once per CTA
+//    into shared memory, or, when every warp owns its own slice of the row
+//    (W8A32 with n = 8192), by each warp in registers without a barrier.
+//    q/k/v (and gate/up) read one vector: one preparation.
+//  * Warp roles: consumer warps compute rows from the ring; a producer warp
+//    issues the bulk copies; a publisher warp accounts finished units, makes
+//    the rows visible (gpu-scope fence, counter add) and polls the counters an
+//    op waits for, so no consumer ever stalls on a global memory fence.
+//  * Rows are computed exactly as in gemv_stream_kernel (same row kernels,
+//    same slice order), so each op's output is bit-identical to the
+//    corresponding mli_gemv_* call.
+//  * The last CTA to finish returns every counter to zero, so the next launch
+//    (or graph replay) starts clean without a host-side reset.
+#include <cstring>
+#include <vector>
+
+#include "gemv_rows.cuh"
+#include "mli_common.cuh"
+#include "mli_internal.h"
+
+namespace mli {
+namespace chain {
+
+constexpr int kMaxRing = 6;
+constexpr int kHeader = 256;
+constexpr int kMaxSlices = 8;
+constexpr int kMaxOps = 1 << 16;
+
+// Device-side descriptor of one GEMV of the chain, 64 bytes (geometry
+// precomputed on the host, as plan_stream does for the single-GEMV kernel).
+// Kernels copy the table into shared memory when it fits.
+struct Op {
+  float* y;
+  const void* act;   // fp32 x (W8A32, fused W8A8) or int8 xq (W8A8)
+  const float* xs;   // W8A8 activation scale
+  const int8_t* w;
+  const float* s;
+  int n, d;          // in / out features
+  int unit_base;     // first work unit of this op
+  int wait;          // ops [0, wait) complete before this op reads its activation
+  int epoch;         // ops of one epoch read the same activation
+  uint16_t S, R;     // slices per row, rows per stage
+  __host__ __device__ const float* x() const { return static_cast<const float*>(act); }
+  __host__ __device__ const int8_t* xq() const { return static_cast<const int8_t*>(act); }
+  __host__ __device__ int G() const { return n / kGroup; }
+};
+static_assert(sizeof(Op) == 64, "chain op descriptor is 64 bytes");
+
+struct Args {
+  const Op* ops;        // global copy of the table
+  uint32_t table_off;   // its shared-memory copy (0: read it from global)
+  int count;
+  int units;            // stages of all ops
+  unsigned* done;       // [count] finished rows per op (zero between launches)
+  unsigned* finished;   // CTAs finished in this launch
+  int ring;
+  uint32_t slot_bytes;  // ring slot: the largest stage of the chain
+  uint32_t x_off, ring_off, part_off;
+  int part_stride;      // floats of split-K partials per slot
+};
+
+// Shared-memory header: full[6] @0, empty[6] @48, free[6] @96, per-slot
+// warp counters @144, flags @176, reduction scratch (one float per consumer
+// warp) @192.
+struct Smem {
+  uint64_t* full;   // weights of the slot's unit landed (bulk copy)
+  uint64_t* empty;  // consumers finished the slot's unit and stored its rows
+  uint64_t* free;   // the publisher has accounted for it: the slot may be refilled
+  int* counters;
+  volatile int* broken;
+  int* issued;
+  int* last_cta;
+  int* dep_known;   // ops [0, *dep_known) are known complete (publisher -> consumers)
+  float* red;
+  __device__ explicit Smem(unsigned char* b)
+      : full(reinterpret_cast<uint64_t*>(b)),
+        empty(reinterpret_cast<uint64_t*>(b + 48)),
+        free(reinterpret_cast<uint64_t*>(b + 96)),
+        counters(reinterpret_cast<int*>(b + 144)),
+        broken(reinterpret_cast<volatile int*>(b + 176)),
+        issued(reinterpret_cast<int*>(b + 180)),
+        last_cta(reinterpret_cast<int*>(b + 184)),
+        dep_known(reinterpret_cast<int*>(b + 188)),
+        red(reinterpret_cast<float*>(b + 192)) {}
+};
+
+__device__ __forceinline__ void st_release_cta(int* p, int v) {
+  asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_cta(const int* p) {
+  int v;
+  asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Op holding global unit u, searching forward from op `o` (units grow).
+__device__ __forceinline__ int find_op(const Op* ops, int count, int u, int o) {
+  while (o + 1 < count && ops[o + 1].unit_base <= u) ++o;
+  return o;
+}
+
+// Bulk copies of unit u (a stage of op o) into ring slot `slot`.
+__device__ __forceinline__ void issue_unit(const Args& a, const Op* ops, unsigned char* ring,
+                                           uint64_t* full, int o, int u, int slot) {
+  const Op& op = ops[o];
+  const int R = op.R, G = op.G();
+  const int row0 = (u - op.unit_base) * R;
+  const int rows = min(R, op.d - row0);
+  const uint32_t wb = static_cast<uint32_t>(rows) * op.n;
+  const uint32_t sb = static_cast<uint32_t>(rows) * G * 4u;
+  unsigned char* dst = ring + static_cast<size_t>(slot) * a.slot_bytes;
+  mbar_arrive_expect_tx(&full[slot], wb + sb);
+  bulk_copy_g2s(dst, op.w + static_cast<size_t>(row0) * op.n, wb, &full[slot]);
+  bulk_copy_g2s(dst + static_cast<size_t>(R) * op.n, op.s + static_cast<size_t>(row0) * G, sb,
+                &full[slot]);
+}
+
+__device__ __forceinline__ void fence_acq_rel_gpu() {
+  asm volatile("fence.acq_rel.gpu;" ::: "memory");
+}
+__device__ __forceinline__ void red_add_relaxed_gpu(unsigned* p, unsigned v) {
+  asm volatile("red.relaxed.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Publisher lane: waits until ops [from, to) have all their rows (acquire
+// loads), bounded in time.
+__device__ __forceinline__ bool wait_ops(const Args& a, const Op* ops, int from, int to) {
+  const uint64_t t0 = global_timer_ns();
+  for (int j = from; j < to; ++j) {
+    const unsigned target = static_cast<unsigned>(ops[j].d);
+    while (ld_acquire_gpu(a.done + j) < target)
+      if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------------------
+// Activation preparation.  The activation was written by other SMs of this
+// launch (or before it): L2-coherent loads, every load of a thread in flight
+// before the first is used.
+// ---------------------------------------------------------------------------
+constexpr int kPre = 8;  // float4 of activation held per consumer thread
+
+// Shared preparation: consumer thread t holds columns 4t + 4 kT j, j < kPre
+// (the whole activation for n <= 4 kT kPre).
+template <int kT>
+__device__ __forceinline__ void cta_x_load(const float* x, int n, float4 (&v)[kPre]) {
+  const int t = static_cast<int>(threadIdx.x);
+#pragma unroll
+  for (int j = 0; j < kPre; ++j) {
+    const int c = 4 * kT * j + 4 * t;
+    v[j] = c < n ? __ldcg(reinterpret_cast<const float4*>(x + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
+// W8A32 digit planes and group factors (digit_quad) of the held activation
+// into shared memory.
+template <int kT>
+__device__ __forceinline__ void cta_digits(const float4 (&v)[kPre], int n, int8_t* planes, float* fac) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int j = 0; j < kPre; ++j) {
+    const int c = 4 * kT * j + 4 * static_cast<int>(threadIdx.x);
+    if (4 * kT * j < n) digit_quad(v[j], c < n, c, n, planes, fac, lane);  // CTA-uniform
+  }
+}
+
+// Fused W8A8: the quantised activation into shared memory, bit-identical to
+// x_quant_prologue; from the held values when they cover n, else read twice.
+template <int kT>
+__device__ __forceinline__ float cta_quant(const float4 (&v)[kPre], const float* x, int n, int8_t* xq,
+                                           float* red) {
+  constexpr int kW = kT / 32;
+  const int t = static_cast<int>(threadIdx.x);
+  const bool hold = n <= 4 * kT * kPre;
+  float m = 0.f;
+  if (hold) {
+#pragma unroll
+    for (int j = 0; j < kPre; ++j)
+      m = fmaxf(m, fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w))));
+  } else {
+    for (int c = 4 * t; c < n; c += 4 * kT) {
+      const float4 u = __ldcg(reinterpret_cast<const float4*>(x + c));
+      m = fmaxf(m, fmaxf(fmaxf(fabsf(u.x), fabsf(u.y)), fmaxf(fabsf(u.z), fabsf(u.w))));
+    }
+  }
+  m = warp_max(m);
+  if ((t & 31) == 0) red[t >> 5] = m;
+  named_sync<kT>();
+  float amax = red[0];
+#pragma unroll
+  for (int w = 1; w < kW; ++w) amax = fmaxf(amax, red[w]);
+  const float scale = act_scale(amax);
+  const float inv = 1.0f / scale;
+  if (hold) {
+#pragma unroll
+    for (int j = 0; j < kPre; ++j) {
+      const int c = 4 * kT * j + 4 * t;
+      if (c < n) *reinterpret_cast<uint32_t*>(xq + c) = quant_quad(v[j], inv);
+    }
+  } else {
+    for (int c = 4 * t; c < n; c += 4 * kT)
+      *reinterpret_cast<uint32_t*>(xq + c) = quant_quad(__ldcg(reinterpret_cast<const float4*>(x + c)), inv);
+  }
+  return scale;
+}
+
+// Per-warp preparation (W8A32, when no two warps share a slice): the lane's
+// chunks k = 0, 1 of its slice, 16 columns each at col0 + 512k, as
+// v[4k + j] = columns col0 + 512k + 4j .. + 3.
+__device__ __forceinline__ void warp_x_load(const float* x, int col0, unsigned vmask, float4 (&v)[kPre]) {
+#pragma unroll
+  for (int k = 0; k < 2; ++k)
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      v[4 * k + j] = ((vmask >> k) & 1u) ? __ldcg(reinterpret_cast<const float4*>(x + col0 + 512 * k + 4 * j))
+                                        : make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+// The lane's digit planes of chunks 0, 1 in registers.  The quad of lanes
+// holding a group (group lane/4 + 8k of the slice) finds the group's max
+// together, so digits and factors are exactly those of digit_quad.
+__device__ __forceinline__ void warp_digits(const float4 (&v)[kPre], unsigned vmask, uint4 (&xd)[2][4],
+                                            float (&fac)[2]) {
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    float m = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float4 q = v[4 * k + j];
+      m = fmaxf(m, fmaxf(fmaxf(fabsf(q.x), fabsf(q.y)), fmaxf(fabsf(q.z), fabsf(q.w))));
+    }
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    const int e = static_cast<int>(__float_as_uint(m) >> 23);
+    float scale_up, factor;
+    if (e >= 13 && e <= 254) {
+      scale_up = __uint_as_float(static_cast<uint32_t>(259 - e) << 23);
+      factor = __uint_as_float(static_cast<uint32_t>(e - 12) << 23);
+    } else if (e == 255) {
+      scale_up = 0.f;
+      factor = __uint_as_float(0x7fc00000u);
+    } else {
+      scale_up = 0.f;
+      factor = 0.f;
+    }
+    uint32_t words[4][4];  // [plane][word]
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float4 q = v[4 * k + j];
+      uint32_t t0[4], t1[4], t2[4], t3[4];
+      digits4(q.x * scale_up, t0);
+      digits4(q.y * scale_up, t1);
+      digits4(q.z * scale_up, t2);
+      digits4(q.w * scale_up, t3);
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        const uint32_t lo = __byte_perm(t0[p], t1[p], 0x0040);
+        const uint32_t hi = __byte_perm(t2[p], t3[p], 0x0040);
+        words[p][j] = __byte_perm(lo, hi, 0x5410);
+      }
+    }
+    const bool valid = (vmask >> k) & 1u;
+#pragma unroll
+    for (int p = 0; p < 4; ++p)
+      xd[k][p] = valid ? make_uint4(words[p][0], words[p][1], words[p][2], words[p][3]) : make_uint4(0, 0, 0, 0);
+    fac[k] = valid ? factor : 0.f;
+  }
+}
+
+// A consumer warp's role in an op: its slice, its rows of a stage, and the
+// chunks of its lanes that fall inside the row.
+template <Form F, int kW>
+struct Role {
+  int sl, wj, col0;
+  bool on;
+  unsigned vmask;
+  __device__ Role(const Op& op, int warp, int lane) {
+    constexpr int K = chunks_per_lane(F);
+    const int S = op.S;
+    sl = warp % S;
+    wj = warp / S;
+    on = wj < kW / S;
+    const int g_slice = min(8 * K, op.G() - sl * 8 * K);
+    vmask = 0;
+#pragma unroll
+    for (int k = 0; k < K; ++k)
+      if (on && (lane >> 2) + 8 * k < g_slice) vmask |= 1u << k;
+    col0 = sl * slice_cols(F) + 16 * lane;
+  }
+};
+
+// Warps 0 .. kW-1 consume (kRB rows per warp per stage), warp kW is the
+// producer (bulk copies), warp kW + 1 the publisher (completion counters and
+// dependency polls).  Consumers never wait on global memory ordering: the
+// gpu-scope fences and the polls run on the publisher warp.
+template <Form F, int kW, int kRB>
+__global__ void __launch_bounds__((kW + 2) * 32, 1) gemv_chain_kernel(const Args a) {
+  constexpr int kT = kW * 32;  // consumer threads
+  extern __shared__ __align__(1024) unsigned char smem[];
+  Smem sm(smem);
+  unsigned char* ring = smem + a.ring_off;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grid = static_cast<int>(gridDim.x);
+  const int cta = static_cast<int>(blockIdx.x);
+  const int cnt = cta < a.units ? (a.units - 1 - cta) / grid + 1 : 0;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < a.ring; ++i) {
+      mbar_init(&sm.full[i], 1);
+      mbar_init(&sm.empty[i], 1);
+      mbar_init(&sm.free[i], 1);
+      sm.counters[i] = 0;
+    }
+    *sm.broken = 0;
+    *sm.last_cta = 0;
+    *sm.issued = 0;
+    *sm.dep_known = 0;
+    fence_barrier_init();
+  }
+  if (a.table_off != 0) {
+    const uint4* src = reinterpret_cast<const uint4*>(a.ops);
+    uint4* dst = reinterpret_cast<uint4*>(smem + a.table_off);
+    for (int i = threadIdx.x; i < a.count * 4; i += blockDim.x) dst[i] = __ldg(src + i);
+  }
+  __syncthreads();
+  const Op* ops = a.table_off != 0 ? reinterpret_cast<const Op*>(smem + a.table_off) : a.ops;
+
+  if (warp == kW) {
+    // ---- producer: unit i into slot i % ring once the publisher freed it
+    if (lane == 0) {
+      int o = 0;
+      for (int i = 0; i < cnt; ++i) {
+        const int slot = i % a.ring;
+        if (i >= a.ring && !mbar_wait_bounded(&sm.free[slot], ((i / a.ring) - 1) & 1, kWaitLimitNs)) {
+          record_device_error(kDevStageTimeout);
+          *sm.broken = 1;
+        }
+        if (*sm.broken) break;
+        const int u = cta + i * grid;
+        o = find_op(ops, a.count, u, o);
+        fence_proxy_async_smem();  // consumers' reads of the slot precede the copy's writes
+        issue_unit(a, ops, ring, sm.full, o, u, slot);
+        *sm.issued = i + 1;
+      }
+    }
+  } else if (warp == kW + 1) {
+    // ---- publisher: per unit in order, the dependency of its op (if the
+    // consumers will wait for one), then its completion; a CTA's rows of an
+    // op are published once it has passed its last unit of that op.
+    int o = 0, cur = -1, known = 0;
+    unsigned pending = 0;
+    for (int i = 0; i < cnt; ++i) {
+      const int u = cta + i * grid;
+      o = find_op(ops, a.count, u, o);
+      const Op& op = ops[o];
+      if (o != cur) {
+        cur = o;
+        if (op.wait > known) {
+          if (lane == 0 && !*sm.broken && !wait_ops(a, ops, known, op.wait)) {
+            record_device_error(kDevChainTimeout);
+            *sm.broken = 1;
+          }
+          known = op.wait;
+          __syncwarp();
+          if (lane == 0) st_release_cta(sm.dep_known, known);
+        }
+      }
+      if (lane == 0) {
+        const int slot = i % a.ring;
+        if (!mbar_wait_bounded(&sm.empty[slot], (i / a.ring) & 1, kWaitLimitNs)) {
+          record_device_error(kDevStageTimeout);
+          *sm.broken = 1;
+        }
+        mbar_arrive(&sm.free[slot]);
+        pending += static_cast<unsigned>(min(static_cast<int>(op.R), op.d - (u - op.unit_base) * op.R));
+        // the CTA's next unit (u + grid) belongs to a later op, or there is none
+        const bool last_of_op = i + 1 == cnt || (o + 1 < a.count && ops[o + 1].unit_base <= u + grid);
+        if (last_of_op) {
+          if (!*sm.broken) {
+            fence_acq_rel_gpu();  // with the add: release of the rows (stored by consumer warps)
+            red_add_relaxed_gpu(a.done + o, pending);
+          }
+          pending = 0;
+        }
+      }
+      __syncwarp();
+    }
+  } else {
+    // ---- consumers
+    constexpr int K = chunks_per_lane(F);
+    constexpr int kSlice = slice_cols(F);
+    constexpr int kLanesPerRow = 32 / kRB;
+    int o = 0, cur = -1, known = 0, epoch = -1;
+    int n = 0, d = 0, Gr = 0, S = 1, R = 0, base = 0;
+    float* y = nullptr;
+    int sl = 0, wj = 0;
+    bool warp_on = false;
+    unsigned vmask = 0;
+    float xscale = 0.f;
+    uint4 xd[2][4];  // W8A32 digit planes of chunks 0, 1
+    float fac[2];
+    uint4 xv[4];     // W8A8 int8 chunks 0..3
+    float4 pre[kPre];  // the activation's loads while it is prepared
+
+    for (int i = 0; i < cnt; ++i) {
+      const int u = cta + i * grid;
+      o = find_op(ops, a.count, u, o);
+      if (o != cur) {
+        const Op& op = ops[o];
+        const int wait = op.wait, ep = op.epoch;
+        if (wait > known) {
+          // The publisher polls the counters; each warp waits for its word.
+          if (lane == 0) {
+            const uint64_t t0 = global_timer_ns();
+            while (ld_acquire_cta(sm.dep_known) < wait && !*sm.broken) {
+              if (global_timer_ns() - t0 > 2 * kWaitLimitNs) {
+                record_device_error(kDevChainTimeout);
+                *sm.broken = 1;
+              }
+            }
+          }
+          __syncwarp();
+          known = wait;
+        }
+        n = op.n; d = op.d; Gr = op.G(); R = op.R; base = op.unit_base; y = op.y;
+        if (ep != epoch) {
+          epoch = ep;
+          const Role<F, kW> role(op, warp, lane);
+          S = op.S; sl = role.sl; wj = role.wj; warp_on = role.on; vmask = role.vmask;
+          const int col0 = role.col0;
+          if constexpr (F == Form::kW8A8) {
+            xscale = __ldcg(op.xs);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              xv[k] = ((vmask >> k) & 1u)
+                          ? __ldcg(reinterpret_cast<const uint4*>(op.xq() + col0 + 512 * k))
+                          : make_uint4(0, 0, 0, 0);
+          } else if (F == Form::kW8A32 && op.S == kW) {
+            // every warp owns its slice: prepare it in registers, no barrier
+            warp_x_load(op.x(), col0, vmask, pre);
+            if constexpr (F == Form::kW8A32) warp_digits(pre, vmask, xd, fac);
+          } else {
+            cta_x_load<kT>(op.x(), n, pre);
+            named_sync<kT>();  // every consumer is done reading the shared region
+            if constexpr (F == Form::kW8A32) {
+              int8_t* planes = reinterpret_cast<int8_t*>(smem + a.x_off);
+              float* facs = reinterpret_cast<float*>(planes + 4 * n);
+              cta_digits<kT>(pre, n, planes, facs);
+              named_sync<kT>();
+#pragma unroll
+              for (int k = 0; k < 2; ++k) {
+                const bool v = (vmask >> k) & 1u;
+#pragma unroll
+                for (int p = 0; p < 4; ++p)
+                  xd[k][p] = v ? *reinterpret_cast<const uint4*>(planes + p * n + col0 + 512 * k)
+                               : make_uint4(0, 0, 0, 0);
+                fac[k] = v ? facs[(col0 + 512 * k) >> 6] : 0.f;
+              }
+            } else {
+              int8_t* q8 = reinterpret_cast<int8_t*>(smem + a.x_off);
+              xscale = cta_quant<kT>(pre, op.x(), n, q8, sm.red);
+              named_sync<kT>();
+#pragma unroll
+              for (int k = 0; k < 4; ++k)
+                xv[k] = ((vmask >> k) & 1u) ? *reinterpret_cast<const uint4*>(q8 + col0 + 512 * k)
+                                            : make_uint4(0, 0, 0, 0);
+            }
+          }
+        }
+        cur = o;
+      }
+      const int slot = i % a.ring;
+      const int row0 = (u - base) * R;
+      const int rows = min(R, d - row0);
+      bool ok = !*sm.broken;
+      if (ok && !mbar_wait_bounded(&sm.full[slot], (i / a.ring) & 1, kWaitLimitNs)) {
+        record_device_error(kDevStageTimeout);
+        *sm.broken = 1;
+        ok = false;
+      }
+      ok = __all_sync(0xffffffffu, ok);
+      const int8_t* wst = reinterpret_cast<const int8_t*>(ring + static_cast<size_t>(slot) * a.slot_bytes);
+      const float* sst = reinterpret_cast<const float*>(wst + static_cast<size_t>(R) * n);
+      float* part = reinterpret_cast<float*>(smem + a.part_off) + slot * a.part_stride;
+      if (ok && warp_on) {
+        const int j0 = wj * kRB;
+        const int nvalid = rows - j0;
+        if (nvalid > 0) {
+          const int8_t* wr = wst + static_cast<size_t>(j0) * n + sl * kSlice;
+          const float* sr = sst + j0 * Gr + sl * 8 * K;
+          float v[kRB];
+          if constexpr (F == Form::kW8A32)
+            rows_w8a32<kRB>(wr, sr, n, Gr, nvalid, xd, fac, vmask, lane, v);
+          else
+            rows_w8a8<kRB>(wr, sr, n, Gr, nvalid, xv, vmask, lane, xscale, v);
+          const float total = warp_sum_rows<kRB>(v, lane);
+          const int r = lane / kLanesPerRow;
+          if ((lane & (kLanesPerRow - 1)) == 0 && r < nvalid) part[(j0 + r) * S + sl] = total;
+        }
+      }
+      // The last warp to finish with this slot sums the slices of its rows in
+      // slice order, stores them and hands the slot to the publisher.
+      __syncwarp();
+      int last = 0;
+      if (lane == 0) {
+        __threadfence_block();
+        last = atomicAdd(&sm.counters[slot], 1) == kW - 1;
+        if (last) sm.counters[slot] = 0;
+        __threadfence_block();
+      }
+      if (__shfl_sync(0xffffffffu, last, 0)) {
+        if (!*sm.broken) {
+          for (int rr = lane; rr < rows; rr += 32) {
+            float v = part[rr * S];
+            for (int s2 = 1; s2 < S; ++s2) v += part[rr * S + s2];
+            y[row0 + rr] = v;
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.empty[slot]);
+      }
+    }
+  }
+
+  __syncthreads();
+  if (threadIdx.x == kW * 32) {
+    // After an error, copies still in flight land before the CTA exits.
+    const int iss = *sm.issued;
+    for (int s = 0; s < a.ring && s < iss; ++s) {
+      const int last_i = s + ((iss - 1 - s) / a.ring) * a.ring;
+      mbar_wait_bounded(&sm.full[s], (last_i / a.ring) & 1, kWaitLimitNs);
+    }
+    __threadfence();
+    *sm.last_cta = atomicAdd(a.finished, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  // The last CTA returns the counters to zero for the next launch: every
+  // other CTA has left its loops, so nobody reads them any more.
+  if (*sm.last_cta) {
+    for (int j = threadIdx.x; j < a.count; j += (kW + 2) * 32) a.done[j] = 0;
+    if (threadIdx.x == 0) *a.finished = 0;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Kernel shape: consumer warps per CTA, rows per warp per stage, CTAs per SM.
+struct Variant {
+  int warps, rb, per_sm;
+};
+
+struct Plan {
+  std::vector<Op> ops;
+  Args args = {};
+  Variant v = {};
+  size_t smem = 0;
+  int grid = 0;
+  int epochs = 0;
+};
+
+bool overlaps(const void* a, size_t an, const void* b, size_t bn) {
+  const uintptr_t pa = reinterpret_cast<uintptr_t>(a), pb = reinterpret_cast<uintptr_t>(b);
+  return pa < pb + bn && pb < pa + an;
+}
+
+// The kernel shape for a chain of `form`: 8 consumer warps of 8 (W8A32) or
+// 4 (W8A8) rows each -- 64 row slices of 1024 columns (W8A32) or 32 of 2048
+// (W8A8) in flight per SM.  Launch flags bit 8 halves the rows per warp (for
+// comparisons).
+Variant pick_variant(int form, unsigned flags) {
+  const bool a32 = form == 0;
+  if (flags & (1u << 8)) return {8, a32 ? 4 : 2, 1};
+  return {8, a32 ? 8 : 4, 1};
+}
+
+// Validates the op list and lays out the chain.  Returns MLI_OK,
+// MLI_ERR_INVALID_ARG or MLI_ERR_UNSUPPORTED (without touching the device).
+int plan_chain(const mli_gemv_op* in, int count, int sm_count, int smem_per_sm, int smem_optin,
+               unsigned flags, Plan* p) {
+  if (!in || count <= 0 || sm_count <= 0 || smem_optin <= 0 || smem_per_sm <= 0)
+    return MLI_ERR_INVALID_ARG;
+  if (count > kMaxOps) return MLI_ERR_UNSUPPORTED;
+  const int form = in[0].form;
+  if (form < 0 || form > 2) return MLI_ERR_INVALID_ARG;
+  const Form f = static_cast<Form>(form);
+  const Variant var = pick_variant(form, flags);
+  p->v = var;
+  p->ops.assign(count, Op{});
+  long long units = 0;
+  size_t slot = 0, xbytes = 0;
+  int part_stride = 0, epoch = -1;
+  for (int i = 0; i < count; ++i) {
+    const mli_gemv_op& s = in[i];
+    if (s.form != form) return MLI_ERR_INVALID_ARG;
+    if (!s.y || !s.w_q || !s.w_s || s.n <= 0 || s.d <= 0 || s.group_size <= 0) return MLI_ERR_INVALID_ARG;
+    if (f == Form::kW8A8 ? (!s.xq || !s.xs) : !s.x) return MLI_ERR_INVALID_ARG;
+    if (s.wait < 0 || s.wait > i) return MLI_ERR_INVALID_ARG;
+    if (f != Form::kW8A8 && overlaps(s.y, 4u * s.d, s.x, 4u * s.n)) return MLI_ERR_INVALID_ARG;
+    if (s.group_size != kGroup || s.n % 256 != 0) return MLI_ERR_UNSUPPORTED;
+    if (!aligned(s.w_q, 16) || !aligned(s.w_s, 16) ||
+        !aligned(f == Form::kW8A8 ? static_cast<const void*>(s.xq) : s.x, 16))
+      return MLI_ERR_UNSUPPORTED;
+    Op& op = p->ops[i];
+    op.y = s.y;
+    op.act = f == Form::kW8A8 ? static_cast<const void*>(s.xq) : static_cast<const void*>(s.x);
+    op.xs = s.xs;
+    op.w = s.w_q;
+    op.s = s.w_s;
+    op.n = s.n;
+    op.d = s.d;
+    const int S = (s.n + slice_cols(f) - 1) / slice_cols(f);
+    if (S > kMaxSlices) return MLI_ERR_UNSUPPORTED;
+    const int R = var.rb * (var.warps / S);
+    op.S = static_cast<uint16_t>(S);
+    op.R = static_cast<uint16_t>(R);
+    const int n_stages = (s.d + R - 1) / R;
+    op.unit_base = static_cast<int>(units);
+    units += n_stages;
+    if (units > (1ll << 30)) return MLI_ERR_UNSUPPORTED;
+    op.wait = s.wait;
+    // Same activation as the previous op, with the same prefix to wait for:
+    // the CTA keeps its prepared copy.
+    const bool same = i > 0 && s.n == in[i - 1].n && s.wait == in[i - 1].wait &&
+                      (f == Form::kW8A8 ? (s.xq == in[i - 1].xq && s.xs == in[i - 1].xs)
+                                        : s.x == in[i - 1].x);
+    if (!same) ++epoch;
+    op.epoch = epoch;
+    const size_t stage = static_cast<size_t>(R) * s.n + static_cast<size_t>(R) * op.G() * 4u;
+    if (stage > slot) slot = stage;
+    // shared activation region: fused W8A8 its int8 copy; W8A32 its digit
+    // planes and group factors, unless every warp owns a slice (prepared in
+    // registers)
+    const size_t xb = f == Form::kW8A8Fused ? static_cast<size_t>(s.n)
+                      : (f == Form::kW8A32 && S < var.warps) ? 4u * s.n + op.G() * 4u : 0u;
+    if (xb > xbytes) xbytes = xb;
+    if (R * S > part_stride) part_stride = R * S;
+  }
+  Args& a = p->args;
+  a.count = count;
+  a.units = static_cast<int>(units);
+  a.slot_bytes = static_cast<uint32_t>(align_up(slot, 128));
+  a.part_stride = part_stride;
+  const size_t budget = var.per_sm == 1 ? static_cast<size_t>(smem_optin)
+                                        : static_cast<size_t>(smem_per_sm) / var.per_sm - 1024;
+  const size_t per_slot = a.slot_bytes + static_cast<size_t>(part_stride) * 4u;
+  // Layout: header | op table (when it fits) | activation region | ring | partials.
+  auto ring_for = [&](size_t table) -> int {
+    const size_t ring_off = align_up(kHeader + table + xbytes, 128);
+    if (budget <= ring_off) return 0;
+    const size_t r = (budget - ring_off) / per_slot;
+    return static_cast<int>(r < kMaxRing ? r : kMaxRing);
+  };
+  const size_t table = align_up(sizeof(Op) * count, 128);
+  const int ring_global = ring_for(0), ring_shared = ring_for(table);
+  // Keep the table in shared memory unless that costs a ring slot the chain
+  // needs (three slots keep the stream going across an op switch).
+  const bool shared_table = table <= 16384 && ring_shared >= (ring_global < 3 ? ring_global : 3);
+  a.table_off = shared_table ? kHeader : 0u;
+  a.x_off = static_cast<uint32_t>(kHeader + (shared_table ? table : 0));
+  a.ring_off = static_cast<uint32_t>(align_up(a.x_off + xbytes, 128));
+  const int ring = shared_table ? ring_shared : ring_global;
+  if (ring < 2) return MLI_ERR_UNSUPPORTED;
+  a.ring = ring;
+  a.part_off = static_cast<uint32_t>(a.ring_off + static_cast<size_t>(ring) * a.slot_bytes);
+  p->smem = a.part_off + static_cast<size_t>(ring) * part_stride * 4u;
+  p->grid = var.per_sm * sm_count;  // every CTA resident (cooperative launch)
+  p->epochs = epoch + 1;
+  return MLI_OK;
+}
+
+using KernelFn = void (*)(const Args);
+
+template <Form F>
+KernelFn kernel_shape(const Variant& v) {
+  if constexpr (F == Form::kW8A32)
+    return v.rb == 8 ? gemv_chain_kernel<F, 8, 8> : gemv_chain_kernel<F, 8, 4>;
+  else
+    return v.rb == 4 ? gemv_chain_kernel<F, 8, 4> : gemv_chain_kernel<F, 8, 2>;
+}
+
+KernelFn kernel_for(int form, const Variant& v) {
+  switch (form) {
+    case 0: return kernel_shape<Form::kW8A32>(v);
+    case 1: return kernel_shape<Form::kW8A8>(v);
+    default: return kernel_shape<Form::kW8A8Fused>(v);
+  }
+}
+
+}  // namespace chain
+}  // namespace mli
+
+struct mli_chain {
+  int device;
+  int form;
+  size_t smem;
+  int grid;
+  int threads;
+  mli::chain::KernelFn kernel;
+  mli::chain::Args args;
+  void* dev_mem;  // op table, then the counters
+};
+
+using namespace mli;
+
+extern "C" {
+
+int mli_chain_create(const mli_gemv_op* ops, int count, mli_chain** chain_out) {
+  if (!chain_out) return set_status(MLI_ERR_INVALID_ARG);
+  *chain_out = nullptr;
+  if (!ops || count <= 0) return set_status(MLI_ERR_INVALID_ARG);
+  cudaError_t err = cudaSuccess;
+  const DeviceInfo& dev = current_device(&err);
+  if (err != cudaSuccess) return set_status(MLI_ERR_CUDA, err);
+  chain::Plan p;
+  const int rc = chain::plan_chain(ops, count, dev.sm_count, dev.smem_per_sm, dev.smem_optin_per_cta,
+                                   launch_flags(), &p);
+  if (rc != MLI_OK) return set_status(rc);
+  const chain::KernelFn kfn = chain::kernel_for(ops[0].form, p.v);
+  const int threads = (p.v.warps + 2) * 32;
+  err = ensure_dynamic_smem(reinterpret_cast<const void*>(kfn), p.smem);
+  if (err != cudaSuccess) return check_cuda(err);
+  int per_sm = 0;
+  err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, threads, p.smem);
+  if (err != cudaSuccess) return check_cuda(err);
+  if (per_sm < p.v.per_sm) return set_status(MLI_ERR_UNSUPPORTED);
+  const size_t table = chain::align_up(sizeof(chain::Op) * count, 256);
+  const size_t counters = sizeof(unsigned) * (static_cast<size_t>(count) + 1);
+  void* mem = nullptr;
+  err = cudaMalloc(&mem, table + counters);
+  if (err != cudaSuccess) return set_status(MLI_ERR_CUDA, err);
+  err = cudaMemcpy(mem, p.ops.data(), sizeof(chain::Op) * count, cudaMemcpyHostToDevice);
+  if (err == cudaSuccess) err = cudaMemset(static_cast<char*>(mem) + table, 0, counters);
+  if (err != cudaSuccess) {
+    cudaFree(mem);
+    return set_status(MLI_ERR_CUDA, err);
+  }
+  mli_chain* c = new mli_chain;
+  c->device = dev.device;
+  c->form = ops[0].form;
+  c->smem = p.smem;
+  c->grid = p.grid;
+  c->threads = threads;
+  c->kernel = kfn;
+  c->args = p.args;
+  c->args.ops = static_cast<const chain::Op*>(mem);
+  c->args.done = reinterpret_cast<unsigned*>(static_cast<char*>(mem) + table);
+  c->args.finished = c->args.done + count;
+  c->dev_mem = mem;
+  *chain_out = c;
+  return set_status(MLI_OK);
+}
+
+int mli_chain_run(mli_chain* chain, void* stream) {
+  if (!chain) return set_status(MLI_ERR_INVALID_ARG);
+  int cur = -1;
+  cudaError_t err = cudaGetDevice(&cur);
+  if (err != cudaSuccess) return set_status(MLI_ERR_CUDA, err);
+  if (cur != chain->device) return set_status(MLI_ERR_INVALID_ARG);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(chain->grid);
+  cfg.blockDim = dim3(chain->threads);
+  cfg.dynamicSmemBytes = chain->smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return check_cuda(cudaLaunchKernelEx(&cfg, chain->kernel, chain->args));
+}
+
+int mli_chain_destroy(mli_chain* chain) {
+  if (!chain) return set_status(MLI_ERR_INVALID_ARG);
+  const cudaError_t err = cudaFree(chain->dev_mem);
+  delete chain;
+  return err == cudaSuccess ? set_status(MLI_OK) : set_status(MLI_ERR_CUDA, err);
+}
+
+int mli_debug_plan_chain(const mli_gemv_op* ops, int count, int sm_count, int smem_optin,
+                         int* out) {
+  if (!out) return set_status(MLI_ERR_INVALID_ARG);
+  chain::Plan p;
+  const int rc = chain::plan_chain(ops, count, sm_count, smem_optin + 1024, smem_optin, 0u, &p);
+  if (rc != MLI_OK) return set_status(rc);
+  out[0] = p.grid;
+  out[1] = static_cast<int>(p.smem);
+  out[2] = p.args.ring;
+  out[3] = static_cast<int>(p.args.slot_bytes);
+  out[4] = p.args.units;
+  out[5] = p.epochs;
+  return set_status(MLI_OK);
+}
+
+}  // extern "C"

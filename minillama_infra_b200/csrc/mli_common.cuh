@@ -19,6 +19,7 @@ enum DeviceError : unsigned int {
   kDevStageTimeout = 1,  // bulk copy of the activation vector never landed
   kDevMmaTimeout = 2,    // tensor-core pipeline barrier never completed
   kDevPeerTimeout = 3,   // rows of a row-sharded step never arrived from a rank
+  kDevChainTimeout = 4,  // a chained GEMV's inputs were never completed
 };
 extern __device__ unsigned int g_device_error;
 

@@ -16,13 +16,13 @@ from __future__ import annotations
 
 import ctypes
 
-from ._lib import check, lib
+from ._lib import GemvOp, check, lib
 
 __all__ = [
     "matmul_int8", "matmul_dp4a", "quantize_activation", "matmul_dp4a_fused",
     "quantize_activation_rows", "gemm_w8a8", "gemm_w8a8_cuda_core", "gemm_workspace_bytes",
     "quantize_weights", "group_dots",
-    "device_error", "set_pdl", "copy_from_ptr",
+    "device_error", "set_pdl", "copy_from_ptr", "GemvChain", "DECODE_LAYER_WAITS",
 ]
 
 
@@ -134,3 +134,53 @@ def set_pdl(enabled: bool) -> None:
     flags = lib().mli_get_launch_flags()
     flags = (flags | 1) if enabled else (flags & ~1)
     lib().mli_set_launch_flags(flags)
+
+
+# Waits of a decode layer's GEMVs q, k, v, o, gate, up, down at chain index
+# b + 0..6, relative to b: o after q/k/v (attention), gate/up after o (residual
+# + norm), down after gate/up (SwiGLU); the next layer's q/k/v wait for down.
+DECODE_LAYER_WAITS = (0, 0, 0, 3, 4, 4, 6)
+_FORMS = {"w8a32": 0, "w8a8": 1, "w8a8_fused": 2}
+
+
+class GemvChain:
+    """A chain of batch-1 GEMVs run as one persistent launch (mli_chain_*).
+
+    `ops` is a sequence of dicts with keys form ("w8a32", "w8a8" or
+    "w8a8_fused"), y, w_q, w_s, n, d, wait and x (or xq and xs for "w8a8");
+    tensors or raw device pointers.  Op i reads its activation only once ops
+    [0, wait) have finished.  Each op's y is bit-identical to the single call
+    (matmul_int8 / matmul_dp4a / matmul_dp4a_fused).  The buffers must
+    outlive the chain; the chain keeps references to the tensors given.
+    """
+
+    def __init__(self, ops, group_size: int = 64):
+        arr = (GemvOp * len(ops))()
+        self._keep = []
+        for i, o in enumerate(ops):
+            e = arr[i]
+            e.form = _FORMS[o["form"]]
+            e.n, e.d, e.group_size, e.wait, e.reserved = o["n"], o["d"], group_size, o.get("wait", 0), 0
+            for key in ("y", "x", "xq", "xs", "w_q", "w_s"):
+                t = o.get(key)
+                setattr(e, key, _ptr(t))
+                if t is not None and not isinstance(t, int):
+                    self._keep.append(t)
+        self.count = len(ops)
+        self._h = ctypes.c_void_p()
+        check(lib().mli_chain_create(arr, len(ops), ctypes.byref(self._h)), "mli_chain_create")
+
+    def run(self, stream=None):
+        check(lib().mli_chain_run(self._h, _stream(stream)), "mli_chain_run")
+
+    def close(self):
+        if self._h is not None and self._h.value:
+            lib().mli_chain_destroy(self._h)
+        self._h = None
+        self._keep = []
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,191 @@
+"""GPU checks of the chained GEMV launch (mli_chain_*) through the C ABI.
+
+Every op of a chain must give exactly (bit for bit) the output of its single
+call -- matmul_int8 / matmul_dp4a / matmul_dp4a_fused, whose own parity with
+the oracle is covered by test_gpu_parity.py -- whatever the dependencies:
+independent ops, a pure dependency chain (x of op i = y of op i - 1), and the
+decode structure with activation buffers reused by every layer (which also
+checks that no SM reads a stale activation from its L1).  One op of each
+chain is also checked against the oracle directly.
+"""
+import numpy as np
+import pytest
+
+from oracle import oracle as orc
+from minillama_infra_b200 import ops, synth
+from minillama_infra_b200._lib import MliError, lib
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+TOL = {"w8a32": 1e-5, "w8a8": 1e-6, "w8a8_fused": 1e-6}
+
+
+def dev():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    return torch.device("cuda:0")
+
+
+def weights(d, n, seed):
+    return synth.weights_gpu(d, n, seed=seed, device=dev())
+
+
+def single(form, y, x, q, s, n, d, xq=None, xs=None):
+    if form == "w8a32":
+        ops.matmul_int8(y, x, q, s, n, d, 64)
+    elif form == "w8a8":
+        ops.matmul_dp4a(y, xq, xs, q, s, n, d, 64)
+    else:
+        ops.matmul_dp4a_fused(y, x, q, s, n, d, 64)
+
+
+def bits(t):
+    return t.cpu().numpy().view(np.uint32)
+
+
+@pytest.mark.parametrize("form", ["w8a32", "w8a8", "w8a8_fused"])
+def test_chain_independent_ops_match_single_calls(form):
+    shapes = [(2048, 2048), (512, 2048), (512, 2048), (2048, 2048), (8192, 2048), (8192, 2048),
+              (2048, 8192), (300, 512), (37, 3072), (5, 1280)]
+    chain, refs = [], []
+    for i, (d, n) in enumerate(shapes):
+        q, s = weights(d, n, 50 + i)
+        x = torch.from_numpy(synth.activation_np(n, 90 + i, outliers=form != "w8a32")).to(dev())
+        op = dict(form=form, n=n, d=d, wait=0, w_q=q, w_s=s, y=torch.full((d,), float("nan"), device=dev()))
+        ref = torch.empty(d, device=dev())
+        if form == "w8a8":
+            xq = torch.empty(n, dtype=torch.int8, device=dev())
+            xs = torch.empty(1, device=dev())
+            ops.quantize_activation(xq, xs, x, n)
+            op.update(xq=xq, xs=xs)
+            single(form, ref, None, q, s, n, d, xq, xs)
+        else:
+            op.update(x=x)
+            single(form, ref, x, q, s, n, d)
+        chain.append(op)
+        refs.append(ref)
+    c = ops.GemvChain(chain)
+    for rep in range(3):  # counters return to zero between runs
+        for op in chain:
+            op["y"].fill_(float("nan"))
+        c.run()
+        torch.cuda.synchronize()
+        for i, (op, ref) in enumerate(zip(chain, refs)):
+            assert np.array_equal(bits(op["y"]), bits(ref)), (rep, i, shapes[i])
+    c.close()
+    assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("form", ["w8a32", "w8a8_fused"])
+def test_chain_dependencies_match_sequential_calls(form):
+    """x of op i is y of op i - 1 (wait = i): every op needs the whole output
+    of the previous one, produced by other SMs in the same launch."""
+    dims = [2048, 8192, 2048, 2048, 512, 1024, 8192, 2048]
+    bufs = [torch.from_numpy(synth.activation_np(dims[0], 7)).to(dev())]
+    bufs += [torch.full((d,), float("nan"), device=dev()) for d in dims[1:]]
+    ws = [weights(dims[i + 1], dims[i], 300 + i) for i in range(len(dims) - 1)]
+    chain = [dict(form=form, n=dims[i], d=dims[i + 1], wait=i, x=bufs[i], y=bufs[i + 1],
+                  w_q=ws[i][0], w_s=ws[i][1]) for i in range(len(dims) - 1)]
+    # sequential single calls into separate buffers
+    seq = [bufs[0].clone()] + [torch.empty(d, device=dev()) for d in dims[1:]]
+    for i in range(len(dims) - 1):
+        single(form, seq[i + 1], seq[i], ws[i][0], ws[i][1], dims[i], dims[i + 1])
+    torch.cuda.synchronize()
+    c = ops.GemvChain(chain)
+    for rep in range(3):
+        for b in bufs[1:]:
+            b.fill_(float("nan"))
+        c.run()
+        torch.cuda.synchronize()
+        for i in range(1, len(dims)):
+            assert np.array_equal(bits(bufs[i]), bits(seq[i])), (rep, i)
+    # first op against the oracle
+    x0 = bufs[0].cpu().numpy()
+    wq, wsc = ws[0][0].cpu().numpy(), ws[0][1].cpu().numpy()
+    if form == "w8a32":
+        ref = orc.gemv_w8a32_f64(x0, wq, wsc)
+    else:
+        xq, xs = orc.quantize_activation(x0)
+        ref = orc.gemv_w8a8_f64(xq, xs, wq, wsc)
+    assert orc.max_abs_rel(bufs[1].cpu().numpy(), ref) <= TOL[form]
+    c.close()
+    assert ops.device_error() == 0
+
+
+def _decode_chain(form, layers):
+    """Llama-3.2-1B layer GEMVs in decode order with the decode waits.  Four
+    activation buffers are reused by every layer, as in a forward pass: q/k/v
+    read A (the previous layer's down output), o reads q's output (standing in
+    for attention), gate/up read o's output, down reads gate's output."""
+    A = torch.from_numpy(synth.activation_np(2048, 11)).to(dev())
+    Q = torch.empty(2048, device=dev())
+    K = torch.empty(512, device=dev())
+    V = torch.empty(512, device=dev())
+    O = torch.empty(2048, device=dev())
+    Gt = torch.empty(8192, device=dev())
+    U = torch.empty(8192, device=dev())
+    outs = {"q": Q, "k": K, "v": V, "o": O, "gate": Gt, "up": U}
+    srcs = {"q": A, "k": A, "v": A, "o": Q, "gate": O, "up": O, "down": Gt}
+    w = [[weights(d, n, 1000 * l + i) for i, (_, d, n) in enumerate(synth.LLAMA_1B)] for l in range(layers)]
+    names = ["q", "k", "v", "o", "gate", "up", "down"]
+    chain = []
+    for l in range(layers):
+        for i, (_, d, n) in enumerate(synth.LLAMA_1B):
+            nm = names[i]
+            chain.append(dict(form=form, n=n, d=d, wait=7 * l + ops.DECODE_LAYER_WAITS[i],
+                              x=srcs[nm], y=outs.get(nm, A), w_q=w[l][i][0], w_s=w[l][i][1]))
+    return A, outs, w, chain
+
+
+@pytest.mark.parametrize("form", ["w8a32", "w8a8_fused"])
+def test_chain_decode_structure_reused_buffers(form):
+    layers = 3
+    A, outs, w, chain = _decode_chain(form, layers)
+    a0 = A.clone()
+    # reference: the same calls one by one (every layer feeds the next, so the
+    # final buffers depend on every op)
+    for l in range(layers):
+        for i, (_, d, n) in enumerate(synth.LLAMA_1B):
+            op = chain[7 * l + i]
+            single(form, op["y"], op["x"], op["w_q"], op["w_s"], n, d)
+    torch.cuda.synchronize()
+    final = {k: bits(v) for k, v in outs.items()}
+    final["a"] = bits(A)
+    c = ops.GemvChain(chain)
+    for rep in range(2):
+        A.copy_(a0)
+        for t in outs.values():
+            t.fill_(float("nan"))
+        c.run()
+        torch.cuda.synchronize()
+        assert np.array_equal(bits(A), final["a"]), rep
+        for k, t in outs.items():
+            assert np.array_equal(bits(t), final[k]), (rep, k)
+    # the same chain captured into a CUDA graph and replayed
+    stream = torch.cuda.Stream()
+    A.copy_(a0)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        c.run()
+    for rep in range(2):
+        A.copy_(a0)
+        g.replay()
+        torch.cuda.synchronize()
+        assert np.array_equal(bits(A), final["a"]), ("graph", rep)
+        assert np.array_equal(bits(outs["up"]), final["up"]), ("graph", rep)
+    del g
+    c.close()
+    assert ops.device_error() == 0
+
+
+def test_chain_rejects_bad_arguments():
+    l = lib()
+    assert l.mli_chain_run(None, None) == 1
+    assert l.mli_chain_destroy(None) == 1
+    q, s = weights(64, 256, 1)
+    x = torch.zeros(256, device=dev())
+    y = torch.zeros(64, device=dev())
+    with pytest.raises(MliError):
+        ops.GemvChain([dict(form="w8a32", n=256, d=64, wait=1, x=x, y=y, w_q=q, w_s=s)])
+    with pytest.raises(MliError):
+        ops.GemvChain([dict(form="w8a32", n=192, d=64, wait=0, x=x, y=y, w_q=q, w_s=s)])

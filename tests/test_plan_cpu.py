@@ -52,3 +52,88 @@ def test_plan_rejects_bad_arguments():
     assert l.mli_debug_plan_gemv(3, 2048, 2048, 148, 233472, 232448, out) == _lib.MLI_ERR_INVALID_ARG
     assert l.mli_debug_plan_gemv(0, 2048, 0, 148, 233472, 232448, out) == _lib.MLI_ERR_INVALID_ARG
     assert l.mli_debug_plan_gemv(0, 2000, 64, 148, 233472, 232448, out) == _lib.MLI_ERR_UNSUPPORTED
+
+
+# ---------------------------------------------------------------------------
+# Chain planner (mli_debug_plan_chain): fake, aligned device addresses only.
+# ---------------------------------------------------------------------------
+def _chain(layers=16, form=0, n_x=None):
+    """Decode-structured chain of the Llama-3.2-1B layer GEMVs."""
+    from minillama_infra_b200.ops import DECODE_LAYER_WAITS
+
+    mb = 1 << 20
+    arr = (_lib.GemvOp * (7 * layers))()
+    # activation buffers: 1 = layer input (q/k/v), 2 = attention out (o),
+    # 3 = ffn input (gate/up), 4 = SwiGLU out (down); reused by every layer
+    src = [1, 1, 1, 2, 3, 3, 4]
+    for l in range(layers):
+        for i, (_, d, n) in enumerate(synth.LLAMA_1B):
+            e = arr[7 * l + i]
+            e.form, e.n, e.d, e.group_size = form, n, d, 64
+            e.wait = 7 * l + DECODE_LAYER_WAITS[i]
+            if form == 1:
+                e.xq, e.xs = mb * (10 + src[i]), mb * (20 + src[i])
+            else:
+                e.x = mb * (10 + src[i])
+            e.y = mb * (100 + 7 * l + i)
+            e.w_q, e.w_s = mb * (1000 + 7 * l + i), mb * (2000 + 7 * l + i)
+    return arr
+
+
+def plan_chain(arr, count=None, sm=148, optin=232448):
+    out = (ctypes.c_int * 6)()
+    rc = _lib.lib().mli_debug_plan_chain(arr, len(arr) if count is None else count, sm, optin, out)
+    return rc, dict(zip(["grid", "smem", "ring", "slot", "units", "epochs"], out))
+
+
+@pytest.mark.parametrize("form", [0, 1, 2])
+def test_chain_plan_llama_step(form):
+    arr = _chain(16, form)
+    rc, p = plan_chain(arr)
+    assert rc == _lib.MLI_OK
+    assert p["grid"] == 148
+    assert p["smem"] <= B200["smem_optin"]
+    assert 2 <= p["ring"] <= 6
+    # every op's stage is 64 row slices of 1024 columns (W8A32) or 32 of 2048
+    # (W8A8): 64 KB of weights plus their scales, whatever n is
+    assert p["slot"] == 65536 + 65536 // 64 * 4
+    units = 0
+    for _, d, n in synth.LLAMA_1B:
+        rows = 65536 // n  # rows per stage
+        units += -(-d // rows)
+    assert p["units"] == 16 * units
+    # q/k/v share the layer input, gate/up the ffn input: 4 activations a layer
+    assert p["epochs"] == 16 * 4
+
+
+def test_chain_plan_rejects_bad_chains():
+    arr = _chain(1)
+    assert plan_chain(arr)[0] == _lib.MLI_OK
+    bad = _chain(1)
+    bad[3].wait = 4  # waits for itself
+    assert plan_chain(bad)[0] == _lib.MLI_ERR_INVALID_ARG
+    bad = _chain(1)
+    bad[2].form = 2  # mixed forms
+    assert plan_chain(bad)[0] == _lib.MLI_ERR_INVALID_ARG
+    bad = _chain(1)
+    bad[1].y = bad[1].x  # output over its own activation
+    assert plan_chain(bad)[0] == _lib.MLI_ERR_INVALID_ARG
+    bad = _chain(1)
+    bad[0].w_q = None
+    assert plan_chain(bad)[0] == _lib.MLI_ERR_INVALID_ARG
+    bad = _chain(1)
+    bad[4].n = 2000  # not a multiple of 256
+    assert plan_chain(bad)[0] == _lib.MLI_ERR_UNSUPPORTED
+    bad = _chain(1)
+    bad[5].group_size = 32
+    assert plan_chain(bad)[0] == _lib.MLI_ERR_UNSUPPORTED
+    bad = _chain(1)
+    bad[5].w_s += 4  # misaligned scales
+    assert plan_chain(bad)[0] == _lib.MLI_ERR_UNSUPPORTED
+    assert plan_chain(arr, count=0)[0] == _lib.MLI_ERR_INVALID_ARG
+    out = (ctypes.c_int * 6)()
+    assert _lib.lib().mli_debug_plan_chain(None, 3, 148, 232448, out) == _lib.MLI_ERR_INVALID_ARG
+    # W8A32 rows wider than eight 1024-column slices do not fit the row kernels
+    wide = _chain(1)
+    wide[6].n = 16384
+    assert plan_chain(wide)[0] == _lib.MLI_ERR_UNSUPPORTED
