@@ -140,8 +140,9 @@ int mli_chain_run(mli_chain* chain, void* stream);
 int mli_chain_destroy(mli_chain* chain);
 
 /* Test hook: the chain plan on a hypothetical device without touching any
- * GPU.  out[6] = grid, shared bytes per CTA, ring slots, slot bytes, work
- * units (weight stages), activation epochs. */
+ * GPU.  out[7] = grid, shared bytes per CTA, ring slots, slot bytes, work
+ * units (weight stages), activation epochs, phases (runs of ops between
+ * growing dependency prefixes). */
 int mli_debug_plan_chain(const mli_gemv_op* ops, int count, int sm_count,
                          int smem_optin, int* out);
 

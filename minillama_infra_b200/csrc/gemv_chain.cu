@@ -81,7 +81,9 @@ static_assert(sizeof(Op) == 64, "chain op descriptor is 64 bytes");
 
 struct Args {
   const Op* ops;        // global copy of the table
-  uint32_t table_off;   // its shared-memory copy (0: read it from global)
+  const int* phases;    // [n_phases + 1] first unit of every phase, then the unit count
+  uint32_t table_off;   // shared-memory copy of ops, then phases (0: read them from global)
+  int n_phases;
   int count;
   int units;            // stages of all ops
   unsigned* done;       // [count] finished rows per op (zero between launches)
@@ -136,6 +138,46 @@ __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
 __device__ __forceinline__ int find_op(const Op* ops, int count, int u, int o) {
   while (o + 1 < count && ops[o + 1].unit_base <= u) ++o;
   return o;
+}
+
+// A CTA's units, in chain order: in every phase (a run of ops that needs no
+// new dependency), CTA c of G takes the contiguous range
+// [start + c T / G, start + (c + 1) T / G) of the phase's T units.  Without
+// dependencies a CTA thus touches only a few ops (few activation changes);
+// with them every phase is still spread over all SMs.
+struct Cursor {
+  const int* ph;
+  int n_ph, cta, grid;
+  int p, u, hi;
+  __device__ void range() {
+    for (; p < n_ph; ++p) {
+      const long long lo = ph[p], t = ph[p + 1] - ph[p];
+      u = static_cast<int>(lo + t * cta / grid);
+      hi = static_cast<int>(lo + t * (cta + 1) / grid);
+      if (u < hi) return;
+    }
+    u = hi = 0;
+  }
+  __device__ Cursor(const int* phases, int n, int c, int g) : ph(phases), n_ph(n), cta(c), grid(g), p(0) {
+    range();
+  }
+  __device__ bool valid() const { return p < n_ph; }
+  __device__ void next() {
+    if (++u >= hi) {
+      ++p;
+      range();
+    }
+  }
+};
+
+// Units of CTA `cta` in all phases.
+__device__ __forceinline__ int cta_units(const int* ph, int n_ph, int cta, int grid) {
+  int c = 0;
+  for (int p = 0; p < n_ph; ++p) {
+    const long long lo = ph[p], t = ph[p + 1] - ph[p];
+    c += static_cast<int>(lo + t * (cta + 1) / grid - (lo + t * cta / grid));
+  }
+  return c;
 }
 
 // Bulk copies of unit u (a stage of op o) into ring slot `slot`.
@@ -342,7 +384,6 @@ __global__ void __launch_bounds__((kW + 2) * 32, 1) gemv_chain_kernel(const Args
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int grid = static_cast<int>(gridDim.x);
   const int cta = static_cast<int>(blockIdx.x);
-  const int cnt = cta < a.units ? (a.units - 1 - cta) / grid + 1 : 0;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < a.ring; ++i) {
@@ -361,22 +402,28 @@ __global__ void __launch_bounds__((kW + 2) * 32, 1) gemv_chain_kernel(const Args
     const uint4* src = reinterpret_cast<const uint4*>(a.ops);
     uint4* dst = reinterpret_cast<uint4*>(smem + a.table_off);
     for (int i = threadIdx.x; i < a.count * 4; i += blockDim.x) dst[i] = __ldg(src + i);
+    int* pdst = reinterpret_cast<int*>(smem + a.table_off + sizeof(Op) * a.count);
+    for (int i = threadIdx.x; i <= a.n_phases; i += blockDim.x) pdst[i] = __ldg(a.phases + i);
   }
   __syncthreads();
   const Op* ops = a.table_off != 0 ? reinterpret_cast<const Op*>(smem + a.table_off) : a.ops;
+  const int* phases =
+      a.table_off != 0 ? reinterpret_cast<const int*>(smem + a.table_off + sizeof(Op) * a.count) : a.phases;
+  const int cnt = cta_units(phases, a.n_phases, cta, grid);
 
   if (warp == kW) {
     // ---- producer: unit i into slot i % ring once the publisher freed it
     if (lane == 0) {
       int o = 0;
-      for (int i = 0; i < cnt; ++i) {
+      Cursor cur(phases, a.n_phases, cta, grid);
+      for (int i = 0; i < cnt; ++i, cur.next()) {
         const int slot = i % a.ring;
         if (i >= a.ring && !mbar_wait_bounded(&sm.free[slot], ((i / a.ring) - 1) & 1, kWaitLimitNs)) {
           record_device_error(kDevStageTimeout);
           *sm.broken = 1;
         }
         if (*sm.broken) break;
-        const int u = cta + i * grid;
+        const int u = cur.u;
         o = find_op(ops, a.count, u, o);
         fence_proxy_async_smem();  // consumers' reads of the slot precede the copy's writes
         issue_unit(a, ops, ring, sm.full, o, u, slot);
@@ -389,8 +436,10 @@ __global__ void __launch_bounds__((kW + 2) * 32, 1) gemv_chain_kernel(const Args
     // op are published once it has passed its last unit of that op.
     int o = 0, cur = -1, known = 0;
     unsigned pending = 0;
+    Cursor it(phases, a.n_phases, cta, grid);
     for (int i = 0; i < cnt; ++i) {
-      const int u = cta + i * grid;
+      const int u = it.u;
+      it.next();  // now at the CTA's next unit (if any)
       o = find_op(ops, a.count, u, o);
       const Op& op = ops[o];
       if (o != cur) {
@@ -413,8 +462,8 @@ __global__ void __launch_bounds__((kW + 2) * 32, 1) gemv_chain_kernel(const Args
         }
         mbar_arrive(&sm.free[slot]);
         pending += static_cast<unsigned>(min(static_cast<int>(op.R), op.d - (u - op.unit_base) * op.R));
-        // the CTA's next unit (u + grid) belongs to a later op, or there is none
-        const bool last_of_op = i + 1 == cnt || (o + 1 < a.count && ops[o + 1].unit_base <= u + grid);
+        // the CTA's next unit belongs to a later op, or there is none
+        const bool last_of_op = i + 1 == cnt || (o + 1 < a.count && ops[o + 1].unit_base <= it.u);
         if (last_of_op) {
           if (!*sm.broken) {
             fence_acq_rel_gpu();  // with the add: release of the rows (stored by consumer warps)
@@ -442,8 +491,9 @@ __global__ void __launch_bounds__((kW + 2) * 32, 1) gemv_chain_kernel(const Args
     uint4 xv[4];     // W8A8 int8 chunks 0..3
     float4 pre[kPre];  // the activation's loads while it is prepared
 
-    for (int i = 0; i < cnt; ++i) {
-      const int u = cta + i * grid;
+    Cursor it(phases, a.n_phases, cta, grid);
+    for (int i = 0; i < cnt; ++i, it.next()) {
+      const int u = it.u;
       o = find_op(ops, a.count, u, o);
       if (o != cur) {
         const Op& op = ops[o];
@@ -594,6 +644,7 @@ struct Variant {
 
 struct Plan {
   std::vector<Op> ops;
+  std::vector<int> phases;  // first unit of every phase, then the unit count
   Args args = {};
   Variant v = {};
   size_t smem = 0;
@@ -629,6 +680,8 @@ int plan_chain(const mli_gemv_op* in, int count, int sm_count, int smem_per_sm, 
   const Variant var = pick_variant(form, flags);
   p->v = var;
   p->ops.assign(count, Op{});
+  p->phases.clear();
+  int max_wait = -1;
   long long units = 0;
   size_t slot = 0, xbytes = 0;
   int part_stride = 0, epoch = -1;
@@ -658,6 +711,10 @@ int plan_chain(const mli_gemv_op* in, int count, int sm_count, int smem_per_sm, 
     op.R = static_cast<uint16_t>(R);
     const int n_stages = (s.d + R - 1) / R;
     op.unit_base = static_cast<int>(units);
+    if (s.wait > max_wait) {  // a new dependency: a new phase
+      p->phases.push_back(op.unit_base);
+      max_wait = s.wait;
+    }
     units += n_stages;
     if (units > (1ll << 30)) return MLI_ERR_UNSUPPORTED;
     op.wait = s.wait;
@@ -678,8 +735,10 @@ int plan_chain(const mli_gemv_op* in, int count, int sm_count, int smem_per_sm, 
     if (xb > xbytes) xbytes = xb;
     if (R * S > part_stride) part_stride = R * S;
   }
+  p->phases.push_back(static_cast<int>(units));
   Args& a = p->args;
   a.count = count;
+  a.n_phases = static_cast<int>(p->phases.size()) - 1;
   a.units = static_cast<int>(units);
   a.slot_bytes = static_cast<uint32_t>(align_up(slot, 128));
   a.part_stride = part_stride;
@@ -693,7 +752,7 @@ int plan_chain(const mli_gemv_op* in, int count, int sm_count, int smem_per_sm, 
     const size_t r = (budget - ring_off) / per_slot;
     return static_cast<int>(r < kMaxRing ? r : kMaxRing);
   };
-  const size_t table = align_up(sizeof(Op) * count, 128);
+  const size_t table = align_up(sizeof(Op) * count + sizeof(int) * p->phases.size(), 128);
   const int ring_global = ring_for(0), ring_shared = ring_for(table);
   // Keep the table in shared memory unless that costs a ring slot the chain
   // needs (three slots keep the stream going across an op switch).
@@ -766,13 +825,18 @@ int mli_chain_create(const mli_gemv_op* ops, int count, mli_chain** chain_out) {
   err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, threads, p.smem);
   if (err != cudaSuccess) return check_cuda(err);
   if (per_sm < p.v.per_sm) return set_status(MLI_ERR_UNSUPPORTED);
+  // device block: op table | phases | counters
   const size_t table = chain::align_up(sizeof(chain::Op) * count, 256);
+  const size_t phases = chain::align_up(sizeof(int) * p.phases.size(), 256);
   const size_t counters = sizeof(unsigned) * (static_cast<size_t>(count) + 1);
   void* mem = nullptr;
-  err = cudaMalloc(&mem, table + counters);
+  err = cudaMalloc(&mem, table + phases + counters);
   if (err != cudaSuccess) return set_status(MLI_ERR_CUDA, err);
-  err = cudaMemcpy(mem, p.ops.data(), sizeof(chain::Op) * count, cudaMemcpyHostToDevice);
-  if (err == cudaSuccess) err = cudaMemset(static_cast<char*>(mem) + table, 0, counters);
+  char* base = static_cast<char*>(mem);
+  err = cudaMemcpy(base, p.ops.data(), sizeof(chain::Op) * count, cudaMemcpyHostToDevice);
+  if (err == cudaSuccess)
+    err = cudaMemcpy(base + table, p.phases.data(), sizeof(int) * p.phases.size(), cudaMemcpyHostToDevice);
+  if (err == cudaSuccess) err = cudaMemset(base + table + phases, 0, counters);
   if (err != cudaSuccess) {
     cudaFree(mem);
     return set_status(MLI_ERR_CUDA, err);
@@ -785,8 +849,9 @@ int mli_chain_create(const mli_gemv_op* ops, int count, mli_chain** chain_out) {
   c->threads = threads;
   c->kernel = kfn;
   c->args = p.args;
-  c->args.ops = static_cast<const chain::Op*>(mem);
-  c->args.done = reinterpret_cast<unsigned*>(static_cast<char*>(mem) + table);
+  c->args.ops = reinterpret_cast<const chain::Op*>(base);
+  c->args.phases = reinterpret_cast<const int*>(base + table);
+  c->args.done = reinterpret_cast<unsigned*>(base + table + phases);
   c->args.finished = c->args.done + count;
   c->dev_mem = mem;
   *chain_out = c;
@@ -831,6 +896,7 @@ int mli_debug_plan_chain(const mli_gemv_op* ops, int count, int sm_count, int sm
   out[3] = static_cast<int>(p.args.slot_bytes);
   out[4] = p.args.units;
   out[5] = p.epochs;
+  out[6] = p.args.n_phases;
   return set_status(MLI_OK);
 }
 

@@ -81,9 +81,9 @@ def _chain(layers=16, form=0, n_x=None):
 
 
 def plan_chain(arr, count=None, sm=148, optin=232448):
-    out = (ctypes.c_int * 6)()
+    out = (ctypes.c_int * 7)()
     rc = _lib.lib().mli_debug_plan_chain(arr, len(arr) if count is None else count, sm, optin, out)
-    return rc, dict(zip(["grid", "smem", "ring", "slot", "units", "epochs"], out))
+    return rc, dict(zip(["grid", "smem", "ring", "slot", "units", "epochs", "phases"], out))
 
 
 @pytest.mark.parametrize("form", [0, 1, 2])
@@ -104,6 +104,8 @@ def test_chain_plan_llama_step(form):
     assert p["units"] == 16 * units
     # q/k/v share the layer input, gate/up the ffn input: 4 activations a layer
     assert p["epochs"] == 16 * 4
+    # q/k/v, o, gate/up, down: 4 dependency phases a layer
+    assert p["phases"] == 16 * 4
 
 
 def test_chain_plan_rejects_bad_chains():
@@ -131,9 +133,17 @@ def test_chain_plan_rejects_bad_chains():
     bad[5].w_s += 4  # misaligned scales
     assert plan_chain(bad)[0] == _lib.MLI_ERR_UNSUPPORTED
     assert plan_chain(arr, count=0)[0] == _lib.MLI_ERR_INVALID_ARG
-    out = (ctypes.c_int * 6)()
+    out = (ctypes.c_int * 7)()
     assert _lib.lib().mli_debug_plan_chain(None, 3, 148, 232448, out) == _lib.MLI_ERR_INVALID_ARG
     # W8A32 rows wider than eight 1024-column slices do not fit the row kernels
     wide = _chain(1)
     wide[6].n = 16384
     assert plan_chain(wide)[0] == _lib.MLI_ERR_UNSUPPORTED
+
+
+def test_chain_plan_independent_ops_form_one_phase():
+    arr = _chain(2)
+    for e in arr:
+        e.wait = 0
+    rc, p = plan_chain(arr)
+    assert rc == _lib.MLI_OK and p["phases"] == 1
