@@ -159,9 +159,10 @@ int mli_quantize_activation_rows(int8_t* xq, float* xs, const float* x, int m,
  * on the CUDA-core path.  Each token's row is within the W8A8 tolerance of
  * mli_gemv_w8a8 on that token.  `workspace` (device, may be NULL) lets the
  * tensor-core path split K over CTAs to fill the GPU: it needs
- * mli_gemm_w8a8_workspace_bytes(m, n, d) bytes, zeroed once before its first
- * use (the kernel leaves it zeroed again); without it K is not split.  Calls
- * that share a workspace must not overlap on the GPU. */
+ * mli_gemm_w8a8_workspace_bytes(m, n, d) bytes, any contents (the splits'
+ * partial sums, summed in split order by a second launch on the same
+ * stream); without it K is not split.  Calls that share a workspace must not
+ * overlap on the GPU. */
 size_t mli_gemm_w8a8_workspace_bytes(int m, int n, int d);
 int mli_gemm_w8a8(float* y, const int8_t* xq, const float* xs,
                   const int8_t* w_q, const float* w_s, int m, int n, int d,
@@ -179,8 +180,8 @@ int mli_gemm_w8a8(float* y, const int8_t* xq, const float* xs,
  * (mli_gemm_w8a8_workspace_bytes) fits 12 MiB -- every shape on a 148-SM
  * B200 -- and returns MLI_ERR_UNSUPPORTED otherwise.  The first call on a
  * device looks up the array's device address (make it before any stream
- * capture).  All calls share the array and every call resets its counters:
- * calls that overlap on the GPU race, so issue them in one stream order. */
+ * capture).  All calls share the array: calls that overlap on the GPU race,
+ * so issue them in one stream order. */
 int mli_gemm_w8a8_noalloc(float* y, const int8_t* xq, const float* xs,
                           const int8_t* w_q, const float* w_s, int m, int n,
                           int d, int group_size, void* stream);

@@ -12,14 +12,18 @@
 //     the activations (BN x 128 B) with 2-D TMA loads (128-byte swizzle, the
 //     canonical K-major UMMA layout) into a 6-stage shared-memory ring;
 //   * warp 1 owns the tensor memory and issues the MMAs from one thread: a
-//     64-column group is two K=32 MMAs into one of two int32 accumulators
-//     (the second MMA accumulates onto the first), committed to an mbarrier;
-//   * warps 2-9 are the epilogue: each reads its 32 accumulator rows over half
-//     of the BN token columns (tcgen05.ld), converts the exact int32 group dot
-//     and adds ws[r][g] * I into fp32 registers, then frees the accumulator.
-// Tiles of K are split over CTAs so a layer fills the GPU; the last CTA of a
-// tile sums the splits' partials in split order (deterministic) from the
-// caller's workspace, scales by xs[t] and writes Y.
+//     64-column group is two K=32 MMAs accumulating into one of up to eight
+//     int32 accumulators, committed to an mbarrier;
+//   * warps 2.. are the epilogue (4 lane quarters x up to 4 token-column
+//     slices): each reads its 32 accumulator rows over its slice of the BN
+//     token columns (tcgen05.ld), recovers the exact int32 group dot
+//     as a float (the accumulators start at a bias that makes the int32 result
+//     the bits of 1.5 * 2^23 + I), adds ws[r][g] * I into fp32 registers, and
+//     refills the accumulator with the bias for its next use.
+// Tiles of K are split over CTAs so a layer fills the GPU; each split writes
+// its partial into the caller's workspace and a small kernel launched right
+// after sums the splits in split order (deterministic) over the whole GPU,
+// scales by xs[t] and writes Y.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -35,8 +39,16 @@ namespace tc {
 constexpr int kBM = 128;             // weight rows per tile (UMMA M)
 constexpr int kChunk = 128;          // K bytes per stage (one 128-byte swizzle atom)
 constexpr int kStages = 6;
-constexpr int kThreads = 320;        // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
-constexpr int kEpiWarps = 8;
+// Warp 0 TMA, warp 1 MMA, warps 2.. epilogue: 4 lane quarters x kSlices token
+// column slices (kCols columns each).  Two slices (8 epilogue warps): a
+// measured tie with four, at more registers per thread and no spills.
+template <int kBN>
+struct Shape {
+  static constexpr int kSlices = 2;
+  static constexpr int kEpiWarps = 4 * kSlices;
+  static constexpr int kThreads = (kEpiWarps + 2) * 32;
+  static constexpr int kCols = kBN / kSlices;
+};
 constexpr int kMaxAccBufs = 8;
 
 // Accumulator buffers per tile width: as many as tensor memory holds (512
@@ -48,8 +60,7 @@ struct Args {
   float* y;
   const float* xs;
   const float* ws;
-  float* partial;        // [splits][m][d] fp32 (splits > 1)
-  unsigned* counters;    // [tiles] zero on entry and on exit (splits > 1)
+  float* partial;        // [splits][m][d] fp32 (splits > 1): summed by splitk_reduce_kernel
   int m, n, d, G;
   int bn;                // tokens per tile (multiple of 16, <= 128)
   int tiles_m, tiles_n, splits, chunks;
@@ -131,6 +142,36 @@ __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// Accumulator bias: int32 accumulation onto the bits of 1.5 * 2^23 leaves the
+// bits of the float 1.5 * 2^23 + I for any |I| < 2^22 (a group dot is at most
+// 64 * 128 * 128 = 2^20 in magnitude), so one subtraction recovers (float)I
+// exactly -- no int->float conversion instruction in the epilogue.
+constexpr uint32_t kAccBias = 0x4B400000u;
+constexpr float kAccBiasF = 12582912.0f;  // 1.5 * 2^23
+
+// Fills this warp's 32 lanes x (8 * kN) columns at taddr with the bias.
+template <int kN>
+__device__ __forceinline__ void tmem_fill_bias(uint32_t taddr) {
+  const uint32_t b = kAccBias;
+#pragma unroll
+  for (int q = 0; q < kN; ++q)
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(
+                     taddr + 8 * q),
+                 "r"(b), "r"(b), "r"(b), "r"(b), "r"(b), "r"(b), "r"(b), "r"(b)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// 4-byte global -> shared asynchronous copy (no register round trip).
+__device__ __forceinline__ void cp_async4(void* dst_smem, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst_smem)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+
 // ---------------------------------------------------------------------------
 // Shared memory: ring of (A 16 KB | B bn*128 B) stages, 1024-byte aligned,
 // then the barriers.
@@ -144,11 +185,21 @@ struct Smem {
   uint64_t* acc_empty;
   uint32_t* tmem_base;
   int* flag;
+  float* ws;             // [kBM][kWsStride] group scales of the current window
+  float* xs;             // [bn] activation scales of the tile's tokens
 };
+
+// The epilogue stages the tile's group scales ws[row][g] for a window of up to
+// kWsWin groups in shared memory (row stride kWsStride floats, odd, so the
+// 32 rows a warp reads at once fall in 32 banks): one burst of coalesced
+// loads instead of a dependent global load per group.
+constexpr int kWsWin = 48;
+constexpr int kWsStride = kWsWin + 1;
+constexpr uint32_t kWsBytes = kBM * kWsStride * 4u;
 
 __host__ __device__ constexpr uint32_t stage_bytes(int bn) { return 16384u + static_cast<uint32_t>(bn) * 128u; }
 __host__ __device__ constexpr uint32_t smem_bytes(int bn) {
-  return 1024u /* alignment slack */ + kStages * stage_bytes(bn) + 512u;
+  return 1024u /* alignment slack */ + kStages * stage_bytes(bn) + 512u + kWsBytes + 512u /* xs */;
 }
 
 __device__ __forceinline__ Smem carve(unsigned char* raw, int bn) {
@@ -164,17 +215,20 @@ __device__ __forceinline__ Smem carve(unsigned char* raw, int bn) {
   s.acc_empty = bars + 2 * kStages + kMaxAccBufs;
   s.tmem_base = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 2 * kMaxAccBufs);
   s.flag = reinterpret_cast<int*>(s.tmem_base + 1);
+  s.ws = reinterpret_cast<float*>(base + kStages * stage_bytes(bn) + 512u);
+  s.xs = s.ws + kBM * kWsStride;
   return s;
 }
 __device__ __forceinline__ unsigned char* stage_a(const Smem& s, int i) { return s.ring + i * s.stage; }
 __device__ __forceinline__ unsigned char* stage_b(const Smem& s, int i) { return s.ring + i * s.stage + 16384; }
 
+template <int kEpiWarps>
 __device__ __forceinline__ void epi_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
 }
 
 template <int kBN>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
     gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap map_w,
                         const __grid_constant__ CUtensorMap map_x, const Args a) {
   extern __shared__ unsigned char smem_raw[];
@@ -193,6 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nchunks = c_end - c_begin;
   const int ngroups = 2 * nchunks;
   constexpr int kAccBufs = acc_bufs(kBN);
+  constexpr int kEpiWarps = Shape<kBN>::kEpiWarps;
   constexpr uint32_t kTmemCols = kAccBufs * kBN;  // 128, 256 or 512: a power of two
 
   if (threadIdx.x == 0) {
@@ -262,8 +317,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t b_base = smem_u32(stage_b(sm, s));
         for (int g = 0; g < 2; ++g, ++gi) {
           const int buf = gi % kAccBufs;
-          if (gi >= kAccBufs &&
-              !mbar_wait_bounded(&sm.acc_empty[buf], ((gi / kAccBufs) - 1) & 1, kWaitLimitNs)) {
+          // use u of a buffer waits for phase u: the epilogue's bias fill
+          // (phase 0) or its read of use u - 1
+          if (!mbar_wait_bounded(&sm.acc_empty[buf], (gi / kAccBufs) & 1, kWaitLimitNs)) {
             ok = false;
             break;
           }
@@ -272,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < 2; ++kk) {
             const uint32_t koff = static_cast<uint32_t>((2 * g + kk) * 32);
-            mma_i8(d, sw128_desc(a_base + koff), sw128_desc(b_base + koff), idesc, kk > 0);
+            mma_i8(d, sw128_desc(a_base + koff), sw128_desc(b_base + koff), idesc, true);
           }
           mma_commit(&sm.acc_full[buf]);
         }
@@ -285,49 +341,79 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------- epilogue (warps 2..9) ----------------
-    griddep_wait();  // xs and the outputs belong to the stream order
     const int quad = warp & 3;                 // TMEM lanes 32*quad .. +31
-    const int half = (warp - 2) >> 2;          // token columns [half*kBN/2, +kBN/2)
-    constexpr int kCols = kBN / 2;
+    const int half = (warp - 2) >> 2;          // token column slice [half*kCols, +kCols)
+    constexpr int kCols = Shape<kBN>::kCols;
     const int row = row0 + 32 * quad + lane;
     const bool row_ok = row < a.d;
     float acc[kCols];
 #pragma unroll
     for (int j = 0; j < kCols; ++j) acc[j] = 0.f;
-    const float* ws_row = a.ws + static_cast<size_t>(row_ok ? row : 0) * a.G;
+    const int et = static_cast<int>(threadIdx.x) - 64;  // epilogue thread 0..255
+    // every accumulator buffer starts at the bias
+    const uint32_t tlane = tmem + (static_cast<uint32_t>(32 * quad) << 16) + static_cast<uint32_t>(half * kCols);
+#pragma unroll
+    for (int b = 0; b < kAccBufs; ++b) tmem_fill_bias<kCols / 8>(tlane + static_cast<uint32_t>(b * kBN));
+    tmem_wait_st();
+    tmem_fence_before();
+    __syncwarp();
+    if (lane == 0)
+      for (int b = 0; b < kAccBufs; ++b) mbar_arrive(&sm.acc_empty[b]);
+    griddep_wait();  // xs and the outputs belong to the stream order
     bool ok = true;
     for (int gi = 0; gi < ngroups; ++gi) {
       const int buf = gi % kAccBufs;
-      const int g = 2 * c_begin + gi;
-      const float wsc = row_ok ? __ldg(ws_row + g) : 0.f;
-      if (!mbar_wait_bounded(&sm.acc_full[buf], (gi / kAccBufs) & 1, kWaitLimitNs)) {
-        ok = false;
-        break;
+      if (gi % kWsWin == 0) {
+        // stage the scales of groups gi .. gi + wn - 1 of the tile's rows:
+        // two threads per row, every copy in flight at once
+        const int wn = ngroups - gi < kWsWin ? ngroups - gi : kWsWin;
+        epi_sync<kEpiWarps>();  // every epilogue thread is done with the previous window
+        constexpr int kTpr = kEpiWarps * 32 / kBM;  // threads per row
+        const int rl = et / kTpr, rr = row0 + rl;
+        float* dst = sm.ws + rl * kWsStride;
+        if (rr < a.d) {
+          const float* src = a.ws + static_cast<size_t>(rr) * a.G + 2 * c_begin + gi;
+          for (int g = et % kTpr; g < wn; g += kTpr) cp_async4(dst + g, src + g);
+        } else {
+          for (int g = et % kTpr; g < wn; g += kTpr) dst[g] = 0.f;
+        }
+        if (gi == 0 && et < kBN) sm.xs[et] = tok0 + et < a.m ? __ldg(a.xs + tok0 + et) : 0.f;
+        cp_async_wait_all();
+        epi_sync<kEpiWarps>();
       }
+      const float wsc = sm.ws[(32 * quad + lane) * kWsStride + gi % kWsWin];
+      // After a timeout the warp keeps walking the groups without waiting, so
+      // that every epilogue warp meets the same window barriers.
+      if (ok && !mbar_wait_bounded(&sm.acc_full[buf], (gi / kAccBufs) & 1, kWaitLimitNs)) ok = false;
+      if (!ok) continue;
       tmem_fence_after();
       const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * quad) << 16) +
                              static_cast<uint32_t>(buf * kBN + half * kCols);
       if constexpr (kCols >= 32) {
-        uint32_t r[kCols / 32][32];
+        // 32 columns at a time: fewer live registers next to acc[kCols]
 #pragma unroll
-        for (int q = 0; q < kCols / 32; ++q) tmem_ld32(taddr + 32 * q, r[q]);
-        tmem_wait_ld();
-#pragma unroll
-        for (int q = 0; q < kCols / 32; ++q)
+        for (int q = 0; q < kCols / 32; ++q) {
+          uint32_t r[32];
+          tmem_ld32(taddr + 32 * q, r);
+          tmem_wait_ld();
 #pragma unroll
           for (int j = 0; j < 32; ++j)
-            acc[32 * q + j] = fmaf(static_cast<float>(static_cast<int>(r[q][j])), wsc, acc[32 * q + j]);
+            acc[32 * q + j] = fmaf(__uint_as_float(r[j]) - kAccBiasF, wsc, acc[32 * q + j]);
+        }
+        tmem_fill_bias<kCols / 8>(taddr);  // ready for the buffer's next use
       } else {
         uint32_t r[kCols / 8][8];
 #pragma unroll
         for (int q = 0; q < kCols / 8; ++q) tmem_ld8(taddr + 8 * q, r[q]);
         tmem_wait_ld();
+        tmem_fill_bias<kCols / 8>(taddr);
 #pragma unroll
         for (int q = 0; q < kCols / 8; ++q)
 #pragma unroll
           for (int j = 0; j < 8; ++j)
-            acc[8 * q + j] = fmaf(static_cast<float>(static_cast<int>(r[q][j])), wsc, acc[8 * q + j]);
+            acc[8 * q + j] = fmaf(__uint_as_float(r[q][j]) - kAccBiasF, wsc, acc[8 * q + j]);
       }
+      tmem_wait_st();
       tmem_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.acc_empty[buf]);
@@ -336,7 +422,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       record_device_error(kDevMmaTimeout);
       *sm.flag = 1;
     }
-    epi_sync();
+    epi_sync<kEpiWarps>();
     const bool good = *sm.flag == 0;
     const int t_base = tok0 + half * kCols;
     if (good && a.splits == 1) {
@@ -344,57 +430,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int j = 0; j < kCols; ++j) {
           const int t = t_base + j;
-          if (t < a.m) a.y[static_cast<size_t>(t) * a.d + row] = acc[j] * a.xs[t];
+          if (t < a.m) a.y[static_cast<size_t>(t) * a.d + row] = acc[j] * sm.xs[half * kCols + j];
         }
       }
-    } else if (good) {
-      // write this split's partial, then the last split of the tile reduces
+    } else if (good && row_ok) {
+      // this split's partial; splitk_reduce_kernel sums the splits in order
       float* my_part = a.partial + static_cast<size_t>(split) * a.m * a.d;
-      if (row_ok) {
 #pragma unroll
-        for (int j = 0; j < kCols; ++j) {
-          const int t = t_base + j;
-          if (t < a.m) my_part[static_cast<size_t>(t) * a.d + row] = acc[j];
-        }
-      }
-      __threadfence();
-      epi_sync();
-      if (threadIdx.x == 64) {
-        const unsigned prev = atomicAdd(a.counters + tile, 1u);
-        *sm.flag = (prev == static_cast<unsigned>(a.splits - 1)) ? 2 : 0;
-        if (prev == static_cast<unsigned>(a.splits - 1)) a.counters[tile] = 0;  // self-reset
-        __threadfence();
-      }
-      epi_sync();
-      if (*sm.flag == 2 && row_ok) {
-        // Sum the splits in split order.  The split loop is outermost so the
-        // loads of all columns of one split are independent and in flight
-        // together.
-        __threadfence();
-        float v[kCols];
-#pragma unroll
-        for (int j = 0; j < kCols; ++j) v[j] = 0.f;
-        for (int s2 = 0; s2 < a.splits; ++s2) {
-          if (s2 == split) {
-#pragma unroll
-            for (int j = 0; j < kCols; ++j) v[j] += acc[j];
-          } else {
-            const float* src = a.partial + static_cast<size_t>(s2) * a.m * a.d + row;
-            float pv[kCols];
-#pragma unroll
-            for (int j = 0; j < kCols; ++j) {
-              const int t = t_base + j < a.m ? t_base + j : a.m - 1;
-              pv[j] = __ldcg(src + static_cast<size_t>(t) * a.d);
-            }
-#pragma unroll
-            for (int j = 0; j < kCols; ++j) v[j] += pv[j];
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < kCols; ++j) {
-          const int t = t_base + j;
-          if (t < a.m) a.y[static_cast<size_t>(t) * a.d + row] = v[j] * a.xs[t];
-        }
+      for (int j = 0; j < kCols; ++j) {
+        const int t = t_base + j;
+        if (t < a.m) my_part[static_cast<size_t>(t) * a.d + row] = acc[j];
       }
     }
   }
@@ -406,6 +451,46 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
                  : "memory");
+  }
+}
+
+// Split-K: y[t][r] = xs[t] * sum_s partial[s][t][r], the splits summed in split
+// order (deterministic), over the whole GPU at once.  Launched right after
+// the GEMM (programmatic dependent launch): the partials are read only after
+// griddepcontrol.wait.
+constexpr int kReduceThreads = 256;
+constexpr int kReduceElems = 4;  // consecutive outputs per thread
+
+__global__ void __launch_bounds__(kReduceThreads)
+    splitk_reduce_kernel(float* y, const float* partial, const float* xs, int splits, int m, int d) {
+  griddep_wait();
+  const size_t md = static_cast<size_t>(m) * d;
+  const size_t i0 = (static_cast<size_t>(blockIdx.x) * kReduceThreads + threadIdx.x) * kReduceElems;
+  if (i0 >= md) return;
+  float v[kReduceElems];
+#pragma unroll
+  for (int e = 0; e < kReduceElems; ++e) v[e] = 0.f;
+  int s = 0;
+  for (; s + 4 <= splits; s += 4) {  // four splits' loads in flight
+    float p[4][kReduceElems];
+#pragma unroll
+    for (int b = 0; b < 4; ++b)
+#pragma unroll
+      for (int e = 0; e < kReduceElems; ++e)
+        p[b][e] = i0 + e < md ? __ldcg(partial + static_cast<size_t>(s + b) * md + i0 + e) : 0.f;
+#pragma unroll
+    for (int b = 0; b < 4; ++b)
+#pragma unroll
+      for (int e = 0; e < kReduceElems; ++e) v[e] += p[b][e];
+  }
+  for (; s < splits; ++s)
+#pragma unroll
+    for (int e = 0; e < kReduceElems; ++e)
+      v[e] += i0 + e < md ? __ldcg(partial + static_cast<size_t>(s) * md + i0 + e) : 0.f;
+#pragma unroll
+  for (int e = 0; e < kReduceElems; ++e) {
+    const size_t i = i0 + e;
+    if (i < md) y[i] = v[e] * __ldg(xs + i / d);
   }
 }
 
@@ -465,7 +550,7 @@ cudaError_t launch_bn(const CUtensorMap& mw, const CUtensorMap& mx, const Args& 
   const uint32_t smem = smem_bytes(kBN);
   cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(gemm_w8a8_tc_kernel<kBN>), smem);
   if (e != cudaSuccess) return e;
-  return launch(gemm_w8a8_tc_kernel<kBN>, dim3(grid), dim3(kThreads), smem, stream, true, mw, mx, a);
+  return launch(gemm_w8a8_tc_kernel<kBN>, dim3(grid), dim3(Shape<kBN>::kThreads), smem, stream, true, mw, mx, a);
 }
 
 }  // namespace tc
@@ -473,8 +558,7 @@ cudaError_t launch_bn(const CUtensorMap& mw, const CUtensorMap& mx, const Args& 
 size_t gemm_tc_workspace_bytes(int m, int n, int d, int sm_count) {
   const tc::Plan p = tc::plan(m, n, d, sm_count, true);
   if (p.splits <= 1) return 256;
-  return 256 + static_cast<size_t>(p.tiles_m) * p.tiles_n * sizeof(unsigned) +
-         static_cast<size_t>(p.splits) * m * d * sizeof(float) + 256;
+  return 256 + static_cast<size_t>(p.splits) * m * d * sizeof(float);
 }
 
 // Tensor-core path: m >= 16, n % 128 == 0, group 64, 16-byte aligned
@@ -505,12 +589,7 @@ int gemm_w8a8_tc(float* y, const int8_t* xq, const float* xs, const int8_t* w_q,
   a.tiles_n = p.tiles_n;
   a.splits = p.splits;
   a.chunks = p.chunks;
-  if (p.splits > 1) {
-    unsigned char* ws = static_cast<unsigned char*>(workspace);
-    a.counters = reinterpret_cast<unsigned*>(ws);
-    const size_t cbytes = (static_cast<size_t>(p.tiles_m) * p.tiles_n * sizeof(unsigned) + 255) & ~size_t(255);
-    a.partial = reinterpret_cast<float*>(ws + cbytes);
-  }
+  if (p.splits > 1) a.partial = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + 256);
   const int grid = p.tiles_m * p.tiles_n * p.splits;
   switch (p.bn) {
     case 16: err = tc::launch_bn<16>(mw, mx, a, grid, stream); break;
@@ -518,7 +597,12 @@ int gemm_w8a8_tc(float* y, const int8_t* xq, const float* xs, const int8_t* w_q,
     case 64: err = tc::launch_bn<64>(mw, mx, a, grid, stream); break;
     default: err = tc::launch_bn<128>(mw, mx, a, grid, stream); break;
   }
-  return check_cuda(err);
+  if (err != cudaSuccess || p.splits == 1) return check_cuda(err);
+  const size_t per_block = static_cast<size_t>(tc::kReduceThreads) * tc::kReduceElems;
+  const size_t md = static_cast<size_t>(m) * d;
+  const unsigned blocks = static_cast<unsigned>((md + per_block - 1) / per_block);
+  return check_cuda(launch(tc::splitk_reduce_kernel, dim3(blocks), dim3(tc::kReduceThreads), 0, stream, true,
+                           y, static_cast<const float*>(a.partial), xs, p.splits, m, d));
 }
 
 }  // namespace mli
@@ -530,12 +614,12 @@ int gemm_w8a8_tc(float* y, const int8_t* xq, const float* xs, const int8_t* w_q,
 // host framework owns every byte of device memory through its own pool, or a
 // serving loop whose policy forbids allocations on the request path.  This
 // entry point gives them the split-K tensor-core path anyway, with its scratch
-// (the per-tile counters and the per-split partial sums) in a fixed array
+// (the per-split partial sums) in a fixed array
 // compiled into the library.  Every GPU that loads the library holds the array
 // until the process exits.  The array is sized for the largest split-K
 // workspace a B200 (148 SMs) can need: split-K never runs more partial tiles
 // than there are SMs, and a partial tile is at most 128 rows x 128 tokens of
-// fp32 (64 KiB), so 148 x 64 KiB plus the counters fits in 12 MiB.
+// fp32 (64 KiB), so 148 x 64 KiB fits in 12 MiB.
 namespace mli {
 namespace {
 
@@ -575,14 +659,8 @@ extern "C" int mli_gemm_w8a8_noalloc(float* y, const int8_t* xq, const float* xs
   if (err != cudaSuccess) return set_status(MLI_ERR_CUDA, err);
   const size_t need = gemm_tc_workspace_bytes(m, n, d, info.sm_count);
   if (need > kNoAllocWorkspaceBytes) return set_status(MLI_ERR_UNSUPPORTED);
-  // The array keeps the previous call's contents: the tile counters must
-  // start at zero, the partial sums are always written before they are read.
-  const tc::Plan p = tc::plan(m, n, d, info.sm_count, true);
-  if (p.splits > 1) {
-    const size_t cbytes = static_cast<size_t>(p.tiles_m) * p.tiles_n * sizeof(unsigned);
-    err = cudaMemsetAsync(g_noalloc_ptr[dev], 0, cbytes, static_cast<cudaStream_t>(stream));
-    if (err != cudaSuccess) return set_status(MLI_ERR_CUDA, err);
-  }
+  // The array keeps the previous call's contents; nothing in it needs to
+  // start at zero (the partial sums are always written before they are read).
   return gemm_w8a8_tc(y, xq, xs, w_q, w_s, m, n, d, g_noalloc_ptr[dev], kNoAllocWorkspaceBytes,
                       static_cast<cudaStream_t>(stream));
 }

@@ -227,7 +227,7 @@ def test_gemm_w8a8_cuda_core_parity(m):
 def test_gemm_w8a8_tensor_core_parity(m, n, d, workspace):
     got, (xq, xs, tw, ts, ws) = _gemm_case(m, n, d, 7 * m + d, workspace)
     if ws is not None:
-        assert int(ws.view(torch.int32)[:64].abs().sum()) == 0  # counters restored
+        ws.fill_(0x7F)  # the workspace may hold anything between calls
         y2 = torch.empty(m * d, dtype=torch.float32, device=dev())
         ops.gemm_w8a8(y2, xq, xs, tw, ts, m, n, d, 64, workspace=ws)
         torch.cuda.synchronize()
