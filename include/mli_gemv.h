@@ -215,9 +215,25 @@ int mli_gemv_rowshard(int form, float* const* peer_logits,
                       int rows, int row_offset, int d_total, int rank, int world,
                       int group_size, void* stream);
 
+/* mli_gemv_rowshard and mli_rowshard_wait_argmax in one launch: the last
+ * CTA of this rank's GEMV waits (bounded by timeout_us) for every rank's rows
+ * of this step, reduces every rank's CTA partials to the argmax, writes it to
+ * *out and advances the step -- one kernel per step instead of two.  own_block
+ * is this rank's peer block (its header holds the counters, the step and the
+ * launch's finished-CTA count); shard_rows is a HOST array of `world` row
+ * counts (every rank's `rows`) summing to d_total.  On expiry *out = -1 and
+ * the device error word is set. */
+int mli_gemv_rowshard_argmax(int form, float* const* peer_logits,
+                             unsigned long long* const* peer_rows, void* own_block,
+                             const float* x, const int8_t* w_q, const float* w_s, int n,
+                             int rows, int row_offset, int d_total, int rank, int world,
+                             int group_size, const int* shard_rows, long long* out,
+                             int timeout_us, void* stream);
+
 /* Bytes of one rank's peer block for a d_total-row layer:
  *   [0, 64)    uint64 row counters, one per source rank
  *   [128, 132) uint32 step counter
+ *   [192, 196) uint32 finished-CTA count of a fused step (zero between steps)
  *   [256, ...) fp32 logits [2][d_total], then (at the next 16-byte boundary)
  *              the CTAs' (max, first index) partials int2 [2][8][512].
  * mli_gemv_rowshard's peer_logits[p] and mli_rowshard_wait_argmax's logits

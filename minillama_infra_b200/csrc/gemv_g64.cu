@@ -97,15 +97,25 @@ struct StreamArgs {
   const unsigned* step;
   float* peer_y[kMaxPeers];
   unsigned long long* peer_rows[kMaxPeers];
+  // Fused argmax (row-sharded, out != nullptr): the last CTA of the launch
+  // waits for every rank's rows of this step, reduces the CTA partials to the
+  // argmax, writes it and advances the step.
+  long long* out;
+  unsigned* step_rw;                   // this rank's step counter
+  unsigned* ctas_done;                 // this rank's finished-CTA count (zero between launches)
+  const unsigned long long* my_rows;   // this rank's per-source row counters
+  unsigned long long timeout_ns;
+  int shard_rows[kMaxPeers];
+  int shard_ctas[kMaxPeers];
 };
 
 // ---------------------------------------------------------------------------
 // The streaming kernel
 // ---------------------------------------------------------------------------
-// Stores one finished output row: locally, or (row-sharded) into every rank's
-// logits buffer over NVLink.
-// Row-sharded launches stage the CTA's rows (a contiguous range) in shared
-// memory and publish them once at the end of the CTA.
+// Stores one finished output row: locally, or (row-sharded) into the CTA's
+// shared staging; row-sharded launches publish a CTA's rows (a contiguous
+// range) to every rank as one coalesced burst at the end of the CTA, which
+// costs less than per-stage remote stores.
 template <bool kPeer>
 __device__ __forceinline__ void store_row(const StreamArgs& a, int row, float v, float* staged,
                                           int cta_row0) {
@@ -114,6 +124,10 @@ __device__ __forceinline__ void store_row(const StreamArgs& a, int row, float v,
   } else {
     staged[row - cta_row0] = v;
   }
+}
+
+__device__ __forceinline__ void fence_acq_rel_sys() {
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
 }
 
 // (max, first index) over v[0..n) by the CTA's 256 threads, scanning each
@@ -310,31 +324,100 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_stream_kernel(const StreamAr
   if constexpr (kPeer) {
     // Publish the CTA's rows to every rank as one coalesced burst, with the
     // rows' (max, first index) in this CTA's partial slot, then raise every
-    // rank's counter for this rank by the rows produced.
+    // rank's counter for this rank by the rows produced.  A CTA that gave up
+    // on a stage publishes nothing (the counters are never raised for rows
+    // that were not produced).
     __syncthreads();
-    if (*sm.broken) return;  // never raise the counters for rows that were not produced
-    const int cta_rows = max(0, min((begin + cnt) * a.R, a.d) - cta_row0);
-    __shared__ float s_best_v;
-    __shared__ int s_best_i;
-    cta_first_max(staged, cta_rows, a.row_offset + cta_row0, sm.red, sm.red_i, &s_best_v, &s_best_i);
-    __syncthreads();
-    const size_t off = static_cast<size_t>(parity) * a.d_total + a.row_offset + cta_row0;
-    for (int p = 0; p < a.world; ++p) {
-      float* dst = a.peer_y[p] + off;
-      for (int i = threadIdx.x; i < cta_rows; i += kConsumerThreads) dst[i] = staged[i];
-      if (threadIdx.x == 0) {
-        int2* slot = rowshard_partials(a.peer_y[p], a.d_total) +
-                     (static_cast<size_t>(parity) * kMaxPeers + a.rank) * kMaxRankCtas + blockIdx.x;
-        *slot = make_int2(__float_as_int(s_best_v), s_best_i);
+    const bool broken = *sm.broken != 0;
+    if (!broken) {
+      const int cta_rows = max(0, min((begin + cnt) * a.R, a.d) - cta_row0);
+      __shared__ float s_best_v;
+      __shared__ int s_best_i;
+      cta_first_max(staged, cta_rows, a.row_offset + cta_row0, sm.red, sm.red_i, &s_best_v, &s_best_i);
+      __syncthreads();
+      const size_t off = static_cast<size_t>(parity) * a.d_total + a.row_offset + cta_row0;
+      for (int p = 0; p < a.world; ++p) {
+        float* dst = a.peer_y[p] + off;
+        for (int i = threadIdx.x; i < cta_rows; i += kConsumerThreads) dst[i] = staged[i];
+        if (threadIdx.x == 0) {
+          int2* slot = rowshard_partials(a.peer_y[p], a.d_total) +
+                       (static_cast<size_t>(parity) * kMaxPeers + a.rank) * kMaxRankCtas + blockIdx.x;
+          *slot = make_int2(__float_as_int(s_best_v), s_best_i);
+        }
+      }
+      // The barrier orders every thread's stores before thread 0's
+      // system-scope release fence, which (being cumulative) publishes them
+      // before the increments.
+      __syncthreads();
+      if (threadIdx.x == 0 && cta_rows > 0) {
+        fence_acq_rel_sys();
+        for (int p = 0; p < a.world; ++p)
+          atomicAdd_system(a.peer_rows[p] + a.rank, static_cast<unsigned long long>(cta_rows));
       }
     }
-    // The barrier orders every thread's stores before thread 0's system-scope
-    // fence, which (being cumulative) publishes them before the increments.
+    if (a.out == nullptr) return;
+    // Fused argmax: the last CTA to finish takes over.
+    __shared__ int s_last;
+    if (threadIdx.x == 0) {
+      __threadfence();
+      s_last = atomicAdd(a.ctas_done, 1u) == gridDim.x - 1;
+    }
     __syncthreads();
-    if (threadIdx.x == 0 && cta_rows > 0) {
-      __threadfence_system();
-      for (int p = 0; p < a.world; ++p)
-        atomicAdd_system(a.peer_rows[p] + a.rank, static_cast<unsigned long long>(cta_rows));
+    if (!s_last) return;
+    __shared__ int s_fail;
+    if (threadIdx.x == 0) {
+      *a.ctas_done = 0;  // every other CTA of this launch is done with it
+      s_fail = 0;
+    }
+    __syncthreads();
+    const unsigned s = *a.step;
+    if (threadIdx.x < a.world) {
+      const unsigned long long target =
+          static_cast<unsigned long long>(s + 1) * static_cast<unsigned long long>(a.shard_rows[threadIdx.x]);
+      const uint64_t t0 = global_timer_ns();
+      while (ld_acquire_sys(a.my_rows + threadIdx.x) < target) {
+        if (global_timer_ns() - t0 > a.timeout_ns) {
+          atomicExch(&s_fail, 1);
+          break;
+        }
+      }
+    }
+    __syncthreads();
+    if (s_fail) {
+      if (threadIdx.x == 0) {
+        record_device_error(kDevPeerTimeout);
+        *a.out = -1;
+      }
+      return;
+    }
+    // Every rank's CTAs left their rows' (max, first index) in this step's
+    // half of this rank's partials: reduce those, not the whole logits.
+    const float* own = a.peer_y[a.rank];
+    const int2* parts = rowshard_partials(own, a.d_total) + static_cast<size_t>(parity) * kMaxPeers * kMaxRankCtas;
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int r = 0; r < a.world; ++r)
+      for (int c = threadIdx.x; c < a.shard_ctas[r]; c += kConsumerThreads) {
+        const int2 pr = __ldcg(parts + r * kMaxRankCtas + c);
+        argmax_combine(bv, bi, __int_as_float(pr.x), pr.y);
+      }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      argmax_combine(bv, bi, ov, oi);
+    }
+    if ((threadIdx.x & 31) == 0) {
+      sm.red[threadIdx.x >> 5] = bv;
+      sm.red_i[threadIdx.x >> 5] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      for (int w = 1; w < kConsumerWarps; ++w) argmax_combine(bv, bi, sm.red[w], sm.red_i[w]);
+      const float x0 = __ldcg(own + static_cast<size_t>(parity) * a.d_total);
+      if (bi == 0x7fffffff || x0 != x0) bi = 0;  // the reference's scan starts from x[0]
+      *a.out = bi;
+      *a.step_rw = s + 1;
     }
   }
 }
@@ -607,6 +690,46 @@ int mli_gemv_rowshard(int form, float* const* peer_logits, unsigned long long* c
   }
   return launch_stream(form == 0 ? Form::kW8A32 : Form::kW8A8Fused, a, n, rows,
                        static_cast<cudaStream_t>(stream));
+}
+
+int mli_gemv_rowshard_argmax(int form, float* const* peer_logits,
+                             unsigned long long* const* peer_rows, void* own_block,
+                             const float* x, const int8_t* w_q, const float* w_s, int n,
+                             int rows, int row_offset, int d_total, int rank, int world,
+                             int group_size, const int* shard_rows, long long* out,
+                             int timeout_us, void* stream) {
+  if (!peer_logits || !peer_rows || !own_block || !x || !shard_rows || !out || world <= 0 ||
+      world > kMaxPeers || rank < 0 || rank >= world || rows <= 0 || row_offset < 0 ||
+      row_offset + rows > d_total || n <= 0 || group_size <= 0 || timeout_us <= 0 ||
+      (form != 0 && form != 2) || !w_q || !w_s)
+    return set_status(MLI_ERR_INVALID_ARG);
+  for (int p = 0; p < world; ++p)
+    if (!peer_logits[p] || !peer_rows[p]) return set_status(MLI_ERR_INVALID_ARG);
+  if (!fast_path_ok(n, group_size) || !aligned(x, 16) || !aligned(w_q, 16) || !aligned(w_s, 16))
+    return set_status(MLI_ERR_UNSUPPORTED);
+  StreamArgs a = {};
+  a.x = x; a.w = w_q; a.s = w_s;
+  a.world = world; a.rank = rank; a.row_offset = row_offset; a.d_total = d_total;
+  unsigned char* blk = static_cast<unsigned char*>(own_block);
+  a.step = reinterpret_cast<const unsigned*>(blk + 128);
+  a.step_rw = reinterpret_cast<unsigned*>(blk + 128);
+  a.ctas_done = reinterpret_cast<unsigned*>(blk + 192);
+  a.my_rows = reinterpret_cast<const unsigned long long*>(blk);
+  a.out = out;
+  a.timeout_ns = static_cast<unsigned long long>(timeout_us) * 1000ull;
+  long long total = 0;
+  const Form f = form == 0 ? Form::kW8A32 : Form::kW8A8Fused;
+  for (int p = 0; p < world; ++p) {
+    a.peer_y[p] = peer_logits[p];
+    a.peer_rows[p] = peer_rows[p];
+    if (shard_rows[p] <= 0) return set_status(MLI_ERR_INVALID_ARG);
+    a.shard_rows[p] = shard_rows[p];
+    a.shard_ctas[p] = rowshard_grid(form, n, shard_rows[p]);
+    if (a.shard_ctas[p] <= 0 || a.shard_ctas[p] > kMaxRankCtas) return set_status(MLI_ERR_UNSUPPORTED);
+    total += shard_rows[p];
+  }
+  if (total != d_total || shard_rows[rank] != rows) return set_status(MLI_ERR_INVALID_ARG);
+  return launch_stream(f, a, n, rows, static_cast<cudaStream_t>(stream));
 }
 
 int mli_debug_plan_gemv(int form, int n, int d, int sm_count, int smem_per_sm,

@@ -233,6 +233,23 @@ __device__ __forceinline__ bool named_sync_or(bool pred) {
   return r != 0;
 }
 
+// First-maximum rule of the reference's host scan (`if (logits[i] > max_val)`
+// starting from max_val = logits[0]): a larger value wins, equal values keep
+// the smaller index, -0.0 and +0.0 are equal, a NaN never wins (every
+// comparison with it is false) -- and a NaN in x[0] makes the answer 0.
+__device__ __forceinline__ void argmax_combine(float& bv, int& bi, float v, int i) {
+  if (v > bv || (v == bv && i < bi)) {
+    bv = v;
+    bi = i;
+  }
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);

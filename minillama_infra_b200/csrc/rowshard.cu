@@ -24,21 +24,11 @@ constexpr int kWaitThreads = 256;
 // Grid the row-sharded streaming GEMV uses for `rows` rows (gemv_g64.cu).
 int rowshard_grid(int form, int n, int rows);
 
-// First-maximum rule of the reference's host scan (`if (logits[i] > max_val)`
-// starting from max_val = logits[0]): a larger value wins, equal values keep
-// the smaller index, -0.0 and +0.0 are equal, a NaN never wins (every
-// comparison with it is false) -- and a NaN in x[0] makes the answer 0.
-__device__ __forceinline__ void argmax_combine(float& bv, int& bi, float v, int i) {
-  if (v > bv || (v == bv && i < bi)) {
-    bv = v;
-    bi = i;
-  }
-}
-
 // Block-wide argmax of x[0..n) (every thread of a 1024-thread CTA calls it);
 // returns the index on every thread.  Each thread scans its elements in
 // increasing index order with a strict `>`, so its candidate is its first
-// maximum; candidates then combine with the rule above.  Loads bypass L1:
+// maximum; candidates then combine with argmax_combine (the reference's
+// first-maximum rule).  Loads bypass L1:
 // the values may have just been written by other GPUs.
 __device__ __forceinline__ int block_argmax(const float* x, int n) {
   __shared__ float red_v[kArgmaxThreads / 32];
@@ -114,11 +104,6 @@ struct WaitArgs {
   int shard_ctas[kMaxPeers];        // CTAs (partial slots) each rank writes per step
 };
 
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
 
 __global__ void __launch_bounds__(kWaitThreads) rowshard_wait_argmax_kernel(const WaitArgs a) {
   __shared__ unsigned s_step;

@@ -101,13 +101,15 @@ class PeerShardedLinear:
     include/mli_gemv.h, mli_rowshard_block_bytes):
         [0, 64)    uint64 row counters, one per source rank (raised over NVLink)
         [128, 132) uint32 step counter (local)
+        [192, 196) uint32 finished-CTA count of a fused step (local)
         [256, ...) fp32 logits [2][d] (the half is the step's parity), then the
                    CTAs' (max, first index) partials
-    and opens every other rank's block.  A step is two launches on the current
-    stream: mli_gemv_rowshard (this rank's rows, stored into every rank's logits
-    with the CTAs' partials, then the counters raised) and
-    mli_rowshard_wait_argmax (bounded wait for all ranks' rows, argmax from the
-    partials, step + 1).  The handles travel through torch.distributed (any
+    and opens every other rank's block.  A step is one launch on the current
+    stream, mli_gemv_rowshard_argmax: this rank's rows stored into every rank's
+    logits with the CTAs' partials, the counters raised, then the launch's last
+    CTA waits (bounded) for all ranks' rows, takes the argmax from the partials
+    and advances the step.  (forward(fused=False) runs the same as two launches,
+    mli_gemv_rowshard + mli_rowshard_wait_argmax.)  The handles travel through torch.distributed (any
     backend); no collective runs on the data path.  world == 1 needs no
     process group (the single GPU then gets the fused GEMV + argmax).
     """
@@ -165,20 +167,29 @@ class PeerShardedLinear:
         """fp32 view of this rank's logits half (0 or 1) -- a device pointer wrapper."""
         return self.base + self.HEADER + half * self.d * 4
 
-    def forward(self, x, stream=None):
+    def forward(self, x, stream=None, fused: bool = True):
+        """One step: this rank's rows to every rank, then the argmax into
+        self.out -- one launch (fused) or the GEMV and the wait kernel."""
         import torch
 
         from ._lib import check
 
         st = torch.cuda.current_stream().cuda_stream if stream is None else stream
-        check(self.lib.mli_gemv_rowshard(self.form_code, self._peer_logits, self._peer_rows,
-                                         self.base + 128, x.data_ptr(), self.w_q.data_ptr(),
-                                         self.w_s.data_ptr(), self.n, self.shard.rows, self.shard.r0,
-                                         self.d, self.rank, self.world, 64, st), "mli_gemv_rowshard")
-        check(self.lib.mli_rowshard_wait_argmax(self.form_code, self.n, self.base + self.HEADER, self.base,
-                                                self.base + 128, self._shard_rows, self.world, self.d,
-                                                self.out.data_ptr(), self.timeout_us, st),
-              "mli_rowshard_wait_argmax")
+        if fused:
+            check(self.lib.mli_gemv_rowshard_argmax(
+                self.form_code, self._peer_logits, self._peer_rows, self.base, x.data_ptr(),
+                self.w_q.data_ptr(), self.w_s.data_ptr(), self.n, self.shard.rows, self.shard.r0, self.d,
+                self.rank, self.world, 64, self._shard_rows, self.out.data_ptr(), self.timeout_us, st),
+                "mli_gemv_rowshard_argmax")
+        else:
+            check(self.lib.mli_gemv_rowshard(self.form_code, self._peer_logits, self._peer_rows,
+                                             self.base + 128, x.data_ptr(), self.w_q.data_ptr(),
+                                             self.w_s.data_ptr(), self.n, self.shard.rows, self.shard.r0,
+                                             self.d, self.rank, self.world, 64, st), "mli_gemv_rowshard")
+            check(self.lib.mli_rowshard_wait_argmax(self.form_code, self.n, self.base + self.HEADER, self.base,
+                                                    self.base + 128, self._shard_rows, self.world, self.d,
+                                                    self.out.data_ptr(), self.timeout_us, st),
+                  "mli_rowshard_wait_argmax")
         self.steps += 1
         return self.out
 

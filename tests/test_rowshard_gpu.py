@@ -158,3 +158,57 @@ def test_rowshard_wait_gives_up_when_rows_never_arrive():
         assert argmax_dev(torch.arange(10, dtype=torch.float32, device=dev())) == 9
     finally:
         b.free()
+
+
+@pytest.mark.parametrize("form", ["w8a32", "w8a8"])
+def test_rowshard_fused_argmax_single_rank(form):
+    """mli_gemv_rowshard_argmax (one launch per step): the same logits and
+    argmax as the two-launch step, over both halves and back."""
+    d, n = 5003, 2048
+    w_q, w_s = synth.weights_gpu(d, n, seed=5, device=dev())
+    x = synth.activation_gpu(n, 6, dev(), outliers=(form == "w8a8"))
+    ref = torch.empty(d, dtype=torch.float32, device=dev())
+    if form == "w8a32":
+        ops.matmul_int8(ref, x, w_q, w_s, n, d, 64)
+    else:
+        ops.matmul_dp4a_fused(ref, x, w_q, w_s, n, d, 64)
+    b = Block(d)
+    P = ctypes.c_void_p
+    out = torch.full((), -7, dtype=torch.int64, device=dev())
+    code = 0 if form == "w8a32" else 2
+    try:
+        for step in range(3):
+            check(lib().mli_gemv_rowshard_argmax(code, (P * 1)(b.logits(0)), (P * 1)(b.base), b.base, x.data_ptr(),
+                                                 w_q.data_ptr(), w_s.data_ptr(), n, d, 0, d, 0, 1, 64,
+                                                 (ctypes.c_int * 1)(d), out.data_ptr(), 1_000_000, None), "fused")
+            torch.cuda.synchronize()
+            got = b.read_logits(step & 1)
+            assert np.array_equal(got.view(np.uint32), ref.cpu().numpy().view(np.uint32))
+            assert int(out.item()) == int(torch.argmax(ref).item())
+        assert ops.device_error() == 0
+    finally:
+        b.free()
+
+
+def test_rowshard_fused_gives_up_when_a_rank_never_arrives():
+    """A declared second rank that never runs: the last CTA's bounded wait
+    expires, *out = -1, device error 3, and the context stays usable."""
+    d, n = 1024, 256
+    w_q, w_s = synth.weights_gpu(512, n, seed=7, device=dev())
+    x = synth.activation_gpu(n, 8, dev())
+    b0, b1 = Block(d), Block(d)  # rank 1's block stands in for a peer that never writes
+    P = ctypes.c_void_p
+    out = torch.zeros((), dtype=torch.int64, device=dev())
+    try:
+        check(lib().mli_gemv_rowshard_argmax(0, (P * 2)(b0.logits(0), b1.logits(0)), (P * 2)(b0.base, b1.base),
+                                             b0.base, x.data_ptr(), w_q.data_ptr(), w_s.data_ptr(), n, 512, 0, d,
+                                             0, 2, 64, (ctypes.c_int * 2)(512, 512), out.data_ptr(), 100_000,
+                                             None), "fused")
+        torch.cuda.synchronize()
+        assert int(out.item()) == -1
+        assert ops.device_error() == 3
+        assert ops.device_error() == 0
+        assert argmax_dev(torch.arange(10, dtype=torch.float32, device=dev())) == 9
+    finally:
+        b0.free()
+        b1.free()
