@@ -98,6 +98,18 @@ int mli_gemv_w8a8_fused(float* y, int8_t* xq_out, float* xs_out,
 
 /* ---- chained decode step (no reference counterpart) -------------------- */
 
+/* Row epilogues of a chained GEMV.  ADD adds each row into y (the residual add
+ * after the reference's down projection, src/model_cuda_v2_shared.cu:215-218,
+ * :414).  SWIGLU pairs the op with the NEXT op of the chain (gate = this op,
+ * up = the next: same n, d, activation and wait, epilogue STORE, its y unused)
+ * and stores (g * (1 / (1 + expf(-g)))) * u into this op's y -- the
+ * reference's silu_mul (:220-227, :410) fused in; both ops count as complete
+ * together.  A SwiGLU pair streams the gate's and the up's rows of a stage
+ * together, so one launch reads both matrices once. */
+#define MLI_EPI_STORE 0
+#define MLI_EPI_ADD 1
+#define MLI_EPI_SWIGLU 2
+
 /* One GEMV of a chain: the arguments of mli_gemv_w8a32 (form 0),
  * mli_gemv_w8a8 (form 1) or mli_gemv_w8a8_fused without xq_out/xs_out
  * (form 2), plus `wait`: ops [0, wait) of the chain are complete before this
@@ -111,7 +123,7 @@ typedef struct mli_gemv_op {
   int d;          /* out-features */
   int group_size; /* 64 */
   int wait;       /* ops [0, wait) complete first */
-  int reserved;   /* 0 */
+  int epilogue;   /* MLI_EPI_*: how the op's rows are stored */
   float* y;
   const float* x;    /* forms 0 and 2 */
   const int8_t* xq;  /* form 1 */

@@ -59,6 +59,13 @@ constexpr int kHeader = 256;
 constexpr int kMaxSlices = 8;
 constexpr int kMaxOps = 1 << 16;
 
+// Row epilogues: store y = v; add into y (the residual add that follows the
+// reference's down projection, src/model_cuda_v2_shared.cu:215-218, :414);
+// SwiGLU with the next op (gate = this op, up = the next one, stored as
+// (g * (1 / (1 + expf(-g)))) * u, :220-227, :410); the companion up op of a
+// SwiGLU pair (no units of its own).
+constexpr int kEpiStore = 0, kEpiAdd = 1, kEpiSwiglu = 2, kEpiCompanion = 3;
+
 // Device-side descriptor of one GEMV of the chain, 64 bytes (geometry
 // precomputed on the host, as plan_stream does for the single-GEMV kernel).
 // Kernels copy the table into shared memory when it fits.
@@ -72,8 +79,12 @@ struct Op {
   int unit_base;     // first work unit of this op
   int wait;          // ops [0, wait) complete before this op reads its activation
   int epoch;         // ops of one epoch read the same activation
-  uint16_t S, R;     // slices per row, rows per stage
+  uint8_t S;         // slices per row
+  uint8_t epi;       // kEpi*: how a finished row is stored
+  uint16_t R;        // rows per stage (a SwiGLU stage: R/2 gate rows, then the R/2 up rows)
   __host__ __device__ const float* x() const { return static_cast<const float*>(act); }
+  // output rows per work unit
+  __host__ __device__ int Ru() const { return epi == kEpiSwiglu ? R / 2 : R; }
   __host__ __device__ const int8_t* xq() const { return static_cast<const int8_t*>(act); }
   __host__ __device__ int G() const { return n / kGroup; }
 };
@@ -181,19 +192,28 @@ __device__ __forceinline__ int cta_units(const int* ph, int n_ph, int cta, int g
 }
 
 // Bulk copies of unit u (a stage of op o) into ring slot `slot`.
+template <bool kEpi>
 __device__ __forceinline__ void issue_unit(const Args& a, const Op* ops, unsigned char* ring,
                                            uint64_t* full, int o, int u, int slot) {
   const Op& op = ops[o];
-  const int R = op.R, G = op.G();
-  const int row0 = (u - op.unit_base) * R;
-  const int rows = min(R, op.d - row0);
+  const int R = op.R, G = op.G(), Ru = kEpi ? op.Ru() : R;
+  const int row0 = (u - op.unit_base) * Ru;
+  const int rows = min(Ru, op.d - row0);
   const uint32_t wb = static_cast<uint32_t>(rows) * op.n;
   const uint32_t sb = static_cast<uint32_t>(rows) * G * 4u;
   unsigned char* dst = ring + static_cast<size_t>(slot) * a.slot_bytes;
-  mbar_arrive_expect_tx(&full[slot], wb + sb);
+  const bool glu = kEpi && op.epi == kEpiSwiglu;
+  mbar_arrive_expect_tx(&full[slot], glu ? 2 * (wb + sb) : wb + sb);
   bulk_copy_g2s(dst, op.w + static_cast<size_t>(row0) * op.n, wb, &full[slot]);
   bulk_copy_g2s(dst + static_cast<size_t>(R) * op.n, op.s + static_cast<size_t>(row0) * G, sb,
                 &full[slot]);
+  if (glu) {  // the up projection's same rows behind the gate's
+    const Op& up = ops[o + 1];
+    bulk_copy_g2s(dst + static_cast<size_t>(Ru) * op.n, up.w + static_cast<size_t>(row0) * op.n, wb,
+                  &full[slot]);
+    bulk_copy_g2s(dst + static_cast<size_t>(R) * op.n + static_cast<size_t>(Ru) * G * 4u,
+                  up.s + static_cast<size_t>(row0) * G, sb, &full[slot]);
+  }
 }
 
 __device__ __forceinline__ void fence_acq_rel_gpu() {
@@ -375,7 +395,7 @@ struct Role {
 // producer (bulk copies), warp kW + 1 the publisher (completion counters and
 // dependency polls).  Consumers never wait on global memory ordering: the
 // gpu-scope fences and the polls run on the publisher warp.
-template <Form F, int kW, int kRB>
+template <Form F, int kW, int kRB, bool kEpi>
 __global__ void __launch_bounds__((kW + 2) * 32, 1) gemv_chain_kernel(const Args a) {
   constexpr int kT = kW * 32;  // consumer threads
   extern __shared__ __align__(1024) unsigned char smem[];
@@ -426,7 +446,7 @@ __global__ void __launch_bounds__((kW + 2) * 32, 1) gemv_chain_kernel(const Args
         const int u = cur.u;
         o = find_op(ops, a.count, u, o);
         fence_proxy_async_smem();  // consumers' reads of the slot precede the copy's writes
-        issue_unit(a, ops, ring, sm.full, o, u, slot);
+        issue_unit<kEpi>(a, ops, ring, sm.full, o, u, slot);
         *sm.issued = i + 1;
       }
     }
@@ -461,13 +481,15 @@ __global__ void __launch_bounds__((kW + 2) * 32, 1) gemv_chain_kernel(const Args
           *sm.broken = 1;
         }
         mbar_arrive(&sm.free[slot]);
-        pending += static_cast<unsigned>(min(static_cast<int>(op.R), op.d - (u - op.unit_base) * op.R));
+        const int ru = kEpi ? op.Ru() : static_cast<int>(op.R);
+        pending += static_cast<unsigned>(min(ru, op.d - (u - op.unit_base) * ru));
         // the CTA's next unit belongs to a later op, or there is none
         const bool last_of_op = i + 1 == cnt || (o + 1 < a.count && ops[o + 1].unit_base <= it.u);
         if (last_of_op) {
           if (!*sm.broken) {
             fence_acq_rel_gpu();  // with the add: release of the rows (stored by consumer warps)
             red_add_relaxed_gpu(a.done + o, pending);
+            if (kEpi && op.epi == kEpiSwiglu) red_add_relaxed_gpu(a.done + o + 1, pending);  // its companion
           }
           pending = 0;
         }
@@ -480,7 +502,7 @@ __global__ void __launch_bounds__((kW + 2) * 32, 1) gemv_chain_kernel(const Args
     constexpr int kSlice = slice_cols(F);
     constexpr int kLanesPerRow = 32 / kRB;
     int o = 0, cur = -1, known = 0, epoch = -1;
-    int n = 0, d = 0, Gr = 0, S = 1, R = 0, base = 0;
+    int n = 0, d = 0, Gr = 0, S = 1, R = 0, Ru = 0, epi = kEpiStore, base = 0;
     float* y = nullptr;
     int sl = 0, wj = 0;
     bool warp_on = false;
@@ -513,6 +535,12 @@ __global__ void __launch_bounds__((kW + 2) * 32, 1) gemv_chain_kernel(const Args
           known = wait;
         }
         n = op.n; d = op.d; Gr = op.G(); R = op.R; base = op.unit_base; y = op.y;
+        if constexpr (kEpi) {
+          Ru = op.Ru();
+          epi = op.epi;
+        } else {
+          Ru = R;
+        }
         if (ep != epoch) {
           epoch = ep;
           const Role<F, kW> role(op, warp, lane);
@@ -560,8 +588,8 @@ __global__ void __launch_bounds__((kW + 2) * 32, 1) gemv_chain_kernel(const Args
         cur = o;
       }
       const int slot = i % a.ring;
-      const int row0 = (u - base) * R;
-      const int rows = min(R, d - row0);
+      const int row0 = (u - base) * Ru;
+      const int rows = min(Ru, d - row0);
       bool ok = !*sm.broken;
       if (ok && !mbar_wait_bounded(&sm.full[slot], (i / a.ring) & 1, kWaitLimitNs)) {
         record_device_error(kDevStageTimeout);
@@ -574,7 +602,8 @@ __global__ void __launch_bounds__((kW + 2) * 32, 1) gemv_chain_kernel(const Args
       float* part = reinterpret_cast<float*>(smem + a.part_off) + slot * a.part_stride;
       if (ok && warp_on) {
         const int j0 = wj * kRB;
-        const int nvalid = rows - j0;
+        // a SwiGLU stage holds the gate's rows [0, Ru) and the up's [Ru, R)
+        const int nvalid = (kEpi && epi == kEpiSwiglu && j0 >= Ru ? Ru + rows : rows) - j0;
         if (nvalid > 0) {
           const int8_t* wr = wst + static_cast<size_t>(j0) * n + sl * kSlice;
           const float* sr = sst + j0 * Gr + sl * 8 * K;
@@ -603,6 +632,15 @@ __global__ void __launch_bounds__((kW + 2) * 32, 1) gemv_chain_kernel(const Args
           for (int rr = lane; rr < rows; rr += 32) {
             float v = part[rr * S];
             for (int s2 = 1; s2 < S; ++s2) v += part[rr * S + s2];
+            if (kEpi && epi == kEpiSwiglu) {
+              const int ru = Ru + rr;
+              float up = part[ru * S];
+              for (int s2 = 1; s2 < S; ++s2) up += part[ru * S + s2];
+              v *= (1.0f / (1.0f + expf(-v)));
+              v *= up;
+            } else if (kEpi && epi == kEpiAdd) {
+              v = __ldcg(y + row0 + rr) + v;
+            }
             y[row0 + rr] = v;
           }
         }
@@ -640,6 +678,7 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 // Kernel shape: consumer warps per CTA, rows per warp per stage, CTAs per SM.
 struct Variant {
   int warps, rb, per_sm;
+  bool epi;  // some op has a non-store epilogue: the kernel with epilogue code
 };
 
 struct Plan {
@@ -663,8 +702,8 @@ bool overlaps(const void* a, size_t an, const void* b, size_t bn) {
 // comparisons).
 Variant pick_variant(int form, unsigned flags) {
   const bool a32 = form == 0;
-  if (flags & (1u << 8)) return {8, a32 ? 4 : 2, 1};
-  return {8, a32 ? 8 : 4, 1};
+  if (flags & (1u << 8)) return {8, a32 ? 4 : 2, 1, false};
+  return {8, a32 ? 8 : 4, 1, false};
 }
 
 // Validates the op list and lays out the chain.  Returns MLI_OK,
@@ -677,7 +716,8 @@ int plan_chain(const mli_gemv_op* in, int count, int sm_count, int smem_per_sm, 
   const int form = in[0].form;
   if (form < 0 || form > 2) return MLI_ERR_INVALID_ARG;
   const Form f = static_cast<Form>(form);
-  const Variant var = pick_variant(form, flags);
+  Variant var = pick_variant(form, flags);
+  for (int i = 0; i < count; ++i) var.epi |= in[i].epilogue != kEpiStore;
   p->v = var;
   p->ops.assign(count, Op{});
   p->phases.clear();
@@ -685,13 +725,25 @@ int plan_chain(const mli_gemv_op* in, int count, int sm_count, int smem_per_sm, 
   long long units = 0;
   size_t slot = 0, xbytes = 0;
   int part_stride = 0, epoch = -1;
-  for (int i = 0; i < count; ++i) {
+  bool companion = false;  // op i is the up projection of the SwiGLU pair started at op i - 1
+  for (int i = 0; i < count; ++i, companion = !companion && in[i - 1].epilogue == kEpiSwiglu) {
     const mli_gemv_op& s = in[i];
     if (s.form != form) return MLI_ERR_INVALID_ARG;
-    if (!s.y || !s.w_q || !s.w_s || s.n <= 0 || s.d <= 0 || s.group_size <= 0) return MLI_ERR_INVALID_ARG;
+    if (s.epilogue < kEpiStore || s.epilogue > kEpiSwiglu) return MLI_ERR_INVALID_ARG;
+    if (companion) {
+      // same activation, shape and dependencies as its gate; no output of its own
+      const mli_gemv_op& g = in[i - 1];
+      if (s.epilogue != kEpiStore || s.n != g.n || s.d != g.d || s.wait != g.wait || s.x != g.x ||
+          s.xq != g.xq || s.xs != g.xs)
+        return MLI_ERR_INVALID_ARG;
+    } else if (!s.y) {
+      return MLI_ERR_INVALID_ARG;
+    }
+    if (s.epilogue == kEpiSwiglu && i + 1 >= count) return MLI_ERR_INVALID_ARG;
+    if (!s.w_q || !s.w_s || s.n <= 0 || s.d <= 0 || s.group_size <= 0) return MLI_ERR_INVALID_ARG;
     if (f == Form::kW8A8 ? (!s.xq || !s.xs) : !s.x) return MLI_ERR_INVALID_ARG;
     if (s.wait < 0 || s.wait > i) return MLI_ERR_INVALID_ARG;
-    if (f != Form::kW8A8 && overlaps(s.y, 4u * s.d, s.x, 4u * s.n)) return MLI_ERR_INVALID_ARG;
+    if (!companion && f != Form::kW8A8 && overlaps(s.y, 4u * s.d, s.x, 4u * s.n)) return MLI_ERR_INVALID_ARG;
     if (s.group_size != kGroup || s.n % 256 != 0) return MLI_ERR_UNSUPPORTED;
     if (!aligned(s.w_q, 16) || !aligned(s.w_s, 16) ||
         !aligned(f == Form::kW8A8 ? static_cast<const void*>(s.xq) : s.x, 16))
@@ -707,9 +759,13 @@ int plan_chain(const mli_gemv_op* in, int count, int sm_count, int smem_per_sm, 
     const int S = (s.n + slice_cols(f) - 1) / slice_cols(f);
     if (S > kMaxSlices) return MLI_ERR_UNSUPPORTED;
     const int R = var.rb * (var.warps / S);
-    op.S = static_cast<uint16_t>(S);
+    op.S = static_cast<uint8_t>(S);
     op.R = static_cast<uint16_t>(R);
-    const int n_stages = (s.d + R - 1) / R;
+    op.epi = static_cast<uint8_t>(companion ? kEpiCompanion : s.epilogue);
+    // a SwiGLU stage holds R/2 gate rows and their R/2 up rows: a warp's rows
+    // must fall in one half
+    if (op.epi == kEpiSwiglu && (R / 2) % var.rb != 0) return MLI_ERR_UNSUPPORTED;
+    const int n_stages = companion ? 0 : (s.d + op.Ru() - 1) / op.Ru();
     op.unit_base = static_cast<int>(units);
     if (s.wait > max_wait) {  // a new dependency: a new phase
       p->phases.push_back(op.unit_base);
@@ -772,19 +828,24 @@ int plan_chain(const mli_gemv_op* in, int count, int sm_count, int smem_per_sm, 
 
 using KernelFn = void (*)(const Args);
 
-template <Form F>
+template <Form F, bool kEpi>
 KernelFn kernel_shape(const Variant& v) {
   if constexpr (F == Form::kW8A32)
-    return v.rb == 8 ? gemv_chain_kernel<F, 8, 8> : gemv_chain_kernel<F, 8, 4>;
+    return v.rb == 8 ? gemv_chain_kernel<F, 8, 8, kEpi> : gemv_chain_kernel<F, 8, 4, kEpi>;
   else
-    return v.rb == 4 ? gemv_chain_kernel<F, 8, 4> : gemv_chain_kernel<F, 8, 2>;
+    return v.rb == 4 ? gemv_chain_kernel<F, 8, 4, kEpi> : gemv_chain_kernel<F, 8, 2, kEpi>;
+}
+
+template <Form F>
+KernelFn kernel_epi(const Variant& v) {
+  return v.epi ? kernel_shape<F, true>(v) : kernel_shape<F, false>(v);
 }
 
 KernelFn kernel_for(int form, const Variant& v) {
   switch (form) {
-    case 0: return kernel_shape<Form::kW8A32>(v);
-    case 1: return kernel_shape<Form::kW8A8>(v);
-    default: return kernel_shape<Form::kW8A8Fused>(v);
+    case 0: return kernel_epi<Form::kW8A32>(v);
+    case 1: return kernel_epi<Form::kW8A8>(v);
+    default: return kernel_epi<Form::kW8A8Fused>(v);
   }
 }
 

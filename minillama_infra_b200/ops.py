@@ -141,6 +141,7 @@ def set_pdl(enabled: bool) -> None:
 # + norm), down after gate/up (SwiGLU); the next layer's q/k/v wait for down.
 DECODE_LAYER_WAITS = (0, 0, 0, 3, 4, 4, 6)
 _FORMS = {"w8a32": 0, "w8a8": 1, "w8a8_fused": 2}
+_EPILOGUES = {"store": 0, "add": 1, "swiglu": 2}
 
 
 class GemvChain:
@@ -150,8 +151,12 @@ class GemvChain:
     "w8a8_fused"), y, w_q, w_s, n, d, wait and x (or xq and xs for "w8a8");
     tensors or raw device pointers.  Op i reads its activation only once ops
     [0, wait) have finished.  Each op's y is bit-identical to the single call
-    (matmul_int8 / matmul_dp4a / matmul_dp4a_fused).  The buffers must
-    outlive the chain; the chain keeps references to the tensors given.
+    (matmul_int8 / matmul_dp4a / matmul_dp4a_fused).  Optional "epilogue":
+    "store" (default), "add" (y += the op's rows: the residual add), or
+    "swiglu" (this op is the gate and the NEXT op the up projection, same n, d,
+    x and wait; y = silu(gate) * up; the next op's y may be None).  The
+    buffers must outlive the chain; the chain keeps references to the tensors
+    given.
     """
 
     def __init__(self, ops, group_size: int = 64):
@@ -160,7 +165,8 @@ class GemvChain:
         for i, o in enumerate(ops):
             e = arr[i]
             e.form = _FORMS[o["form"]]
-            e.n, e.d, e.group_size, e.wait, e.reserved = o["n"], o["d"], group_size, o.get("wait", 0), 0
+            e.n, e.d, e.group_size, e.wait = o["n"], o["d"], group_size, o.get("wait", 0)
+            e.epilogue = _EPILOGUES[o.get("epilogue", "store")]
             for key in ("y", "x", "xq", "xs", "w_q", "w_s"):
                 t = o.get(key)
                 setattr(e, key, _ptr(t))

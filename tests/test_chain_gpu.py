@@ -189,3 +189,45 @@ def test_chain_rejects_bad_arguments():
         ops.GemvChain([dict(form="w8a32", n=256, d=64, wait=1, x=x, y=y, w_q=q, w_s=s)])
     with pytest.raises(MliError):
         ops.GemvChain([dict(form="w8a32", n=192, d=64, wait=0, x=x, y=y, w_q=q, w_s=s)])
+
+
+@pytest.mark.parametrize("form", ["w8a32", "w8a8_fused"])
+def test_chain_swiglu_and_residual_epilogues(form):
+    """One chain: h = silu(W1 x) * (W3 x) (SwiGLU pair), then res += W2 h.
+    Against single calls followed by the reference's elementwise steps
+    (silu_mul, add: src/model_cuda_v2_shared.cu:215-227) in fp32."""
+    dim, hidden = 2048, 8192
+    w1 = weights(hidden, dim, 71)
+    w3 = weights(hidden, dim, 72)
+    w2 = weights(dim, hidden, 73)
+    x = torch.from_numpy(synth.activation_np(dim, 74, outliers=form != "w8a32")).to(dev())
+    res0 = torch.from_numpy(synth.activation_np(dim, 75)).to(dev())
+    g = torch.empty(hidden, device=dev())
+    u = torch.empty(hidden, device=dev())
+    single(form, g, x, w1[0], w1[1], dim, hidden)
+    single(form, u, x, w3[0], w3[1], dim, hidden)
+    h_ref = g * (1.0 / (1.0 + torch.exp(-g)))
+    h_ref = h_ref * u
+    v = torch.empty(dim, device=dev())
+    single(form, v, h_ref, w2[0], w2[1], hidden, dim)
+    res_ref = res0 + v
+    torch.cuda.synchronize()
+
+    h = torch.full((hidden,), float("nan"), device=dev())
+    res = res0.clone()
+    c = ops.GemvChain([
+        dict(form=form, n=dim, d=hidden, wait=0, x=x, y=h, w_q=w1[0], w_s=w1[1], epilogue="swiglu"),
+        dict(form=form, n=dim, d=hidden, wait=0, x=x, y=None, w_q=w3[0], w_s=w3[1]),
+        dict(form=form, n=hidden, d=dim, wait=2, x=h, y=res, w_q=w2[0], w_s=w2[1], epilogue="add"),
+    ])
+    for rep in range(2):
+        res.copy_(res0)
+        h.fill_(float("nan"))
+        c.run()
+        torch.cuda.synchronize()
+        hn, hr = h.cpu().numpy(), h_ref.cpu().numpy()
+        assert not np.isnan(hn).any()
+        assert orc.max_abs_rel(hn, hr) <= 1e-6, rep
+        assert orc.max_abs_rel(res.cpu().numpy(), res_ref.cpu().numpy()) <= 1e-5, rep
+    c.close()
+    assert ops.device_error() == 0

@@ -147,3 +147,52 @@ def test_chain_plan_independent_ops_form_one_phase():
         e.wait = 0
     rc, p = plan_chain(arr)
     assert rc == _lib.MLI_OK and p["phases"] == 1
+
+
+def _ffn_chain(form=0):
+    """gate (SwiGLU with the next op), up (its companion), down (add into the residual)."""
+    mb = 1 << 20
+    arr = (_lib.GemvOp * 3)()
+    for i, (d, n) in enumerate([(8192, 2048), (8192, 2048), (2048, 8192)]):
+        e = arr[i]
+        e.form, e.n, e.d, e.group_size = form, n, d, 64
+        e.w_q, e.w_s = mb * (100 + i), mb * (200 + i)
+    arr[0].x = arr[1].x = mb * 10
+    arr[0].y = mb * 20            # h
+    arr[0].epilogue = 2
+    arr[1].y = None               # the companion's output is unused
+    arr[2].x, arr[2].y, arr[2].wait, arr[2].epilogue = mb * 20, mb * 30, 2, 1
+    return arr
+
+
+@pytest.mark.parametrize("form", [0, 2])
+def test_chain_plan_swiglu_pair_and_add(form):
+    rc, p = plan_chain(_ffn_chain(form))
+    assert rc == _lib.MLI_OK
+    # a SwiGLU stage holds half the rows of a plain one (gate + up rows together);
+    # the companion adds no units
+    rows_gate = 65536 // 2048 // 2
+    rows_down = 65536 // 8192
+    assert p["units"] == -(-8192 // rows_gate) + -(-2048 // rows_down)
+    assert p["phases"] == 2
+
+
+def test_chain_plan_rejects_bad_epilogues():
+    bad = _ffn_chain()
+    bad[1].n = 4096               # companion shape differs from its gate
+    assert plan_chain(bad)[0] == _lib.MLI_ERR_INVALID_ARG
+    bad = _ffn_chain()
+    bad[1].wait = 1               # companion waits differently
+    assert plan_chain(bad)[0] == _lib.MLI_ERR_INVALID_ARG
+    bad = _ffn_chain()
+    bad[1].epilogue = 1           # companion with its own epilogue
+    assert plan_chain(bad)[0] == _lib.MLI_ERR_INVALID_ARG
+    bad = _ffn_chain()
+    bad[2].epilogue = 2           # SwiGLU on the last op: no companion
+    assert plan_chain(bad)[0] == _lib.MLI_ERR_INVALID_ARG
+    bad = _ffn_chain()
+    bad[2].epilogue = 5
+    assert plan_chain(bad)[0] == _lib.MLI_ERR_INVALID_ARG
+    bad = _ffn_chain()
+    bad[0].y = None               # the gate's output is required
+    assert plan_chain(bad)[0] == _lib.MLI_ERR_INVALID_ARG
