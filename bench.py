@@ -19,8 +19,9 @@ activations are N(0, 1) (W8A8: 1% of channels x20).
          the 112 output vectors back.
   decode_chain   the same weights in decode order with decode dependencies
          (o after q/k/v, gate/up after o, down after gate/up, the next layer
-         after down; each GEMV reads the output of the one it follows), also
-         one chain launch: the GEMV part of a decode step, as tok/s.
+         after down), gate/up as one SwiGLU pair and down adding into the
+         residual stream, also one chain launch: the GEMV part of a decode
+         step, as tok/s.
   percall_graph  the 112 single-GEMV calls captured into a CUDA graph
          (programmatic dependent launch between them), for comparison.
 
@@ -185,24 +186,35 @@ def build_chain_independent(wl, form):
 
 
 def build_chain_decode(wl, form, device):
-    """The same weights in decode order: q/k/v read the layer input (the
-    previous layer's down output), o reads q's output, gate/up read o's
-    output, down reads gate's output; waits as in a decode step."""
+    """The same weights in decode order, with the decode step's dependencies:
+    q/k/v read the attention norm's output, o reads q's output (standing in
+    for attention), gate/up run as one SwiGLU pair on the FFN norm's output
+    after o, and down reads the SwiGLU output and adds into the residual
+    stream; the next layer starts after down.  The two norms are outside this
+    path: fixed normalised vectors stand in for their outputs (each op still
+    waits for the ops its real input depends on)."""
     names = ["q", "k", "v", "o", "gate", "up", "down"]
     calls = wl["calls"]
-    x0 = torch.from_numpy(synth.activation_np(2048, 4242, outliers=(form == "w8a8"))).to(device)
+    att_in = torch.from_numpy(synth.activation_np(2048, 4242, outliers=(form == "w8a8"))).to(device)
+    ffn_in = torch.from_numpy(synth.activation_np(2048, 4243, outliers=(form == "w8a8"))).to(device)
+    resid = torch.zeros(2048, dtype=torch.float32, device=device)
     outs = {nm: torch.empty(d, dtype=torch.float32, device=device) for nm, (_, d, _) in zip(names, synth.LLAMA_1B)}
-    downs = [torch.empty(2048, dtype=torch.float32, device=device) for _ in range(synth.LLAMA_1B_LAYERS)]
+    src = {"q": att_in, "k": att_in, "v": att_in, "o": outs["q"], "gate": ffn_in, "up": ffn_in,
+           "down": outs["gate"]}
     chain = []
     for l in range(synth.LLAMA_1B_LAYERS):
-        layer_in = x0 if l == 0 else downs[l - 1]
-        src = {"q": layer_in, "k": layer_in, "v": layer_in, "o": outs["q"], "gate": outs["o"],
-               "up": outs["o"], "down": outs["gate"]}
         for i, nm in enumerate(names):
             _, d, n, q, s = calls[7 * l + i]
-            chain.append(dict(form=chain_form(form), n=n, d=d, wait=7 * l + ops.DECODE_LAYER_WAITS[i],
-                              x=src[nm], y=downs[l] if nm == "down" else outs[nm], w_q=q, w_s=s))
-    return ops.GemvChain(chain)
+            op = dict(form=chain_form(form), n=n, d=d, wait=7 * l + ops.DECODE_LAYER_WAITS[i], x=src[nm],
+                      y=outs.get(nm), w_q=q, w_s=s)
+            if nm == "gate":
+                op["epilogue"] = "swiglu"   # y = silu(gate) * up
+            elif nm == "up":
+                op["y"] = None              # its rows feed the gate's SwiGLU
+            elif nm == "down":
+                op.update(y=resid, epilogue="add")
+            chain.append(op)
+    return ops.GemvChain(chain), resid
 
 
 class PipelinedSteps:
@@ -823,7 +835,7 @@ def main():
     side = {}
     if args.impl == "ours":
         # the decode-ordered chain and the per-call graph, same weights
-        dchain = build_chain_decode(wl, args.form, device)
+        dchain, _resid = build_chain_decode(wl, args.form, device)
         with torch.cuda.stream(stream):
             issue_step_ours(wl, args.form)  # eager warm-up of the single-GEMV kernels
         torch.cuda.synchronize()
@@ -842,8 +854,10 @@ def main():
                                  "steps": side_steps}
         side["decode_chain"]["tok_s_gemv_only"] = round(1000.0 / side["decode_chain"]["ms_per_step"], 1)
         side["decode_chain"]["dependencies"] = ("decode order: o after q/k/v, gate/up after o, down after "
-                                                "gate/up, next layer after down; each GEMV reads the output "
-                                                "of the GEMV it follows")
+                                                "gate/up, next layer after down; gate/up run as one SwiGLU "
+                                                "pair, down adds into the residual stream; fixed normalised "
+                                                "vectors stand in for the two RMSNorm outputs (not part of "
+                                                "this path)")
         side["percall_graph"]["launch"] = "112 single-GEMV C-ABI calls in a CUDA graph, programmatic dependent launch"
         torch.cuda.synchronize()
         del graph
