@@ -49,6 +49,12 @@ enum mli_status_code {
  * runs two CTAs per SM; with this bit only matrices of 16+ stages per SM do,
  * the others leave the second slot to the next kernel in the stream. */
 #define MLI_LAUNCH_ONE_CTA 2u
+/* Batched W8A8 (tensor cores): by default the K splits of an output tile run
+ * as one thread-block cluster and sum their partials over shared memory; with
+ * this bit a split-K launch given a workspace sums them there instead (partial
+ * sums in the workspace and a second kernel), and one without a workspace does
+ * not split K. */
+#define MLI_LAUNCH_NO_CLUSTER 4u
 
 /* ---- library state ------------------------------------------------------ */
 const char* mli_status_string(int status);
@@ -169,12 +175,14 @@ int mli_quantize_activation_rows(int8_t* xq, float* xs, const float* x, int m,
  * m >= 16 with n % 128 == 0 runs on the tcgen05 kind::i8 tensor-core path
  * (tiles of 128 weight rows x up to 128 tokens); smaller m, or other shapes,
  * on the CUDA-core path.  Each token's row is within the W8A8 tolerance of
- * mli_gemv_w8a8 on that token.  `workspace` (device, may be NULL) lets the
- * tensor-core path split K over CTAs to fill the GPU: it needs
- * mli_gemm_w8a8_workspace_bytes(m, n, d) bytes, any contents (the splits'
- * partial sums, summed in split order by a second launch on the same
- * stream); without it K is not split.  Calls that share a workspace must not
- * overlap on the GPU. */
+ * mli_gemv_w8a8 on that token.  The tensor-core path splits K over CTAs to
+ * fill the GPU.  The splits of a tile run as one thread-block cluster and
+ * sum their partials in split order over shared memory, when clusters of
+ * that size fit the GPU in one wave; otherwise `workspace` (device, may be
+ * NULL; mli_gemm_w8a8_workspace_bytes(m, n, d) bytes, any contents) holds
+ * the splits' partial sums, summed in split order by a second launch on the
+ * same stream, and without it K is split only as far as clusters allow.
+ * Calls that share a workspace must not overlap on the GPU. */
 size_t mli_gemm_w8a8_workspace_bytes(int m, int n, int d);
 int mli_gemm_w8a8(float* y, const int8_t* xq, const float* xs,
                   const int8_t* w_q, const float* w_s, int m, int n, int d,
@@ -201,6 +209,11 @@ int mli_gemm_w8a8_noalloc(float* y, const int8_t* xq, const float* xs,
 int mli_gemm_w8a8_cuda_core(float* y, const int8_t* xq, const float* xs,
                             const int8_t* w_q, const float* w_s, int m, int n,
                             int d, int group_size, void* stream);
+/* Tensor-core plan of mli_gemm_w8a8 on the current device (queries it; no
+ * launch).  out[5] = tokens per tile, output tiles, K splits, cluster size
+ * (1: none), 1 when the splits sum through the workspace.  Returns
+ * MLI_ERR_UNSUPPORTED for shapes outside the tensor-core path. */
+int mli_debug_plan_gemm(int m, int n, int d, size_t workspace_bytes, int* out);
 
 /* ---- row-sharded linear layer across GPUs (one process per GPU) --------- */
 

@@ -21,6 +21,7 @@ MLI_ERR_UNSUPPORTED = 2
 MLI_ERR_CUDA = 3
 MLI_ERR_DEVICE = 4
 MLI_LAUNCH_PDL = 1
+MLI_LAUNCH_NO_CLUSTER = 4
 
 # Every symbol include/mli_gemv.h declares with C linkage, with its ctypes
 # signature (device pointers and streams travel as void*).
@@ -72,6 +73,7 @@ SIGNATURES = {
     "mli_chain_run": (_I, [_P, _P]),
     "mli_chain_destroy": (_I, [_P]),
     "mli_debug_plan_chain": (_I, [_OPS, _I, _I, _I, ctypes.POINTER(_I)]),
+    "mli_debug_plan_gemm": (_I, [_I, _I, _I, ctypes.c_size_t, ctypes.POINTER(_I)]),
 }
 
 # The drop-in shim's C++ symbols (include/mli_gemv.h, reference include/model.h:62-64).

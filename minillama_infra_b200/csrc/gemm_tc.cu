@@ -8,22 +8,27 @@
 // 465-501); with m >= 16 tokens the op is a real dense contraction and runs
 // here.  One CTA computes a tile of 128 weight rows x BN tokens over a range of
 // K:
-//   * warp 0 streams 128-byte K chunks of the weight tile (128 x 128 B) and of
-//     the activations (BN x 128 B) with 2-D TMA loads (128-byte swizzle, the
-//     canonical K-major UMMA layout) into a 6-stage shared-memory ring;
+//   * warp 0 streams 128-byte K chunks of the weight tile (128 x 128 B) into a
+//     deep ring (9-11 stages: the weights come from HBM), warp 2 the matching
+//     activation chunks (BN x 128 B, re-read from L2) into a shallow one,
+//     both with 2-D TMA loads (128-byte swizzle, the canonical K-major UMMA
+//     layout);
 //   * warp 1 owns the tensor memory and issues the MMAs from one thread: a
 //     64-column group is two K=32 MMAs accumulating into one of up to eight
 //     int32 accumulators, committed to an mbarrier;
-//   * warps 2.. are the epilogue (4 lane quarters x up to 4 token-column
-//     slices): each reads its 32 accumulator rows over its slice of the BN
-//     token columns (tcgen05.ld), recovers the exact int32 group dot
-//     as a float (the accumulators start at a bias that makes the int32 result
-//     the bits of 1.5 * 2^23 + I), adds ws[r][g] * I into fp32 registers, and
-//     refills the accumulator with the bias for its next use.
-// Tiles of K are split over CTAs so a layer fills the GPU; each split writes
-// its partial into the caller's workspace and a small kernel launched right
-// after sums the splits in split order (deterministic) over the whole GPU,
-// scales by xs[t] and writes Y.
+//   * warps 3.. are the epilogue (4 lane quarters x 2 token-column slices):
+//     each reads its 32 accumulator rows over its slice of the BN token
+//     columns (tcgen05.ld), recovers the exact int32 group dot as a float
+//     (the accumulators start at a bias that makes the int32 result the bits
+//     of 1.5 * 2^23 + I), adds ws[r][g] * I into fp32 registers (packed f32x2
+//     arithmetic) and refills the accumulator with the bias for its next use.
+// K is split over CTAs so a layer fills the GPU.  The splits of a tile run as
+// one thread-block cluster: each stages its partial tile in shared memory and
+// sums a share of the tile over the cluster's partials in split order
+// (deterministic), scales by xs[t] and writes Y.  Where clusters of the
+// wanted size do not fit the GPU at once, the splits may instead write their
+// partials into the caller's workspace, summed in split order by a second,
+// GPU-wide kernel.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -36,17 +41,25 @@ namespace mli {
 
 namespace tc {
 
-constexpr int kBM = 128;             // weight rows per tile (UMMA M)
+constexpr int kBM = 128;             // weight rows per tile (UMMA M); a token's tile row is 32 float4s
 constexpr int kChunk = 128;          // K bytes per stage (one 128-byte swizzle atom)
-constexpr int kStages = 6;
-// Warp 0 TMA, warp 1 MMA, warps 2.. epilogue: 4 lane quarters x kSlices token
-// column slices (kCols columns each).  Two slices (8 epilogue warps): a
-// measured tie with four, at more registers per thread and no spills.
+constexpr int kStageA = kBM * kChunk;  // 16 KB of weights per stage
+// Weight stages stream from HBM and need many bytes in flight per SM;
+// activation stages (bn x 128 bytes) are re-read from L2 by every row tile
+// and need few.  Two rings, each with its own producer warp, keep most of
+// shared memory on the weight stream.
+__host__ __device__ constexpr int stages_a(int bn) { return bn >= 128 ? 9 : (bn >= 64 ? 10 : 11); }
+__host__ __device__ constexpr int stages_b(int bn) { return bn >= 128 ? 3 : 4; }
+constexpr int kMaxStages = 11;
+// Warp 0 weight TMA, warp 1 MMA, warp 2 activation TMA, warps 3.. epilogue:
+// 4 lane quarters x kSlices token column slices (kCols columns each).  A warp
+// reads the tensor-memory lanes of its rank in the warpgroup (warp % 4).
 template <int kBN>
 struct Shape {
   static constexpr int kSlices = 2;
   static constexpr int kEpiWarps = 4 * kSlices;
-  static constexpr int kThreads = (kEpiWarps + 2) * 32;
+  static constexpr int kFirstEpiWarp = 3;
+  static constexpr int kThreads = (kEpiWarps + kFirstEpiWarp) * 32;
   static constexpr int kCols = kBN / kSlices;
 };
 constexpr int kMaxAccBufs = 8;
@@ -60,10 +73,12 @@ struct Args {
   float* y;
   const float* xs;
   const float* ws;
-  float* partial;        // [splits][m][d] fp32 (splits > 1): summed by splitk_reduce_kernel
+  float* partial;        // [splits][m][d] fp32 (splits > 1, no cluster): summed by splitk_reduce_kernel
   int m, n, d, G;
   int bn;                // tokens per tile (multiple of 16, <= 128)
   int tiles_m, tiles_n, splits, chunks;
+  int cluster;           // > 1: the splits of a tile form one cluster and sum over shared memory
+  int vec4;              // outputs may be written as aligned float4 (d % 4 == 0, 16-byte aligned)
 };
 
 // ---------------------------------------------------------------------------
@@ -121,7 +136,7 @@ __device__ __forceinline__ void tmem_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
       "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
@@ -132,11 +147,33 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
 }
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
+      "[%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* r) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
                  "=r"(r[6]), "=r"(r[7])
                : "r"(taddr));
+}
+// This warp's 32 lanes x kCols consecutive accumulator columns at taddr.
+template <int kCols>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[kCols]) {
+  if constexpr (kCols >= 32) {
+#pragma unroll
+    for (int q = 0; q < kCols / 32; ++q) tmem_ld32(taddr + 32 * q, r + 32 * q);
+  } else if constexpr (kCols == 16) {
+    tmem_ld16(taddr, r);
+  } else {
+    static_assert(kCols == 8, "8, 16 or a multiple of 32 columns");
+    tmem_ld8(taddr, r);
+  }
 }
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
@@ -149,19 +186,39 @@ __device__ __forceinline__ void tmem_wait_ld() {
 constexpr uint32_t kAccBias = 0x4B400000u;
 constexpr float kAccBiasF = 12582912.0f;  // 1.5 * 2^23
 
-// Fills this warp's 32 lanes x (8 * kN) columns at taddr with the bias.
-template <int kN>
+// Fills this warp's 32 lanes x kCols columns at taddr with the bias.  Eight
+// columns per store: a store's source is as many consecutive registers as it
+// has columns, and eight registers of the bias stay live for the whole loop.
+template <int kCols>
 __device__ __forceinline__ void tmem_fill_bias(uint32_t taddr) {
+  static_assert(kCols % 8 == 0, "a multiple of 8 columns");
   const uint32_t b = kAccBias;
 #pragma unroll
-  for (int q = 0; q < kN; ++q)
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(
-                     taddr + 8 * q),
-                 "r"(b), "r"(b), "r"(b), "r"(b), "r"(b), "r"(b), "r"(b), "r"(b)
+  for (int q = 0; q < kCols / 8; ++q)
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr + 8 * q),
+                 "r"(b)
                  : "memory");
 }
 __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Two fp32 lanes per instruction (sm_100 packed f32x2 arithmetic); each lane
+// rounds exactly like the scalar instruction.
+__device__ __forceinline__ uint64_t f2_pack(uint32_t lo, uint32_t hi) {
+  uint64_t v;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "r"(lo), "r"(hi));
+  return v;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+// acc + (biased - bias) * w, per lane: (float)I * ws accumulated as before.
+__device__ __forceinline__ uint64_t f2_unbias_fma(uint64_t biased, uint64_t bias, uint64_t w, uint64_t acc) {
+  uint64_t t, d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(t) : "l"(biased), "l"(bias));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(t), "l"(w), "l"(acc));
+  return d;
 }
 
 // 4-byte global -> shared asynchronous copy (no register round trip).
@@ -172,15 +229,57 @@ __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
 }
 
+// Thread-block cluster barrier over every thread of every block of the
+// cluster; release/acquire order the shared-memory writes before it with the
+// reads of other blocks after it.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release;\nbarrier.cluster.wait.acquire;" ::: "memory");
+}
+// Address of the same shared-memory location in block `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_peer(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ int ld_cluster_s32(uint32_t addr) {
+  int v;
+  asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+// Four consecutive outputs of token t, rows r .. r + 3 (those below d).
+__device__ __forceinline__ void store_out4(float* dst, const Args& a, int t, int r, float4 v) {
+  float* p = dst + static_cast<size_t>(t) * a.d + r;
+  if (a.vec4 && r + 3 < a.d) {
+    *reinterpret_cast<float4*>(p) = v;
+  } else {
+    const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (r + i < a.d) p[i] = e[i];
+  }
+}
+
 // ---------------------------------------------------------------------------
-// Shared memory: ring of (A 16 KB | B bn*128 B) stages, 1024-byte aligned,
-// then the barriers.
+// Shared memory (1024-byte aligned): the weight ring, the activation ring,
+// the barriers, the group-scale window and the token scales.
 // ---------------------------------------------------------------------------
 struct Smem {
-  unsigned char* ring;   // stage s: A at ring + s * stage_bytes, B 16 KB after it
-  uint32_t stage;
-  uint64_t* full;
-  uint64_t* empty;
+  unsigned char* a;      // weight stage i at a + i * kStageA
+  unsigned char* b;      // activation stage i at b + i * b_stage
+  uint32_t b_stage;
+  uint64_t* full_a;
+  uint64_t* empty_a;
+  uint64_t* full_b;
+  uint64_t* empty_b;
   uint64_t* acc_full;
   uint64_t* acc_empty;
   uint32_t* tmem_base;
@@ -196,31 +295,46 @@ struct Smem {
 constexpr int kWsWin = 48;
 constexpr int kWsStride = kWsWin + 1;
 constexpr uint32_t kWsBytes = kBM * kWsStride * 4u;
+constexpr uint32_t kBarBytes = 512u;
 
-__host__ __device__ constexpr uint32_t stage_bytes(int bn) { return 16384u + static_cast<uint32_t>(bn) * 128u; }
-__host__ __device__ constexpr uint32_t smem_bytes(int bn) {
-  return 1024u /* alignment slack */ + kStages * stage_bytes(bn) + 512u + kWsBytes + 512u /* xs */;
+__host__ __device__ constexpr uint32_t b_stage_bytes(int bn) { return static_cast<uint32_t>(bn) * kChunk; }
+__host__ __device__ constexpr uint32_t rings_bytes(int bn) {
+  return stages_a(bn) * static_cast<uint32_t>(kStageA) + stages_b(bn) * b_stage_bytes(bn);
 }
+__host__ __device__ constexpr uint32_t smem_bytes(int bn) {
+  return 1024u /* alignment slack */ + rings_bytes(bn) + kBarBytes + kWsBytes + 512u /* xs */;
+}
+static_assert(smem_bytes(128) <= 232448 && smem_bytes(64) <= 232448 && smem_bytes(32) <= 232448 &&
+                  smem_bytes(16) <= 232448,
+              "shared memory per block");
+static_assert((4 * kMaxStages + 16) * 8 + 8 <= kBarBytes, "barrier area");
+// the finished tile ([bn][kBM] fp32) is staged in the weight ring
+static_assert(128 * kBM * 4 <= stages_a(128) * kStageA && 64 * kBM * 4 <= stages_a(64) * kStageA &&
+                  32 * kBM * 4 <= stages_a(32) * kStageA && 16 * kBM * 4 <= stages_a(16) * kStageA,
+              "output tile in the weight ring");
 
 __device__ __forceinline__ Smem carve(unsigned char* raw, int bn) {
   Smem s;
   unsigned char* base = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(raw) + 1023u) & ~static_cast<uintptr_t>(1023u));
-  s.ring = base;
-  s.stage = stage_bytes(bn);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(base + kStages * stage_bytes(bn));
-  s.full = bars;
-  s.empty = bars + kStages;
-  s.acc_full = bars + 2 * kStages;
-  s.acc_empty = bars + 2 * kStages + kMaxAccBufs;
-  s.tmem_base = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 2 * kMaxAccBufs);
+  s.a = base;
+  s.b = base + stages_a(bn) * kStageA;
+  s.b_stage = b_stage_bytes(bn);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + rings_bytes(bn));
+  s.full_a = bars;
+  s.empty_a = bars + kMaxStages;
+  s.full_b = bars + 2 * kMaxStages;
+  s.empty_b = bars + 3 * kMaxStages;
+  s.acc_full = bars + 4 * kMaxStages;
+  s.acc_empty = bars + 4 * kMaxStages + kMaxAccBufs;
+  s.tmem_base = reinterpret_cast<uint32_t*>(bars + 4 * kMaxStages + 2 * kMaxAccBufs);
   s.flag = reinterpret_cast<int*>(s.tmem_base + 1);
-  s.ws = reinterpret_cast<float*>(base + kStages * stage_bytes(bn) + 512u);
+  s.ws = reinterpret_cast<float*>(base + rings_bytes(bn) + kBarBytes);
   s.xs = s.ws + kBM * kWsStride;
   return s;
 }
-__device__ __forceinline__ unsigned char* stage_a(const Smem& s, int i) { return s.ring + i * s.stage; }
-__device__ __forceinline__ unsigned char* stage_b(const Smem& s, int i) { return s.ring + i * s.stage + 16384; }
+__device__ __forceinline__ unsigned char* stage_a(const Smem& s, int i) { return s.a + i * kStageA; }
+__device__ __forceinline__ unsigned char* stage_b(const Smem& s, int i) { return s.b + i * s.b_stage; }
 
 template <int kEpiWarps>
 __device__ __forceinline__ void epi_sync() {
@@ -248,12 +362,17 @@ __global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
   const int ngroups = 2 * nchunks;
   constexpr int kAccBufs = acc_bufs(kBN);
   constexpr int kEpiWarps = Shape<kBN>::kEpiWarps;
+  constexpr int kSA = stages_a(kBN), kSB = stages_b(kBN);
   constexpr uint32_t kTmemCols = kAccBufs * kBN;  // 128, 256 or 512: a power of two
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kStages; ++i) {
-      mbar_init(&sm.full[i], 1);
-      mbar_init(&sm.empty[i], 1);
+    for (int i = 0; i < kSA; ++i) {
+      mbar_init(&sm.full_a[i], 1);
+      mbar_init(&sm.empty_a[i], 1);
+    }
+    for (int i = 0; i < kSB; ++i) {
+      mbar_init(&sm.full_b[i], 1);
+      mbar_init(&sm.empty_b[i], 1);
     }
     for (int i = 0; i < kAccBufs; ++i) {
       mbar_init(&sm.acc_full[i], 1);
@@ -276,28 +395,33 @@ __global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
   griddep_launch_dependents();
 
   if (warp == 0) {
-    // ---------------- TMA producer ----------------
+    // ---------------- weight TMA ----------------
+    // Weights never depend on the previous kernel: no griddepcontrol.wait.
     if (lane == 0) {
-      // Weights never depend on the previous kernel: fill the ring's weight
-      // halves first, then wait for the activations.
-      const int first = nchunks < kStages ? nchunks : kStages;
-      for (int c = 0; c < first; ++c) {
-        mbar_arrive_expect_tx(&sm.full[c], stage_bytes(kBN));
-        tma_load_2d(stage_a(sm, c), &map_w, (c_begin + c) * kChunk, row0, &sm.full[c]);
-      }
-      griddep_wait();
-      for (int c = 0; c < first; ++c) tma_load_2d(stage_b(sm, c), &map_x, (c_begin + c) * kChunk, tok0, &sm.full[c]);
-      for (int c = kStages; c < nchunks; ++c) {
-        const int s = c % kStages;
-        if (!mbar_wait_bounded(&sm.empty[s], ((c / kStages) - 1) & 1, kWaitLimitNs)) {
+      for (int c = 0; c < nchunks; ++c) {
+        const int st = c % kSA;
+        if (c >= kSA && !mbar_wait_bounded(&sm.empty_a[st], ((c / kSA) - 1) & 1, kWaitLimitNs)) {
           record_device_error(kDevMmaTimeout);
           *sm.flag = 1;
           break;
         }
-        mbar_arrive_expect_tx(&sm.full[s], stage_bytes(kBN));
-        const int kx = (c_begin + c) * kChunk;
-        tma_load_2d(stage_a(sm, s), &map_w, kx, row0, &sm.full[s]);
-        tma_load_2d(stage_b(sm, s), &map_x, kx, tok0, &sm.full[s]);
+        mbar_arrive_expect_tx(&sm.full_a[st], kStageA);
+        tma_load_2d(stage_a(sm, st), &map_w, (c_begin + c) * kChunk, row0, &sm.full_a[st]);
+      }
+    }
+  } else if (warp == 2) {
+    // ---------------- activation TMA ----------------
+    if (lane == 0) {
+      griddep_wait();
+      for (int c = 0; c < nchunks; ++c) {
+        const int st = c % kSB;
+        if (c >= kSB && !mbar_wait_bounded(&sm.empty_b[st], ((c / kSB) - 1) & 1, kWaitLimitNs)) {
+          record_device_error(kDevMmaTimeout);
+          *sm.flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&sm.full_b[st], b_stage_bytes(kBN));
+        tma_load_2d(stage_b(sm, st), &map_x, (c_begin + c) * kChunk, tok0, &sm.full_b[st]);
       }
     }
   } else if (warp == 1) {
@@ -307,14 +431,15 @@ __global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
       int gi = 0;
       bool ok = true;
       for (int c = 0; c < nchunks && ok; ++c) {
-        const int s = c % kStages;
-        if (!mbar_wait_bounded(&sm.full[s], (c / kStages) & 1, kWaitLimitNs)) {
+        const int sa = c % kSA, sb = c % kSB;
+        if (!mbar_wait_bounded(&sm.full_a[sa], (c / kSA) & 1, kWaitLimitNs) ||
+            !mbar_wait_bounded(&sm.full_b[sb], (c / kSB) & 1, kWaitLimitNs)) {
           ok = false;
           break;
         }
         tmem_fence_after();
-        const uint32_t a_base = smem_u32(stage_a(sm, s));
-        const uint32_t b_base = smem_u32(stage_b(sm, s));
+        const uint32_t a_base = smem_u32(stage_a(sm, sa));
+        const uint32_t b_base = smem_u32(stage_b(sm, sb));
         for (int g = 0; g < 2; ++g, ++gi) {
           const int buf = gi % kAccBufs;
           // use u of a buffer waits for phase u: the epilogue's bias fill
@@ -332,7 +457,9 @@ __global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
           }
           mma_commit(&sm.acc_full[buf]);
         }
-        mma_commit(&sm.empty[s]);  // the stage is free once its MMAs have read it
+        // the stages are free once their MMAs have read them
+        mma_commit(&sm.empty_a[sa]);
+        mma_commit(&sm.empty_b[sb]);
       }
       if (!ok) {
         record_device_error(kDevMmaTimeout);
@@ -340,44 +467,61 @@ __global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
       }
     }
   } else {
-    // ---------------- epilogue (warps 2..9) ----------------
+    // ---------------- epilogue ----------------
     const int quad = warp & 3;                 // TMEM lanes 32*quad .. +31
-    const int half = (warp - 2) >> 2;          // token column slice [half*kCols, +kCols)
+    const int half = (warp - Shape<kBN>::kFirstEpiWarp) >> 2;  // token column slice [half*kCols, +kCols)
     constexpr int kCols = Shape<kBN>::kCols;
-    const int row = row0 + 32 * quad + lane;
-    const bool row_ok = row < a.d;
-    float acc[kCols];
+    uint64_t acc[kCols / 2];  // fp32 pairs: columns 2j, 2j + 1
 #pragma unroll
-    for (int j = 0; j < kCols; ++j) acc[j] = 0.f;
-    const int et = static_cast<int>(threadIdx.x) - 64;  // epilogue thread 0..255
+    for (int j = 0; j < kCols / 2; ++j) acc[j] = 0;
+    const uint64_t bias2 = f2_pack(__float_as_uint(kAccBiasF), __float_as_uint(kAccBiasF));
+    const int et = static_cast<int>(threadIdx.x) - Shape<kBN>::kFirstEpiWarp * 32;  // epilogue thread
     // every accumulator buffer starts at the bias
     const uint32_t tlane = tmem + (static_cast<uint32_t>(32 * quad) << 16) + static_cast<uint32_t>(half * kCols);
 #pragma unroll
-    for (int b = 0; b < kAccBufs; ++b) tmem_fill_bias<kCols / 8>(tlane + static_cast<uint32_t>(b * kBN));
+    for (int b = 0; b < kAccBufs; ++b) tmem_fill_bias<kCols>(tlane + static_cast<uint32_t>(b * kBN));
     tmem_wait_st();
     tmem_fence_before();
     __syncwarp();
     if (lane == 0)
       for (int b = 0; b < kAccBufs; ++b) mbar_arrive(&sm.acc_empty[b]);
-    griddep_wait();  // xs and the outputs belong to the stream order
+    // Stages the scales of groups g0 .. g0 + wn - 1 of the tile's rows, two
+    // threads per row with every copy in flight at once (waited for by the
+    // caller).
+    auto stage_scales = [&](int g0) {
+      const int wn = ngroups - g0 < kWsWin ? ngroups - g0 : kWsWin;
+      constexpr int kTpr = kEpiWarps * 32 / kBM;  // threads per row
+      const int rl = et / kTpr, rr = row0 + rl;
+      float* dst = sm.ws + rl * kWsStride;
+      if (rr < a.d) {
+        const float* src = a.ws + static_cast<size_t>(rr) * a.G + 2 * c_begin + g0;
+        for (int g = et % kTpr; g < wn; g += kTpr) cp_async4(dst + g, src + g);
+      } else {
+        for (int g = et % kTpr; g < wn; g += kTpr) dst[g] = 0.f;
+      }
+    };
+    // The first window is weight data (no dependency on the previous
+    // kernel); xs and the outputs belong to the stream order.
+    stage_scales(0);
+    griddep_wait();
+    if (et < kBN) sm.xs[et] = tok0 + et < a.m ? __ldg(a.xs + tok0 + et) : 0.f;
+    cp_async_wait_all();
+    epi_sync<kEpiWarps>();
+    // A buffer goes back to the MMA warp once this warp's bias refill of it
+    // has completed.
+    auto release = [&](int b) {
+      tmem_wait_st();
+      tmem_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.acc_empty[b]);
+    };
+    int pending = -1;  // buffer whose refill is in flight
     bool ok = true;
     for (int gi = 0; gi < ngroups; ++gi) {
       const int buf = gi % kAccBufs;
-      if (gi % kWsWin == 0) {
-        // stage the scales of groups gi .. gi + wn - 1 of the tile's rows:
-        // two threads per row, every copy in flight at once
-        const int wn = ngroups - gi < kWsWin ? ngroups - gi : kWsWin;
+      if (gi > 0 && gi % kWsWin == 0) {
         epi_sync<kEpiWarps>();  // every epilogue thread is done with the previous window
-        constexpr int kTpr = kEpiWarps * 32 / kBM;  // threads per row
-        const int rl = et / kTpr, rr = row0 + rl;
-        float* dst = sm.ws + rl * kWsStride;
-        if (rr < a.d) {
-          const float* src = a.ws + static_cast<size_t>(rr) * a.G + 2 * c_begin + gi;
-          for (int g = et % kTpr; g < wn; g += kTpr) cp_async4(dst + g, src + g);
-        } else {
-          for (int g = et % kTpr; g < wn; g += kTpr) dst[g] = 0.f;
-        }
-        if (gi == 0 && et < kBN) sm.xs[et] = tok0 + et < a.m ? __ldg(a.xs + tok0 + et) : 0.f;
+        stage_scales(gi);
         cp_async_wait_all();
         epi_sync<kEpiWarps>();
       }
@@ -389,60 +533,87 @@ __global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
       tmem_fence_after();
       const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * quad) << 16) +
                              static_cast<uint32_t>(buf * kBN + half * kCols);
-      if constexpr (kCols >= 32) {
-        // 32 columns at a time: fewer live registers next to acc[kCols]
+      // every column load in flight at once
+      uint32_t r[kCols];
+      tmem_ld_cols<kCols>(taddr, r);
+      if (pending >= 0) release(pending);  // the previous group's refill overlaps these loads
+      tmem_wait_ld();
+      const uint64_t w2 = f2_pack(__float_as_uint(wsc), __float_as_uint(wsc));
 #pragma unroll
-        for (int q = 0; q < kCols / 32; ++q) {
-          uint32_t r[32];
-          tmem_ld32(taddr + 32 * q, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            acc[32 * q + j] = fmaf(__uint_as_float(r[j]) - kAccBiasF, wsc, acc[32 * q + j]);
-        }
-        tmem_fill_bias<kCols / 8>(taddr);  // ready for the buffer's next use
-      } else {
-        uint32_t r[kCols / 8][8];
-#pragma unroll
-        for (int q = 0; q < kCols / 8; ++q) tmem_ld8(taddr + 8 * q, r[q]);
-        tmem_wait_ld();
-        tmem_fill_bias<kCols / 8>(taddr);
-#pragma unroll
-        for (int q = 0; q < kCols / 8; ++q)
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            acc[8 * q + j] = fmaf(__uint_as_float(r[q][j]) - kAccBiasF, wsc, acc[8 * q + j]);
-      }
-      tmem_wait_st();
-      tmem_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.acc_empty[buf]);
+      for (int j = 0; j < kCols / 2; ++j) acc[j] = f2_unbias_fma(f2_pack(r[2 * j], r[2 * j + 1]), bias2, w2, acc[j]);
+      tmem_fill_bias<kCols>(taddr);  // ready for the buffer's next use
+      pending = buf;
     }
+    if (pending >= 0) release(pending);
     if (!ok) {
       record_device_error(kDevMmaTimeout);
       *sm.flag = 1;
     }
     epi_sync<kEpiWarps>();
-    const bool good = *sm.flag == 0;
-    const int t_base = tok0 + half * kCols;
-    if (good && a.splits == 1) {
-      if (row_ok) {
+    // Every load has landed and every MMA that read the weight ring has
+    // completed, so the ring takes the finished tile as [token][row]:
+    // scaled by xs[t] when it is the whole sum, the raw partial sum of this
+    // block's K range otherwise.
+    if (*sm.flag == 0) {
+      float* tile = reinterpret_cast<float*>(sm.a);
+      const int r_local = 32 * quad + lane;
+      const bool whole = a.splits == 1;
 #pragma unroll
-        for (int j = 0; j < kCols; ++j) {
-          const int t = t_base + j;
-          if (t < a.m) a.y[static_cast<size_t>(t) * a.d + row] = acc[j] * sm.xs[half * kCols + j];
-        }
-      }
-    } else if (good && row_ok) {
-      // this split's partial; splitk_reduce_kernel sums the splits in order
-      float* my_part = a.partial + static_cast<size_t>(split) * a.m * a.d;
-#pragma unroll
-      for (int j = 0; j < kCols; ++j) {
-        const int t = t_base + j;
-        if (t < a.m) my_part[static_cast<size_t>(t) * a.d + row] = acc[j];
+      for (int j = 0; j < kCols / 2; ++j) {
+        float v0, v1;
+        f2_unpack(acc[j], v0, v1);
+        const int c = half * kCols + 2 * j;
+        tile[c * kBM + r_local] = whole ? v0 * sm.xs[c] : v0;
+        tile[(c + 1) * kBM + r_local] = whole ? v1 * sm.xs[c + 1] : v1;
       }
     }
   }
+
+  // ---------------- output (every thread takes part in the barriers) ----------------
+  __syncwarp();
+  if (a.cluster > 1) cluster_sync(); else __syncthreads();
+  if (warp >= Shape<kBN>::kFirstEpiWarp) {
+    constexpr int kEpiThreads = Shape<kBN>::kEpiWarps * 32;
+    constexpr int kQuads = kBN * kBM / 4;  // float4s in the tile; 32 per token
+    const int et = static_cast<int>(threadIdx.x) - Shape<kBN>::kFirstEpiWarp * 32;
+    const uint32_t tile_s = smem_u32(sm.a);
+    if (a.cluster > 1) {
+      // Block `split` of the cluster sums its share of the tile over the
+      // cluster's partial tiles in split order (deterministic), scales by
+      // xs[t] and writes Y.
+      const int s = a.cluster;
+      bool all_good = true;
+      for (int p = 0; p < s; ++p) all_good &= ld_cluster_s32(cluster_peer(smem_u32(sm.flag), p)) == 0;
+      if (all_good) {
+        const int q0 = split * kQuads / s, q1 = (split + 1) * kQuads / s;
+        for (int q = q0 + et; q < q1; q += kEpiThreads) {
+          const int j = q >> 5, t = tok0 + j;
+          if (t >= a.m) continue;
+          float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int p = 0; p < s; ++p) {
+            const float4 u = ld_cluster_f4(cluster_peer(tile_s + 16u * q, p));
+            v.x += u.x;
+            v.y += u.y;
+            v.z += u.z;
+            v.w += u.w;
+          }
+          const float x = sm.xs[j];
+          store_out4(a.y, a, t, row0 + 4 * (q & 31), make_float4(v.x * x, v.y * x, v.z * x, v.w * x));
+        }
+      }
+    } else if (*sm.flag == 0) {
+      // the whole sum (splits == 1), or this split's partial, which
+      // splitk_reduce_kernel sums in split order
+      float* dst = a.splits == 1 ? a.y : a.partial + static_cast<size_t>(split) * a.m * a.d;
+      const float4* tile4 = reinterpret_cast<const float4*>(sm.a);
+      for (int q = et; q < kQuads; q += kEpiThreads) {
+        const int j = q >> 5, t = tok0 + j;
+        if (t < a.m) store_out4(dst, a, t, row0 + 4 * (q & 31), tile4[q]);
+      }
+    }
+  }
+  // no block leaves while the others may still read its tile
+  if (a.cluster > 1) cluster_sync();
 
   // Tensor memory is released by its owner warp once every role is done.
   tmem_fence_before();
@@ -459,38 +630,45 @@ __global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
 // the GEMM (programmatic dependent launch): the partials are read only after
 // griddepcontrol.wait.
 constexpr int kReduceThreads = 256;
-constexpr int kReduceElems = 4;  // consecutive outputs per thread
+constexpr int kReduceElems = 4;   // consecutive outputs per thread (one float4)
+constexpr int kReduceBatch = 8;   // splits whose loads are in flight at once
 
 __global__ void __launch_bounds__(kReduceThreads)
-    splitk_reduce_kernel(float* y, const float* partial, const float* xs, int splits, int m, int d) {
+    splitk_reduce_kernel(float* y, const float* partial, const float* xs, int splits, int m, int d, int vec4) {
   griddep_wait();
   const size_t md = static_cast<size_t>(m) * d;
   const size_t i0 = (static_cast<size_t>(blockIdx.x) * kReduceThreads + threadIdx.x) * kReduceElems;
   if (i0 >= md) return;
-  float v[kReduceElems];
+  float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (vec4 && i0 + kReduceElems <= md) {
+    // d % 4 == 0: the four outputs share a token
+    for (int s0 = 0; s0 < splits; s0 += kReduceBatch) {
+      float4 p[kReduceBatch];
 #pragma unroll
-  for (int e = 0; e < kReduceElems; ++e) v[e] = 0.f;
-  int s = 0;
-  for (; s + 4 <= splits; s += 4) {  // four splits' loads in flight
-    float p[4][kReduceElems];
+      for (int b = 0; b < kReduceBatch; ++b)
+        if (s0 + b < splits) p[b] = __ldcg(reinterpret_cast<const float4*>(partial + static_cast<size_t>(s0 + b) * md + i0));
 #pragma unroll
-    for (int b = 0; b < 4; ++b)
-#pragma unroll
-      for (int e = 0; e < kReduceElems; ++e)
-        p[b][e] = i0 + e < md ? __ldcg(partial + static_cast<size_t>(s + b) * md + i0 + e) : 0.f;
-#pragma unroll
-    for (int b = 0; b < 4; ++b)
-#pragma unroll
-      for (int e = 0; e < kReduceElems; ++e) v[e] += p[b][e];
+      for (int b = 0; b < kReduceBatch; ++b)
+        if (s0 + b < splits) {
+          v.x += p[b].x;
+          v.y += p[b].y;
+          v.z += p[b].z;
+          v.w += p[b].w;
+        }
+    }
+    const float x = __ldg(xs + i0 / d);
+    *reinterpret_cast<float4*>(y + i0) = make_float4(v.x * x, v.y * x, v.z * x, v.w * x);
+    return;
   }
-  for (; s < splits; ++s)
+  float e[kReduceElems] = {0.f, 0.f, 0.f, 0.f};
+  for (int sp = 0; sp < splits; ++sp)
 #pragma unroll
-    for (int e = 0; e < kReduceElems; ++e)
-      v[e] += i0 + e < md ? __ldcg(partial + static_cast<size_t>(s) * md + i0 + e) : 0.f;
+    for (int k = 0; k < kReduceElems; ++k)
+      if (i0 + k < md) e[k] += __ldcg(partial + static_cast<size_t>(sp) * md + i0 + k);
 #pragma unroll
-  for (int e = 0; e < kReduceElems; ++e) {
-    const size_t i = i0 + e;
-    if (i < md) y[i] = v[e] * __ldg(xs + i / d);
+  for (int k = 0; k < kReduceElems; ++k) {
+    const size_t i = i0 + k;
+    if (i < md) y[i] = e[k] * __ldg(xs + i / d);
   }
 }
 
@@ -526,37 +704,131 @@ bool make_map(CUtensorMap* map, const void* base, int rows, int cols, int box_ro
 
 struct Plan {
   int bn, tiles_m, tiles_n, splits, chunks;
+  int cluster;  // > 1: the splits of a tile form one cluster (no workspace)
 };
 
-Plan plan(int m, int n, int d, int sm_count, bool have_ws) {
+// K splits that fill the SMs in one wave, keeping at least two 128-byte chunks
+// (four groups) per split.
+Plan plan(int m, int n, int d, int sm_count) {
   Plan p;
   p.bn = m <= 16 ? 16 : (m <= 32 ? 32 : (m <= 64 ? 64 : 128));
   p.tiles_m = (d + kBM - 1) / kBM;
   p.tiles_n = (m + p.bn - 1) / p.bn;
   p.chunks = n / kChunk;
-  // Split K so the tiles fill the SMs in one wave, keeping at least two
-  // 128-byte chunks (four groups) per split.
   const int tiles = p.tiles_m * p.tiles_n;
-  int splits = have_ws ? sm_count / tiles : 1;
+  int splits = sm_count / tiles;
   if (splits > p.chunks / 2) splits = p.chunks / 2;
   if (splits < 1) splits = 1;
   p.splits = splits;
+  p.cluster = 1;
+  return p;
+}
+
+template <int kBN>
+cudaError_t prepare_bn() {
+  return ensure_dynamic_smem(reinterpret_cast<const void*>(gemm_w8a8_tc_kernel<kBN>), smem_bytes(kBN));
+}
+
+// How many clusters of `size` blocks of the kBN kernel the current device
+// runs at once (cached per device, tile width and size).
+constexpr int kMaxCluster = 16;
+constexpr int kMaxDevicesTc = 64;
+
+template <int kBN>
+int max_active_clusters(int device, int size) {
+  static std::mutex mu;
+  static int cache[kMaxDevicesTc][kMaxCluster + 1];
+  static bool init = false;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!init) {
+    for (auto& row : cache)
+      for (int& v : row) v = -1;
+    init = true;
+  }
+  if (device < 0 || device >= kMaxDevicesTc || size < 1 || size > kMaxCluster) return 0;
+  int& c = cache[device][size];
+  if (c >= 0) return c;
+  c = 0;
+  const void* fn = reinterpret_cast<const void*>(gemm_w8a8_tc_kernel<kBN>);
+  if (prepare_bn<kBN>() != cudaSuccess) return 0;
+  if (size > 8 && cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(size);
+  cfg.blockDim = dim3(Shape<kBN>::kThreads);
+  cfg.dynamicSmemBytes = smem_bytes(kBN);
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = size;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, gemm_w8a8_tc_kernel<kBN>, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  c = n;
+  return c;
+}
+
+int max_active_clusters_bn(int bn, int device, int size) {
+  switch (bn) {
+    case 16: return max_active_clusters<16>(device, size);
+    case 32: return max_active_clusters<32>(device, size);
+    case 64: return max_active_clusters<64>(device, size);
+    default: return max_active_clusters<128>(device, size);
+  }
+}
+
+// How the K splits of a tile are summed: inside a cluster over shared memory
+// (no second kernel) with the largest cluster size whose clusters all fit on
+// the GPU at once, or through the workspace with the split count that fills
+// the SMs and a second kernel.  The estimate behind the choice: a block's
+// time grows with its K chunks (about 0.9 us per 128-byte chunk at 128
+// tokens per tile, 0.5 us at 16-32 tokens on a B200), and the second kernel
+// with the launch gaps around it costs about 4.5 us.
+Plan choose(int m, int n, int d, const DeviceInfo& dev, bool have_ws) {
+  Plan p = plan(m, n, d, dev.sm_count);
+  const int want = p.splits;
+  const int tiles = p.tiles_m * p.tiles_n;
+  int s = (launch_flags() & MLI_LAUNCH_NO_CLUSTER) ? 1 : (want < kMaxCluster ? want : kMaxCluster);
+  while (s > 1 && max_active_clusters_bn(p.bn, dev.device, s) < tiles) --s;
+  bool cluster = s == want || !have_ws;
+  if (!cluster && s > 1) {
+    const double per_chunk_us = p.bn >= 128 ? 0.9 : (p.bn >= 64 ? 0.6 : 0.5);
+    const double t_cluster = ((p.chunks + s - 1) / s) * per_chunk_us;
+    const double t_ws = ((p.chunks + want - 1) / want) * per_chunk_us + 4.5;
+    cluster = t_cluster <= t_ws;
+  }
+  if (cluster) {
+    p.splits = s;
+    p.cluster = s;
+  }
   return p;
 }
 
 template <int kBN>
 cudaError_t launch_bn(const CUtensorMap& mw, const CUtensorMap& mx, const Args& a, int grid,
                       cudaStream_t stream) {
-  const uint32_t smem = smem_bytes(kBN);
-  cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(gemm_w8a8_tc_kernel<kBN>), smem);
+  cudaError_t e = prepare_bn<kBN>();
   if (e != cudaSuccess) return e;
-  return launch(gemm_w8a8_tc_kernel<kBN>, dim3(grid), dim3(Shape<kBN>::kThreads), smem, stream, true, mw, mx, a);
+  if (a.cluster > 8) {
+    e = cudaFuncSetAttribute(reinterpret_cast<const void*>(gemm_w8a8_tc_kernel<kBN>),
+                             cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
+  }
+  return launch_clustered(gemm_w8a8_tc_kernel<kBN>, dim3(grid), dim3(Shape<kBN>::kThreads), smem_bytes(kBN),
+                          stream, true, static_cast<unsigned>(a.cluster), mw, mx, a);
 }
 
 }  // namespace tc
 
 size_t gemm_tc_workspace_bytes(int m, int n, int d, int sm_count) {
-  const tc::Plan p = tc::plan(m, n, d, sm_count, true);
+  const tc::Plan p = tc::plan(m, n, d, sm_count);
   if (p.splits <= 1) return 256;
   return 256 + static_cast<size_t>(p.splits) * m * d * sizeof(float);
 }
@@ -572,7 +844,7 @@ int gemm_w8a8_tc(float* y, const int8_t* xq, const float* xs, const int8_t* w_q,
   if (err != cudaSuccess) return set_status(MLI_ERR_CUDA, err);
   const bool have_ws = workspace != nullptr &&
                        workspace_bytes >= gemm_tc_workspace_bytes(m, n, d, dev.sm_count);
-  const tc::Plan p = tc::plan(m, n, d, dev.sm_count, have_ws);
+  const tc::Plan p = tc::choose(m, n, d, dev, have_ws);
   CUtensorMap mw, mx;
   if (!tc::make_map(&mw, w_q, d, n, tc::kBM) || !tc::make_map(&mx, xq, m, n, p.bn))
     return MLI_ERR_UNSUPPORTED;
@@ -589,7 +861,10 @@ int gemm_w8a8_tc(float* y, const int8_t* xq, const float* xs, const int8_t* w_q,
   a.tiles_n = p.tiles_n;
   a.splits = p.splits;
   a.chunks = p.chunks;
-  if (p.splits > 1) a.partial = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + 256);
+  a.cluster = p.cluster;
+  const bool via_workspace = p.splits > 1 && p.cluster == 1;
+  if (via_workspace) a.partial = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + 256);
+  a.vec4 = d % 4 == 0 && aligned(y, 16) && (!via_workspace || aligned(a.partial, 16));
   const int grid = p.tiles_m * p.tiles_n * p.splits;
   switch (p.bn) {
     case 16: err = tc::launch_bn<16>(mw, mx, a, grid, stream); break;
@@ -597,15 +872,32 @@ int gemm_w8a8_tc(float* y, const int8_t* xq, const float* xs, const int8_t* w_q,
     case 64: err = tc::launch_bn<64>(mw, mx, a, grid, stream); break;
     default: err = tc::launch_bn<128>(mw, mx, a, grid, stream); break;
   }
-  if (err != cudaSuccess || p.splits == 1) return check_cuda(err);
+  if (err != cudaSuccess || !via_workspace) return check_cuda(err);
   const size_t per_block = static_cast<size_t>(tc::kReduceThreads) * tc::kReduceElems;
   const size_t md = static_cast<size_t>(m) * d;
   const unsigned blocks = static_cast<unsigned>((md + per_block - 1) / per_block);
   return check_cuda(launch(tc::splitk_reduce_kernel, dim3(blocks), dim3(tc::kReduceThreads), 0, stream, true,
-                           y, static_cast<const float*>(a.partial), xs, p.splits, m, d));
+                           y, static_cast<const float*>(a.partial), xs, p.splits, m, d, a.vec4));
 }
 
 }  // namespace mli
+
+extern "C" int mli_debug_plan_gemm(int m, int n, int d, size_t workspace_bytes, int* out) {
+  using namespace mli;
+  if (!out || m <= 0 || n <= 0 || d <= 0) return set_status(MLI_ERR_INVALID_ARG);
+  if (m < 16 || n % tc::kChunk != 0) return set_status(MLI_ERR_UNSUPPORTED);
+  cudaError_t err = cudaSuccess;
+  const DeviceInfo& dev = current_device(&err);
+  if (err != cudaSuccess) return set_status(MLI_ERR_CUDA, err);
+  const bool have_ws = workspace_bytes >= gemm_tc_workspace_bytes(m, n, d, dev.sm_count);
+  const tc::Plan p = tc::choose(m, n, d, dev, have_ws);
+  out[0] = p.bn;
+  out[1] = p.tiles_m * p.tiles_n;
+  out[2] = p.splits;
+  out[3] = p.cluster;
+  out[4] = p.splits > 1 && p.cluster == 1;
+  return set_status(MLI_OK);
+}
 
 // ---------------------------------------------------------------------------
 // Allocation-free batched W8A8 (mli_gemm_w8a8_noalloc)

@@ -36,25 +36,41 @@ unsigned launch_flags();
 // attribute when enabled, and returns the launch's cudaError_t.  Launches on
 // the legacy default stream (NULL), which the reference's forward pass uses,
 // never carry it: they keep the plain stream order of <<<>>> launches.
+// `cluster_x` > 1 groups consecutive blocks into thread-block clusters of
+// that many blocks along x (the grid must be a multiple of it).
 template <typename... KArgs, typename... Args>
-cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block,
-                   size_t smem, cudaStream_t stream, bool allow_pdl,
-                   Args&&... args) {
+cudaError_t launch_clustered(void (*kernel)(KArgs...), dim3 grid, dim3 block,
+                             size_t smem, cudaStream_t stream, bool allow_pdl,
+                             unsigned cluster_x, Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   cfg.attrs = attr;
   cfg.numAttrs = 0;
   if (allow_pdl && stream != nullptr && stream != cudaStreamLegacy &&
       (launch_flags() & MLI_LAUNCH_PDL)) {
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.numAttrs = 1;
+    attr[cfg.numAttrs].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[cfg.numAttrs].val.programmaticStreamSerializationAllowed = 1;
+    ++cfg.numAttrs;
+  }
+  if (cluster_x > 1) {
+    attr[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;
+    attr[cfg.numAttrs].val.clusterDim.x = cluster_x;
+    attr[cfg.numAttrs].val.clusterDim.y = 1;
+    attr[cfg.numAttrs].val.clusterDim.z = 1;
+    ++cfg.numAttrs;
   }
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block,
+                   size_t smem, cudaStream_t stream, bool allow_pdl,
+                   Args&&... args) {
+  return launch_clustered(kernel, grid, block, smem, stream, allow_pdl, 1u, std::forward<Args>(args)...);
 }
 
 // Raises the kernel's dynamic shared memory limit to at least `smem` bytes on

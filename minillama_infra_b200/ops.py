@@ -136,6 +136,15 @@ def set_pdl(enabled: bool) -> None:
     lib().mli_set_launch_flags(flags)
 
 
+def set_gemm_clusters(enabled: bool) -> None:
+    """Batched W8A8 split-K: sum the K splits of a tile inside a thread-block
+    cluster (default), or through the caller's workspace."""
+    from ._lib import MLI_LAUNCH_NO_CLUSTER
+    flags = lib().mli_get_launch_flags()
+    flags = (flags & ~MLI_LAUNCH_NO_CLUSTER) if enabled else (flags | MLI_LAUNCH_NO_CLUSTER)
+    lib().mli_set_launch_flags(flags)
+
+
 # Waits of a decode layer's GEMVs q, k, v, o, gate, up, down at chain index
 # b + 0..6, relative to b: o after q/k/v (attention), gate/up after o (residual
 # + norm), down after gate/up (SwiGLU); the next layer's q/k/v wait for down.

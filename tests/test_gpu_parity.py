@@ -235,6 +235,25 @@ def test_gemm_w8a8_tensor_core_parity(m, n, d, workspace):
     assert ops.device_error() == 0
 
 
+@pytest.mark.parametrize("m,n,d", [(16, 3072, 1024), (64, 3072, 3072), (256, 3072, 1024), (100, 8192, 384),
+                                   (300, 1024, 200), (17, 2048, 130)])
+def test_gemm_split_k_cluster_and_workspace_paths(m, n, d):
+    """The K splits of a tile summed inside a thread-block cluster (default)
+    and through the workspace (MLI_LAUNCH_NO_CLUSTER) both match the oracle,
+    and each path is deterministic."""
+    try:
+        for clusters in (True, False):
+            ops.set_gemm_clusters(clusters)
+            got, (xq, xs, tw, ts, ws) = _gemm_case(m, n, d, 3 * m + d, workspace=True)
+            y2 = torch.empty(m * d, dtype=torch.float32, device=dev())
+            ops.gemm_w8a8(y2, xq, xs, tw, ts, m, n, d, 64, workspace=ws)
+            torch.cuda.synchronize()
+            assert np.array_equal(y2.cpu().numpy().reshape(m, d).view(np.uint32), got.view(np.uint32))
+    finally:
+        ops.set_gemm_clusters(True)
+    assert ops.device_error() == 0
+
+
 def test_rows_are_independent_of_sharding():
     """Row r's result is bit-identical whether computed in the full matrix or
     in any row slice (the property the sharded classifier relies on)."""
