@@ -507,44 +507,54 @@ __global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
     if (et < kBN) sm.xs[et] = tok0 + et < a.m ? __ldg(a.xs + tok0 + et) : 0.f;
     cp_async_wait_all();
     epi_sync<kEpiWarps>();
-    // A buffer goes back to the MMA warp once this warp's bias refill of it
-    // has completed.
-    auto release = [&](int b) {
+    // Groups go in pairs (buffers 2k, 2k + 1): one wait for the MMAs and one
+    // release per pair.  A pair's buffers go back to the MMA warp once this
+    // warp's bias refill of them has completed.
+    auto release_pair = [&](int b) {
       tmem_wait_st();
       tmem_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.acc_empty[b]);
+      if (lane == 0) {
+        mbar_arrive(&sm.acc_empty[b]);
+        mbar_arrive(&sm.acc_empty[b + 1]);
+      }
     };
-    int pending = -1;  // buffer whose refill is in flight
+    const uint32_t tlane_acc = tmem + (static_cast<uint32_t>(32 * quad) << 16) + static_cast<uint32_t>(half * kCols);
+    int pending = -1;  // first buffer of the pair whose refill is in flight
     bool ok = true;
-    for (int gi = 0; gi < ngroups; ++gi) {
-      const int buf = gi % kAccBufs;
+    for (int gi = 0; gi < ngroups; gi += 2) {  // ngroups is even: two groups per chunk
+      const int buf = gi % kAccBufs;           // even
       if (gi > 0 && gi % kWsWin == 0) {
         epi_sync<kEpiWarps>();  // every epilogue thread is done with the previous window
         stage_scales(gi);
         cp_async_wait_all();
         epi_sync<kEpiWarps>();
       }
-      const float wsc = sm.ws[(32 * quad + lane) * kWsStride + gi % kWsWin];
+      const float* wrow = sm.ws + (32 * quad + lane) * kWsStride + gi % kWsWin;
       // After a timeout the warp keeps walking the groups without waiting, so
-      // that every epilogue warp meets the same window barriers.
-      if (ok && !mbar_wait_bounded(&sm.acc_full[buf], (gi / kAccBufs) & 1, kWaitLimitNs)) ok = false;
+      // that every epilogue warp meets the same window barriers.  The second
+      // group's commit also covers the first group's MMAs (a commit tracks
+      // every earlier MMA of the issuing thread).
+      if (ok && !mbar_wait_bounded(&sm.acc_full[buf + 1], ((gi + 1) / kAccBufs) & 1, kWaitLimitNs)) ok = false;
       if (!ok) continue;
       tmem_fence_after();
-      const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * quad) << 16) +
-                             static_cast<uint32_t>(buf * kBN + half * kCols);
-      // every column load in flight at once
-      uint32_t r[kCols];
-      tmem_ld_cols<kCols>(taddr, r);
-      if (pending >= 0) release(pending);  // the previous group's refill overlaps these loads
-      tmem_wait_ld();
-      const uint64_t w2 = f2_pack(__float_as_uint(wsc), __float_as_uint(wsc));
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {  // one group's registers live at a time
+        const uint32_t taddr = tlane_acc + static_cast<uint32_t>((buf + h) * kBN);
+        // every column load in flight at once
+        uint32_t r[kCols];
+        tmem_ld_cols<kCols>(taddr, r);
+        if (h == 0 && pending >= 0) release_pair(pending);  // the previous refills overlap these loads
+        tmem_wait_ld();
+        const float w = wrow[h];
+        const uint64_t w2 = f2_pack(__float_as_uint(w), __float_as_uint(w));
 #pragma unroll
-      for (int j = 0; j < kCols / 2; ++j) acc[j] = f2_unbias_fma(f2_pack(r[2 * j], r[2 * j + 1]), bias2, w2, acc[j]);
-      tmem_fill_bias<kCols>(taddr);  // ready for the buffer's next use
+        for (int j = 0; j < kCols / 2; ++j) acc[j] = f2_unbias_fma(f2_pack(r[2 * j], r[2 * j + 1]), bias2, w2, acc[j]);
+        tmem_fill_bias<kCols>(taddr);  // ready for the buffer's next use
+      }
       pending = buf;
     }
-    if (pending >= 0) release(pending);
+    if (pending >= 0) release_pair(pending);
     if (!ok) {
       record_device_error(kDevMmaTimeout);
       *sm.flag = 1;
