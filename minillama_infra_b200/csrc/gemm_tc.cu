@@ -29,11 +29,17 @@
 // wanted size do not fit the GPU at once, the splits may instead write their
 // partials into the caller's workspace, summed in split order by a second,
 // GPU-wide kernel.
+//
+// This file builds as a device module of its own (whole-program compilation,
+// no -rdc): only then does ptxas allocate the epilogue's registers up to its
+// setmaxnreg share.  Its kernels reach the library's device error word
+// through a pointer.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
 #include <mutex>
 
+#define MLI_SEPARATE_DEVICE_MODULE
 #include "mli_common.cuh"
 #include "mli_internal.h"
 
@@ -51,17 +57,31 @@ constexpr int kStageA = kBM * kChunk;  // 16 KB of weights per stage
 __host__ __device__ constexpr int stages_a(int bn) { return bn >= 128 ? 9 : (bn >= 64 ? 10 : 11); }
 __host__ __device__ constexpr int stages_b(int bn) { return bn >= 128 ? 3 : 4; }
 constexpr int kMaxStages = 11;
-// Warp 0 weight TMA, warp 1 MMA, warp 2 activation TMA, warps 3.. epilogue:
-// 4 lane quarters x kSlices token column slices (kCols columns each).  A warp
-// reads the tensor-memory lanes of its rank in the warpgroup (warp % 4).
+// Warpgroup 0: warp 0 weight TMA, warp 1 MMA, warp 2 activation TMA.
+// Warpgroups 1 and 2 are the epilogue, ping-ponging over pairs of
+// accumulator groups (pair p goes to warpgroup 1 + p % 2), so that one
+// warpgroup's tensor-memory loads, refills and waits overlap the other's
+// arithmetic.  Each epilogue warp covers every token column of the 32
+// accumulator lanes of its rank in the warpgroup (warp % 4).
 template <int kBN>
 struct Shape {
-  static constexpr int kSlices = 2;
-  static constexpr int kEpiWarps = 4 * kSlices;
-  static constexpr int kFirstEpiWarp = 3;
-  static constexpr int kThreads = (kEpiWarps + kFirstEpiWarp) * 32;
-  static constexpr int kCols = kBN / kSlices;
+  static constexpr int kEpiWarps = 8;
+  static constexpr int kFirstEpiWarp = 4;
+  static constexpr int kThreads = 12 * 32;
+  static constexpr int kCols = kBN;
+  static constexpr int kLdCols = 16;  // accumulator columns per tensor-memory load
+  // wide tiles keep 128 fp32 sums per epilogue thread: registers move from
+  // the producer warpgroup to the epilogue warpgroups
+  static constexpr bool kSplitRegs = kBN >= 64;
 };
+// Registers per thread after the setmaxnreg split: the producer warpgroup
+// gives up what its loops do not need, the epilogue warpgroups take it (the
+// fp32 sums of a whole lane row of the tile stay in registers).  The split
+// must fit the registers the block is launched with; launch_bn checks that
+// against the compiled kernel before the first launch.
+constexpr int kRegsProducer = 88;
+constexpr int kRegsEpilogue = 208;
+constexpr int kRegsBlock = 128 * (kRegsProducer + 2 * kRegsEpilogue);
 constexpr int kMaxAccBufs = 8;
 
 // Accumulator buffers per tile width: as many as tensor memory holds (512
@@ -79,7 +99,12 @@ struct Args {
   int tiles_m, tiles_n, splits, chunks;
   int cluster;           // > 1: the splits of a tile form one cluster and sum over shared memory
   int vec4;              // outputs may be written as aligned float4 (d % 4 == 0, 16-byte aligned)
+  unsigned int* err;     // the library's device error word
 };
+
+__device__ __forceinline__ void record_device_error(const Args& a, unsigned int code) {
+  if (a.err) atomicCAS(a.err, 0u, code);
+}
 
 // ---------------------------------------------------------------------------
 // PTX wrappers (tcgen05, TMA tensor loads)
@@ -186,19 +211,27 @@ __device__ __forceinline__ void tmem_wait_ld() {
 constexpr uint32_t kAccBias = 0x4B400000u;
 constexpr float kAccBiasF = 12582912.0f;  // 1.5 * 2^23
 
-// Fills this warp's 32 lanes x kCols columns at taddr with the bias.  Eight
-// columns per store: a store's source is as many consecutive registers as it
-// has columns, and eight registers of the bias stay live for the whole loop.
+// Fills this warp's 32 lanes x kCols columns at taddr with the bias: a store's
+// source is as many consecutive registers as it has columns, so 16 columns
+// per store keep 16 registers of the bias live (8 at 8 columns).
 template <int kCols>
 __device__ __forceinline__ void tmem_fill_bias(uint32_t taddr) {
-  static_assert(kCols % 8 == 0, "a multiple of 8 columns");
   const uint32_t b = kAccBias;
+  if constexpr (kCols % 16 == 0) {
 #pragma unroll
-  for (int q = 0; q < kCols / 8; ++q)
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr + 8 * q),
-                 "r"(b)
+    for (int q = 0; q < kCols / 16; ++q)
+      asm volatile(
+          "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(
+              taddr + 16 * q),
+          "r"(b)
+          : "memory");
+  } else {
+    static_assert(kCols == 8, "8 or a multiple of 16 columns");
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr), "r"(b)
                  : "memory");
+  }
 }
+
 __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
@@ -336,6 +369,31 @@ __device__ __forceinline__ Smem carve(unsigned char* raw, int bn) {
 __device__ __forceinline__ unsigned char* stage_a(const Smem& s, int i) { return s.a + i * kStageA; }
 __device__ __forceinline__ unsigned char* stage_b(const Smem& s, int i) { return s.b + i * s.b_stage; }
 
+// Stages the scales of groups g0 .. g0 + wn - 1 (wn = min(left, kWsWin)) of
+// the tile's rows, kThreads / kBM threads per row with every copy in flight
+// at once (waited for by the caller).
+template <int kThreads>
+__device__ __forceinline__ void stage_group_scales(float* ws_smem, const float* ws, int G, int d, int row0, int g0,
+                                                   int left, int et) {
+  const int wn = left < kWsWin ? left : kWsWin;
+  constexpr int kTpr = kThreads / kBM;  // threads per row
+  const int rl = et / kTpr, rr = row0 + rl;
+  float* dst = ws_smem + rl * kWsStride;
+  if (rr < d) {
+    const float* src = ws + static_cast<size_t>(rr) * G + g0;
+    for (int g = et % kTpr; g < wn; g += kTpr) cp_async4(dst + g, src + g);
+  } else {
+    for (int g = et % kTpr; g < wn; g += kTpr) dst[g] = 0.f;
+  }
+}
+
+// Every thread of the block, from the producer and the epilogue branches
+// alike (named barrier 2).
+template <int kThreads>
+__device__ __forceinline__ void block_sync() {
+  asm volatile("bar.sync 2, %0;" ::"n"(kThreads) : "memory");
+}
+
 template <int kEpiWarps>
 __device__ __forceinline__ void epi_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
@@ -376,7 +434,7 @@ __global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
     }
     for (int i = 0; i < kAccBufs; ++i) {
       mbar_init(&sm.acc_full[i], 1);
-      mbar_init(&sm.acc_empty[i], kEpiWarps);
+      mbar_init(&sm.acc_empty[i], 4);  // the four warps of the buffer's epilogue warpgroup
     }
     *sm.flag = 0;
     fence_barrier_init();
@@ -394,6 +452,8 @@ __global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
   const uint32_t tmem = *sm.tmem_base;
   griddep_launch_dependents();
 
+  if (warp < Shape<kBN>::kFirstEpiWarp) {
+  if constexpr (Shape<kBN>::kSplitRegs) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsProducer));
   if (warp == 0) {
     // ---------------- weight TMA ----------------
     // Weights never depend on the previous kernel: no griddepcontrol.wait.
@@ -401,7 +461,7 @@ __global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
       for (int c = 0; c < nchunks; ++c) {
         const int st = c % kSA;
         if (c >= kSA && !mbar_wait_bounded(&sm.empty_a[st], ((c / kSA) - 1) & 1, kWaitLimitNs)) {
-          record_device_error(kDevMmaTimeout);
+          record_device_error(a, kDevMmaTimeout);
           *sm.flag = 1;
           break;
         }
@@ -416,7 +476,7 @@ __global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
       for (int c = 0; c < nchunks; ++c) {
         const int st = c % kSB;
         if (c >= kSB && !mbar_wait_bounded(&sm.empty_b[st], ((c / kSB) - 1) & 1, kWaitLimitNs)) {
-          record_device_error(kDevMmaTimeout);
+          record_device_error(a, kDevMmaTimeout);
           *sm.flag = 1;
           break;
         }
@@ -462,43 +522,45 @@ __global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
         mma_commit(&sm.empty_b[sb]);
       }
       if (!ok) {
-        record_device_error(kDevMmaTimeout);
+        record_device_error(a, kDevMmaTimeout);
         *sm.flag = 1;
       }
     }
+  }
+    // the output barriers of the epilogue branch, in the same order
+    __syncwarp();
+    if (a.cluster > 1) {
+      cluster_sync();
+      cluster_sync();
+    } else {
+      block_sync<Shape<kBN>::kThreads>();
+    }
   } else {
-    // ---------------- epilogue ----------------
-    const int quad = warp & 3;                 // TMEM lanes 32*quad .. +31
-    const int half = (warp - Shape<kBN>::kFirstEpiWarp) >> 2;  // token column slice [half*kCols, +kCols)
+    if constexpr (Shape<kBN>::kSplitRegs) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsEpilogue));
+    // ---------------- epilogue (two warpgroups) ----------------
+    const int quad = warp & 3;                                     // TMEM lanes 32*quad .. +31
+    const int role = (warp - Shape<kBN>::kFirstEpiWarp) >> 2;      // pairs p with p % 2 == role
     constexpr int kCols = Shape<kBN>::kCols;
+    constexpr int kLd = Shape<kBN>::kLdCols;
     uint64_t acc[kCols / 2];  // fp32 pairs: columns 2j, 2j + 1
 #pragma unroll
     for (int j = 0; j < kCols / 2; ++j) acc[j] = 0;
     const uint64_t bias2 = f2_pack(__float_as_uint(kAccBiasF), __float_as_uint(kAccBiasF));
     const int et = static_cast<int>(threadIdx.x) - Shape<kBN>::kFirstEpiWarp * 32;  // epilogue thread
-    // every accumulator buffer starts at the bias
-    const uint32_t tlane = tmem + (static_cast<uint32_t>(32 * quad) << 16) + static_cast<uint32_t>(half * kCols);
-#pragma unroll
-    for (int b = 0; b < kAccBufs; ++b) tmem_fill_bias<kCols>(tlane + static_cast<uint32_t>(b * kBN));
+    const uint32_t tl = tmem + (static_cast<uint32_t>(32 * quad) << 16);
+    // Buffer b always belongs to warpgroup (b / 2) % 2 (pairs alternate and
+    // the buffer count is a multiple of four); each starts at the bias.
+#pragma unroll 1
+    for (int b = 0; b < kAccBufs; ++b)
+      if (((b >> 1) & 1) == role) tmem_fill_bias<kCols>(tl + static_cast<uint32_t>(b * kBN));
     tmem_wait_st();
     tmem_fence_before();
     __syncwarp();
     if (lane == 0)
-      for (int b = 0; b < kAccBufs; ++b) mbar_arrive(&sm.acc_empty[b]);
-    // Stages the scales of groups g0 .. g0 + wn - 1 of the tile's rows, two
-    // threads per row with every copy in flight at once (waited for by the
-    // caller).
+      for (int b = 0; b < kAccBufs; ++b)
+        if (((b >> 1) & 1) == role) mbar_arrive(&sm.acc_empty[b]);
     auto stage_scales = [&](int g0) {
-      const int wn = ngroups - g0 < kWsWin ? ngroups - g0 : kWsWin;
-      constexpr int kTpr = kEpiWarps * 32 / kBM;  // threads per row
-      const int rl = et / kTpr, rr = row0 + rl;
-      float* dst = sm.ws + rl * kWsStride;
-      if (rr < a.d) {
-        const float* src = a.ws + static_cast<size_t>(rr) * a.G + 2 * c_begin + g0;
-        for (int g = et % kTpr; g < wn; g += kTpr) cp_async4(dst + g, src + g);
-      } else {
-        for (int g = et % kTpr; g < wn; g += kTpr) dst[g] = 0.f;
-      }
+      stage_group_scales<kEpiWarps * 32>(sm.ws, a.ws, a.G, a.d, row0, 2 * c_begin + g0, ngroups - g0, et);
     };
     // The first window is weight data (no dependency on the previous
     // kernel); xs and the outputs belong to the stream order.
@@ -507,85 +569,94 @@ __global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
     if (et < kBN) sm.xs[et] = tok0 + et < a.m ? __ldg(a.xs + tok0 + et) : 0.f;
     cp_async_wait_all();
     epi_sync<kEpiWarps>();
-    // Groups go in pairs (buffers 2k, 2k + 1): one wait for the MMAs and one
-    // release per pair.  A pair's buffers go back to the MMA warp once this
-    // warp's bias refill of them has completed.
-    auto release_pair = [&](int b) {
-      tmem_wait_st();
-      tmem_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&sm.acc_empty[b]);
-        mbar_arrive(&sm.acc_empty[b + 1]);
-      }
-    };
-    const uint32_t tlane_acc = tmem + (static_cast<uint32_t>(32 * quad) << 16) + static_cast<uint32_t>(half * kCols);
-    int pending = -1;  // first buffer of the pair whose refill is in flight
     bool ok = true;
-    for (int gi = 0; gi < ngroups; gi += 2) {  // ngroups is even: two groups per chunk
-      const int buf = gi % kAccBufs;           // even
-      if (gi > 0 && gi % kWsWin == 0) {
-        epi_sync<kEpiWarps>();  // every epilogue thread is done with the previous window
-        stage_scales(gi);
+    for (int w0 = 0; w0 < ngroups; w0 += kWsWin) {  // windows of group scales (kWsWin % 4 == 0)
+      if (w0 > 0) {
+        epi_sync<kEpiWarps>();  // both warpgroups are done with the previous window
+        stage_scales(w0);
         cp_async_wait_all();
         epi_sync<kEpiWarps>();
       }
-      const float* wrow = sm.ws + (32 * quad + lane) * kWsStride + gi % kWsWin;
-      // After a timeout the warp keeps walking the groups without waiting, so
-      // that every epilogue warp meets the same window barriers.  The second
-      // group's commit also covers the first group's MMAs (a commit tracks
-      // every earlier MMA of the issuing thread).
-      if (ok && !mbar_wait_bounded(&sm.acc_full[buf + 1], ((gi + 1) / kAccBufs) & 1, kWaitLimitNs)) ok = false;
-      if (!ok) continue;
-      tmem_fence_after();
+      const int wend = ngroups - w0 < kWsWin ? ngroups : w0 + kWsWin;
+      // this warpgroup's pairs of the window (groups gi, gi + 1 in buffers
+      // buf, buf + 1); after a timeout the warp keeps walking the windows
+      // without waiting, so that both warpgroups meet the same barriers
+      for (int gi = w0 + 2 * role; gi < wend; gi += 4) {
+        const int buf = gi % kAccBufs;  // even
+        const float* wrow = sm.ws + (32 * quad + lane) * kWsStride + (gi - w0);
+        // The second group's commit also covers the first group's MMAs (a
+        // commit tracks every earlier MMA of the issuing thread).
+        if (ok && !mbar_wait_bounded(&sm.acc_full[buf + 1], ((gi + 1) / kAccBufs) & 1, kWaitLimitNs)) ok = false;
+        if (!ok) continue;
+        tmem_fence_after();
 #pragma unroll 1
-      for (int h = 0; h < 2; ++h) {  // one group's registers live at a time
-        const uint32_t taddr = tlane_acc + static_cast<uint32_t>((buf + h) * kBN);
-        // every column load in flight at once
-        uint32_t r[kCols];
-        tmem_ld_cols<kCols>(taddr, r);
-        if (h == 0 && pending >= 0) release_pair(pending);  // the previous refills overlap these loads
-        tmem_wait_ld();
-        const float w = wrow[h];
-        const uint64_t w2 = f2_pack(__float_as_uint(w), __float_as_uint(w));
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t taddr = tl + static_cast<uint32_t>((buf + h) * kBN);
+          const float w = wrow[h];
+          const uint64_t w2 = f2_pack(__float_as_uint(w), __float_as_uint(w));
 #pragma unroll
-        for (int j = 0; j < kCols / 2; ++j) acc[j] = f2_unbias_fma(f2_pack(r[2 * j], r[2 * j + 1]), bias2, w2, acc[j]);
-        tmem_fill_bias<kCols>(taddr);  // ready for the buffer's next use
+          for (int q = 0; q < kCols / kLd; ++q) {
+            uint32_t r[kLd];
+            tmem_ld16(taddr + kLd * q, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < kLd / 2; ++j)
+              acc[q * (kLd / 2) + j] = f2_unbias_fma(f2_pack(r[2 * j], r[2 * j + 1]), bias2, w2, acc[q * (kLd / 2) + j]);
+          }
+          tmem_fill_bias<kCols>(taddr);  // ready for the buffer's next use
+        }
+        // both buffers go back to the MMA warp once their refill has completed
+        tmem_wait_st();
+        tmem_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&sm.acc_empty[buf]);
+          mbar_arrive(&sm.acc_empty[buf + 1]);
+        }
       }
-      pending = buf;
     }
-    if (pending >= 0) release_pair(pending);
     if (!ok) {
-      record_device_error(kDevMmaTimeout);
+      record_device_error(a, kDevMmaTimeout);
       *sm.flag = 1;
     }
     epi_sync<kEpiWarps>();
     // Every load has landed and every MMA that read the weight ring has
-    // completed, so the ring takes the finished tile as [token][row]:
-    // scaled by xs[t] when it is the whole sum, the raw partial sum of this
-    // block's K range otherwise.
-    if (*sm.flag == 0) {
-      float* tile = reinterpret_cast<float*>(sm.a);
-      const int r_local = 32 * quad + lane;
+    // completed, so the ring takes the finished tile as [token][row]: the
+    // two warpgroups' sums added in a fixed order (warpgroup 1, then 2),
+    // scaled by xs[t] when the tile is the whole sum, the raw partial sum of
+    // this block's K range otherwise.
+    const bool good = *sm.flag == 0;
+    float* tile = reinterpret_cast<float*>(sm.a);
+    const int r_local = 32 * quad + lane;
+    if (good && role == 0) {
+#pragma unroll
+      for (int j = 0; j < kCols / 2; ++j) {
+        float v0, v1;
+        f2_unpack(acc[j], v0, v1);
+        tile[(2 * j) * kBM + r_local] = v0;
+        tile[(2 * j + 1) * kBM + r_local] = v1;
+      }
+    }
+    epi_sync<kEpiWarps>();
+    if (good && role == 1) {
       const bool whole = a.splits == 1;
 #pragma unroll
       for (int j = 0; j < kCols / 2; ++j) {
         float v0, v1;
         f2_unpack(acc[j], v0, v1);
-        const int c = half * kCols + 2 * j;
-        tile[c * kBM + r_local] = whole ? v0 * sm.xs[c] : v0;
-        tile[(c + 1) * kBM + r_local] = whole ? v1 * sm.xs[c + 1] : v1;
+        float* t0 = tile + (2 * j) * kBM + r_local;
+        float* t1 = tile + (2 * j + 1) * kBM + r_local;
+        const float s0 = *t0 + v0, s1 = *t1 + v1;
+        *t0 = whole ? s0 * sm.xs[2 * j] : s0;
+        *t1 = whole ? s1 * sm.xs[2 * j + 1] : s1;
       }
     }
-  }
 
-  // ---------------- output (every thread takes part in the barriers) ----------------
-  __syncwarp();
-  if (a.cluster > 1) cluster_sync(); else __syncthreads();
-  if (warp >= Shape<kBN>::kFirstEpiWarp) {
+    // ---------------- output (every thread of the block takes part in the barriers) ----------------
+    __syncwarp();
+    if (a.cluster > 1) cluster_sync(); else block_sync<Shape<kBN>::kThreads>();
     constexpr int kEpiThreads = Shape<kBN>::kEpiWarps * 32;
     constexpr int kQuads = kBN * kBM / 4;  // float4s in the tile; 32 per token
-    const int et = static_cast<int>(threadIdx.x) - Shape<kBN>::kFirstEpiWarp * 32;
     const uint32_t tile_s = smem_u32(sm.a);
     if (a.cluster > 1) {
       // Block `split` of the cluster sums its share of the tile over the
@@ -621,9 +692,9 @@ __global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
         if (t < a.m) store_out4(dst, a, t, row0 + 4 * (q & 31), tile4[q]);
       }
     }
+    // no block leaves while the others may still read its tile
+    if (a.cluster > 1) cluster_sync();
   }
-  // no block leaves while the others may still read its tile
-  if (a.cluster > 1) cluster_sync();
 
   // Tensor memory is released by its owner warp once every role is done.
   tmem_fence_before();
@@ -821,9 +892,26 @@ Plan choose(int m, int n, int d, const DeviceInfo& dev, bool have_ws) {
   return p;
 }
 
+// The setmaxnreg split must fit the registers the block is launched with:
+// an increase beyond them would wait forever.  Checked once per kernel
+// against the compiled register count.
+template <int kBN>
+bool register_split_fits() {
+  static const bool fits = []() {
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, gemm_w8a8_tc_kernel<kBN>) != cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    return !Shape<kBN>::kSplitRegs || fa.numRegs * Shape<kBN>::kThreads >= kRegsBlock;
+  }();
+  return fits;
+}
+
 template <int kBN>
 cudaError_t launch_bn(const CUtensorMap& mw, const CUtensorMap& mx, const Args& a, int grid,
                       cudaStream_t stream) {
+  if (!register_split_fits<kBN>()) return cudaErrorInvalidConfiguration;
   cudaError_t e = prepare_bn<kBN>();
   if (e != cudaSuccess) return e;
   if (a.cluster > 8) {
@@ -872,6 +960,7 @@ int gemm_w8a8_tc(float* y, const int8_t* xq, const float* xs, const int8_t* w_q,
   a.splits = p.splits;
   a.chunks = p.chunks;
   a.cluster = p.cluster;
+  a.err = device_error_word();
   const bool via_workspace = p.splits > 1 && p.cluster == 1;
   if (via_workspace) a.partial = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + 256);
   a.vec4 = d % 4 == 0 && aligned(y, 16) && (!via_workspace || aligned(a.partial, 16));

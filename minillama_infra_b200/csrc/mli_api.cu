@@ -21,6 +21,18 @@ std::once_flag g_device_once[kMaxDevices];
 cudaError_t g_device_err[kMaxDevices];
 }  // namespace
 
+unsigned int* device_error_word() {
+  static std::once_flag once[kMaxDevices];
+  static unsigned int* addr[kMaxDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::call_once(once[dev], [dev]() {
+    void* p = nullptr;
+    addr[dev] = cudaGetSymbolAddress(&p, g_device_error) == cudaSuccess ? static_cast<unsigned int*>(p) : nullptr;
+  });
+  return addr[dev];
+}
+
 int set_status(int status, cudaError_t err) {
   t_last_status = status;
   if (status == MLI_ERR_CUDA) t_last_cuda = static_cast<int>(err);

@@ -21,7 +21,9 @@ enum DeviceError : unsigned int {
   kDevPeerTimeout = 3,   // rows of a row-sharded step never arrived from a rank
   kDevChainTimeout = 4,  // a chained GEMV's inputs were never completed
 };
+#ifndef MLI_SEPARATE_DEVICE_MODULE
 extern __device__ unsigned int g_device_error;
+#endif
 
 // Row-sharded layers (gemv_g64.cu, rowshard.cu): at most this many ranks and
 // CTAs per rank.  Each rank's logits buffer ([2][d_total] fp32) is followed,
@@ -42,9 +44,11 @@ __host__ __device__ constexpr size_t rowshard_block_bytes(int d_total) {
          sizeof(int2) * 2 * kMaxPeers * kMaxRankCtas;
 }
 
+#ifndef MLI_SEPARATE_DEVICE_MODULE
 __device__ __forceinline__ void record_device_error(unsigned int code) {
   atomicCAS(&g_device_error, 0u, code);
 }
+#endif
 
 __device__ __forceinline__ uint64_t global_timer_ns() {
   uint64_t t;

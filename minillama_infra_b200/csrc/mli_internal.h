@@ -32,6 +32,11 @@ const DeviceInfo& current_device(cudaError_t* err);
 // Launch-time options (MLI_LAUNCH_* bits).
 unsigned launch_flags();
 
+// Device address of the library's error word on the current device, for
+// kernels of a translation unit built as its own device module (they cannot
+// name the symbol); nullptr if the lookup failed.
+unsigned int* device_error_word();
+
 // cudaLaunchKernelEx wrapper: adds the programmatic-dependent-launch
 // attribute when enabled, and returns the launch's cudaError_t.  Launches on
 // the legacy default stream (NULL), which the reference's forward pass uses,
