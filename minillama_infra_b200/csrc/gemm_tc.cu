@@ -50,18 +50,17 @@ namespace tc {
 constexpr int kBM = 128;             // weight rows per tile (UMMA M); a token's tile row is 32 float4s
 constexpr int kChunk = 128;          // K bytes per stage (one 128-byte swizzle atom)
 constexpr int kStageA = kBM * kChunk;  // 16 KB of weights per stage
-// Weight stages stream from HBM and need many bytes in flight per SM;
-// activation stages (bn x 128 bytes) are re-read from L2 by every row tile
-// and need few.  Two rings, each with its own producer warp, keep most of
-// shared memory on the weight stream.
-__host__ __device__ constexpr int stages_a(int bn) { return bn >= 128 ? 9 : (bn >= 64 ? 10 : 11); }
-__host__ __device__ constexpr int stages_b(int bn) { return bn >= 128 ? 3 : 4; }
-constexpr int kMaxStages = 11;
-// Warpgroup 0: warp 0 weight TMA, warp 1 MMA, warp 2 activation TMA.
-// Warpgroups 1 and 2 are the epilogue, ping-ponging over pairs of
-// accumulator groups (pair p goes to warpgroup 1 + p % 2), so that one
-// warpgroup's tensor-memory loads, refills and waits overlap the other's
-// arithmetic.  Each epilogue warp covers every token column of the 32
+// A stage holds one 128-byte K chunk of the weight tile (16 KB) and of the
+// activation tile (bn x 128 B); 192 KB of stages.
+__host__ __device__ constexpr uint32_t stage_bytes(int bn) { return kStageA + static_cast<uint32_t>(bn) * kChunk; }
+__host__ __device__ constexpr int stages(int bn) {
+  return 196608u / stage_bytes(bn) < 12u ? static_cast<int>(196608u / stage_bytes(bn)) : 12;
+}
+constexpr int kMaxStages = 12;
+// Warpgroup 0: warp 0 TMA, warp 1 MMA (warps 2 and 3 idle).  Warpgroups 1
+// and 2 are the epilogue, ping-ponging over the K chunks (the two groups of
+// chunk c go to warpgroup 1 + c % 2), so that one warpgroup's tensor-memory
+// loads, refills and waits overlap the other's arithmetic.  Each epilogue warp covers every token column of the 32
 // accumulator lanes of its rank in the warpgroup (warp % 4).
 template <int kBN>
 struct Shape {
@@ -83,6 +82,7 @@ constexpr int kRegsProducer = 88;
 constexpr int kRegsEpilogue = 208;
 constexpr int kRegsBlock = 128 * (kRegsProducer + 2 * kRegsEpilogue);
 constexpr int kMaxAccBufs = 8;
+constexpr int kMaxAccPairs = kMaxAccBufs / 2;  // a chunk's two groups fill one pair of buffers
 
 // Accumulator buffers per tile width: as many as tensor memory holds (512
 // columns), at most 8, so the MMAs run up to that many groups ahead of the
@@ -302,18 +302,15 @@ __device__ __forceinline__ void store_out4(float* dst, const Args& a, int t, int
 }
 
 // ---------------------------------------------------------------------------
-// Shared memory (1024-byte aligned): the weight ring, the activation ring,
+// Shared memory (1024-byte aligned): the ring of stages,
 // the barriers, the group-scale window and the token scales.
 // ---------------------------------------------------------------------------
 struct Smem {
-  unsigned char* a;      // weight stage i at a + i * kStageA
-  unsigned char* b;      // activation stage i at b + i * b_stage
-  uint32_t b_stage;
-  uint64_t* full_a;
-  uint64_t* empty_a;
-  uint64_t* full_b;
-  uint64_t* empty_b;
-  uint64_t* acc_full;
+  unsigned char* ring;   // stage i at ring + i * stage: weights, then activations
+  uint32_t stage;
+  uint64_t* full;
+  uint64_t* empty;
+  uint64_t* acc_full;    // per pair of accumulator buffers
   uint64_t* acc_empty;
   uint32_t* tmem_base;
   int* flag;
@@ -330,44 +327,38 @@ constexpr int kWsStride = kWsWin + 1;
 constexpr uint32_t kWsBytes = kBM * kWsStride * 4u;
 constexpr uint32_t kBarBytes = 512u;
 
-__host__ __device__ constexpr uint32_t b_stage_bytes(int bn) { return static_cast<uint32_t>(bn) * kChunk; }
-__host__ __device__ constexpr uint32_t rings_bytes(int bn) {
-  return stages_a(bn) * static_cast<uint32_t>(kStageA) + stages_b(bn) * b_stage_bytes(bn);
-}
+__host__ __device__ constexpr uint32_t rings_bytes(int bn) { return stages(bn) * stage_bytes(bn); }
 __host__ __device__ constexpr uint32_t smem_bytes(int bn) {
   return 1024u /* alignment slack */ + rings_bytes(bn) + kBarBytes + kWsBytes + 512u /* xs */;
 }
 static_assert(smem_bytes(128) <= 232448 && smem_bytes(64) <= 232448 && smem_bytes(32) <= 232448 &&
                   smem_bytes(16) <= 232448,
               "shared memory per block");
-static_assert((4 * kMaxStages + 16) * 8 + 8 <= kBarBytes, "barrier area");
-// the finished tile ([bn][kBM] fp32) is staged in the weight ring
-static_assert(128 * kBM * 4 <= stages_a(128) * kStageA && 64 * kBM * 4 <= stages_a(64) * kStageA &&
-                  32 * kBM * 4 <= stages_a(32) * kStageA && 16 * kBM * 4 <= stages_a(16) * kStageA,
-              "output tile in the weight ring");
+static_assert((2 * kMaxStages + 2 * kMaxAccPairs) * 8 + 8 <= kBarBytes, "barrier area");
+// the finished tile ([bn][kBM] fp32) is staged in the ring
+static_assert(128 * kBM * 4 <= rings_bytes(128) && 64 * kBM * 4 <= rings_bytes(64) &&
+                  32 * kBM * 4 <= rings_bytes(32) && 16 * kBM * 4 <= rings_bytes(16),
+              "output tile in the ring");
 
 __device__ __forceinline__ Smem carve(unsigned char* raw, int bn) {
   Smem s;
   unsigned char* base = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(raw) + 1023u) & ~static_cast<uintptr_t>(1023u));
-  s.a = base;
-  s.b = base + stages_a(bn) * kStageA;
-  s.b_stage = b_stage_bytes(bn);
+  s.ring = base;
+  s.stage = stage_bytes(bn);
   uint64_t* bars = reinterpret_cast<uint64_t*>(base + rings_bytes(bn));
-  s.full_a = bars;
-  s.empty_a = bars + kMaxStages;
-  s.full_b = bars + 2 * kMaxStages;
-  s.empty_b = bars + 3 * kMaxStages;
-  s.acc_full = bars + 4 * kMaxStages;
-  s.acc_empty = bars + 4 * kMaxStages + kMaxAccBufs;
-  s.tmem_base = reinterpret_cast<uint32_t*>(bars + 4 * kMaxStages + 2 * kMaxAccBufs);
+  s.full = bars;
+  s.empty = bars + kMaxStages;
+  s.acc_full = bars + 2 * kMaxStages;
+  s.acc_empty = bars + 2 * kMaxStages + kMaxAccPairs;
+  s.tmem_base = reinterpret_cast<uint32_t*>(bars + 2 * kMaxStages + 2 * kMaxAccPairs);
   s.flag = reinterpret_cast<int*>(s.tmem_base + 1);
   s.ws = reinterpret_cast<float*>(base + rings_bytes(bn) + kBarBytes);
   s.xs = s.ws + kBM * kWsStride;
   return s;
 }
-__device__ __forceinline__ unsigned char* stage_a(const Smem& s, int i) { return s.a + i * kStageA; }
-__device__ __forceinline__ unsigned char* stage_b(const Smem& s, int i) { return s.b + i * s.b_stage; }
+__device__ __forceinline__ unsigned char* stage_a(const Smem& s, int i) { return s.ring + i * s.stage; }
+__device__ __forceinline__ unsigned char* stage_b(const Smem& s, int i) { return s.ring + i * s.stage + kStageA; }
 
 // Stages the scales of groups g0 .. g0 + wn - 1 (wn = min(left, kWsWin)) of
 // the tile's rows, kThreads / kBM threads per row with every copy in flight
@@ -420,21 +411,18 @@ __global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
   const int ngroups = 2 * nchunks;
   constexpr int kAccBufs = acc_bufs(kBN);
   constexpr int kEpiWarps = Shape<kBN>::kEpiWarps;
-  constexpr int kSA = stages_a(kBN), kSB = stages_b(kBN);
+  constexpr int kS = stages(kBN);
+  constexpr int kPairs = kAccBufs / 2;
   constexpr uint32_t kTmemCols = kAccBufs * kBN;  // 128, 256 or 512: a power of two
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kSA; ++i) {
-      mbar_init(&sm.full_a[i], 1);
-      mbar_init(&sm.empty_a[i], 1);
+    for (int i = 0; i < kS; ++i) {
+      mbar_init(&sm.full[i], 1);
+      mbar_init(&sm.empty[i], 1);
     }
-    for (int i = 0; i < kSB; ++i) {
-      mbar_init(&sm.full_b[i], 1);
-      mbar_init(&sm.empty_b[i], 1);
-    }
-    for (int i = 0; i < kAccBufs; ++i) {
+    for (int i = 0; i < kPairs; ++i) {
       mbar_init(&sm.acc_full[i], 1);
-      mbar_init(&sm.acc_empty[i], 4);  // the four warps of the buffer's epilogue warpgroup
+      mbar_init(&sm.acc_empty[i], 4);  // the four warps of the pair's epilogue warpgroup
     }
     *sm.flag = 0;
     fence_barrier_init();
@@ -455,71 +443,63 @@ __global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
   if (warp < Shape<kBN>::kFirstEpiWarp) {
   if constexpr (Shape<kBN>::kSplitRegs) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsProducer));
   if (warp == 0) {
-    // ---------------- weight TMA ----------------
-    // Weights never depend on the previous kernel: no griddepcontrol.wait.
+    // ---------------- TMA producer ----------------
     if (lane == 0) {
-      for (int c = 0; c < nchunks; ++c) {
-        const int st = c % kSA;
-        if (c >= kSA && !mbar_wait_bounded(&sm.empty_a[st], ((c / kSA) - 1) & 1, kWaitLimitNs)) {
-          record_device_error(a, kDevMmaTimeout);
-          *sm.flag = 1;
-          break;
-        }
-        mbar_arrive_expect_tx(&sm.full_a[st], kStageA);
-        tma_load_2d(stage_a(sm, st), &map_w, (c_begin + c) * kChunk, row0, &sm.full_a[st]);
+      // Weights never depend on the previous kernel: fill the ring's weight
+      // halves first, then wait for the activations.
+      const int first = nchunks < kS ? nchunks : kS;
+      for (int c = 0; c < first; ++c) {
+        mbar_arrive_expect_tx(&sm.full[c], stage_bytes(kBN));
+        tma_load_2d(stage_a(sm, c), &map_w, (c_begin + c) * kChunk, row0, &sm.full[c]);
       }
-    }
-  } else if (warp == 2) {
-    // ---------------- activation TMA ----------------
-    if (lane == 0) {
       griddep_wait();
-      for (int c = 0; c < nchunks; ++c) {
-        const int st = c % kSB;
-        if (c >= kSB && !mbar_wait_bounded(&sm.empty_b[st], ((c / kSB) - 1) & 1, kWaitLimitNs)) {
+      for (int c = 0; c < first; ++c) tma_load_2d(stage_b(sm, c), &map_x, (c_begin + c) * kChunk, tok0, &sm.full[c]);
+      for (int c = kS; c < nchunks; ++c) {
+        const int st = c % kS;
+        if (!mbar_wait_bounded(&sm.empty[st], ((c / kS) - 1) & 1, kWaitLimitNs)) {
           record_device_error(a, kDevMmaTimeout);
           *sm.flag = 1;
           break;
         }
-        mbar_arrive_expect_tx(&sm.full_b[st], b_stage_bytes(kBN));
-        tma_load_2d(stage_b(sm, st), &map_x, (c_begin + c) * kChunk, tok0, &sm.full_b[st]);
+        mbar_arrive_expect_tx(&sm.full[st], stage_bytes(kBN));
+        const int kx = (c_begin + c) * kChunk;
+        tma_load_2d(stage_a(sm, st), &map_w, kx, row0, &sm.full[st]);
+        tma_load_2d(stage_b(sm, st), &map_x, kx, tok0, &sm.full[st]);
       }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
+    // Per chunk: one wait for its stage, one for its pair of accumulator
+    // buffers, four MMAs (two K=32 steps per group), one commit for the
+    // pair and one for the stage.
     if (lane == 0) {
       const uint32_t idesc = i8_idesc(kBN);
-      int gi = 0;
       bool ok = true;
-      for (int c = 0; c < nchunks && ok; ++c) {
-        const int sa = c % kSA, sb = c % kSB;
-        if (!mbar_wait_bounded(&sm.full_a[sa], (c / kSA) & 1, kWaitLimitNs) ||
-            !mbar_wait_bounded(&sm.full_b[sb], (c / kSB) & 1, kWaitLimitNs)) {
+      for (int c = 0; c < nchunks; ++c) {
+        const int st = c % kS, pb = c % kPairs;
+        // use u of a pair waits for phase u: the epilogue's bias fill
+        // (phase 0) or its read of use u - 1
+        if (!mbar_wait_bounded(&sm.full[st], (c / kS) & 1, kWaitLimitNs) ||
+            !mbar_wait_bounded(&sm.acc_empty[pb], (c / kPairs) & 1, kWaitLimitNs)) {
           ok = false;
           break;
         }
         tmem_fence_after();
-        const uint32_t a_base = smem_u32(stage_a(sm, sa));
-        const uint32_t b_base = smem_u32(stage_b(sm, sb));
-        for (int g = 0; g < 2; ++g, ++gi) {
-          const int buf = gi % kAccBufs;
-          // use u of a buffer waits for phase u: the epilogue's bias fill
-          // (phase 0) or its read of use u - 1
-          if (!mbar_wait_bounded(&sm.acc_empty[buf], (gi / kAccBufs) & 1, kWaitLimitNs)) {
-            ok = false;
-            break;
-          }
-          tmem_fence_after();
-          const uint32_t d = tmem + static_cast<uint32_t>(buf * kBN);
+        // descriptor start addresses count 16-byte units: a K step of 32
+        // bytes adds 2 (stage bases stay below 2^18 bytes, so no carry)
+        const uint64_t a_desc = sw128_desc(smem_u32(stage_a(sm, st)));
+        const uint64_t b_desc = sw128_desc(smem_u32(stage_b(sm, st)));
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          const uint32_t d = tmem + static_cast<uint32_t>((2 * pb + g) * kBN);
 #pragma unroll
           for (int kk = 0; kk < 2; ++kk) {
-            const uint32_t koff = static_cast<uint32_t>((2 * g + kk) * 32);
-            mma_i8(d, sw128_desc(a_base + koff), sw128_desc(b_base + koff), idesc, true);
+            const uint64_t koff = static_cast<uint64_t>(2 * (2 * g + kk));
+            mma_i8(d, a_desc + koff, b_desc + koff, idesc, true);
           }
-          mma_commit(&sm.acc_full[buf]);
         }
-        // the stages are free once their MMAs have read them
-        mma_commit(&sm.empty_a[sa]);
-        mma_commit(&sm.empty_b[sb]);
+        mma_commit(&sm.acc_full[pb]);
+        mma_commit(&sm.empty[st]);  // the stage is free once its MMAs have read it
       }
       if (!ok) {
         record_device_error(a, kDevMmaTimeout);
@@ -548,8 +528,9 @@ __global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
     const uint64_t bias2 = f2_pack(__float_as_uint(kAccBiasF), __float_as_uint(kAccBiasF));
     const int et = static_cast<int>(threadIdx.x) - Shape<kBN>::kFirstEpiWarp * 32;  // epilogue thread
     const uint32_t tl = tmem + (static_cast<uint32_t>(32 * quad) << 16);
-    // Buffer b always belongs to warpgroup (b / 2) % 2 (pairs alternate and
-    // the buffer count is a multiple of four); each starts at the bias.
+    // Chunk c fills buffer pair c % kPairs; pair pb always belongs to
+    // warpgroup pb % 2 (chunks alternate and kPairs is even).  Every buffer
+    // starts at the bias.
 #pragma unroll 1
     for (int b = 0; b < kAccBufs; ++b)
       if (((b >> 1) & 1) == role) tmem_fill_bias<kCols>(tl + static_cast<uint32_t>(b * kBN));
@@ -557,8 +538,7 @@ __global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
     tmem_fence_before();
     __syncwarp();
     if (lane == 0)
-      for (int b = 0; b < kAccBufs; ++b)
-        if (((b >> 1) & 1) == role) mbar_arrive(&sm.acc_empty[b]);
+      for (int pb = role; pb < kPairs; pb += 2) mbar_arrive(&sm.acc_empty[pb]);
     auto stage_scales = [&](int g0) {
       stage_group_scales<kEpiWarps * 32>(sm.ws, a.ws, a.G, a.d, row0, 2 * c_begin + g0, ngroups - g0, et);
     };
@@ -578,15 +558,14 @@ __global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
         epi_sync<kEpiWarps>();
       }
       const int wend = ngroups - w0 < kWsWin ? ngroups : w0 + kWsWin;
-      // this warpgroup's pairs of the window (groups gi, gi + 1 in buffers
-      // buf, buf + 1); after a timeout the warp keeps walking the windows
-      // without waiting, so that both warpgroups meet the same barriers
+      // this warpgroup's chunks of the window (chunk c = gi / 2: groups gi,
+      // gi + 1 in buffers 2 pb, 2 pb + 1); after a timeout the warp keeps
+      // walking the windows without waiting, so that both warpgroups meet
+      // the same barriers
       for (int gi = w0 + 2 * role; gi < wend; gi += 4) {
-        const int buf = gi % kAccBufs;  // even
+        const int c = gi >> 1, pb = c % kPairs, buf = 2 * pb;
         const float* wrow = sm.ws + (32 * quad + lane) * kWsStride + (gi - w0);
-        // The second group's commit also covers the first group's MMAs (a
-        // commit tracks every earlier MMA of the issuing thread).
-        if (ok && !mbar_wait_bounded(&sm.acc_full[buf + 1], ((gi + 1) / kAccBufs) & 1, kWaitLimitNs)) ok = false;
+        if (ok && !mbar_wait_bounded(&sm.acc_full[pb], (c / kPairs) & 1, kWaitLimitNs)) ok = false;
         if (!ok) continue;
         tmem_fence_after();
 #pragma unroll 1
@@ -609,10 +588,7 @@ __global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
         tmem_wait_st();
         tmem_fence_before();
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&sm.acc_empty[buf]);
-          mbar_arrive(&sm.acc_empty[buf + 1]);
-        }
+        if (lane == 0) mbar_arrive(&sm.acc_empty[pb]);
       }
     }
     if (!ok) {
@@ -620,13 +596,13 @@ __global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
       *sm.flag = 1;
     }
     epi_sync<kEpiWarps>();
-    // Every load has landed and every MMA that read the weight ring has
+    // Every load has landed and every MMA that read the ring has
     // completed, so the ring takes the finished tile as [token][row]: the
     // two warpgroups' sums added in a fixed order (warpgroup 1, then 2),
     // scaled by xs[t] when the tile is the whole sum, the raw partial sum of
     // this block's K range otherwise.
     const bool good = *sm.flag == 0;
-    float* tile = reinterpret_cast<float*>(sm.a);
+    float* tile = reinterpret_cast<float*>(sm.ring);
     const int r_local = 32 * quad + lane;
     if (good && role == 0) {
 #pragma unroll
@@ -657,7 +633,7 @@ __global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
     if (a.cluster > 1) cluster_sync(); else block_sync<Shape<kBN>::kThreads>();
     constexpr int kEpiThreads = Shape<kBN>::kEpiWarps * 32;
     constexpr int kQuads = kBN * kBM / 4;  // float4s in the tile; 32 per token
-    const uint32_t tile_s = smem_u32(sm.a);
+    const uint32_t tile_s = smem_u32(sm.ring);
     if (a.cluster > 1) {
       // Block `split` of the cluster sums its share of the tile over the
       // cluster's partial tiles in split order (deterministic), scales by
@@ -686,7 +662,7 @@ __global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
       // the whole sum (splits == 1), or this split's partial, which
       // splitk_reduce_kernel sums in split order
       float* dst = a.splits == 1 ? a.y : a.partial + static_cast<size_t>(split) * a.m * a.d;
-      const float4* tile4 = reinterpret_cast<const float4*>(sm.a);
+      const float4* tile4 = reinterpret_cast<const float4*>(sm.ring);
       for (int q = et; q < kQuads; q += kEpiThreads) {
         const int j = q >> 5, t = tok0 + j;
         if (t < a.m) store_out4(dst, a, t, row0 + 4 * (q & 31), tile4[q]);
