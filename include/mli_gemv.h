@@ -259,6 +259,7 @@ int mli_gemv_rowshard_argmax(int form, float* const* peer_logits,
  *   [0, 64)    uint64 row counters, one per source rank
  *   [128, 132) uint32 step counter
  *   [192, 196) uint32 finished-CTA count of a fused step (zero between steps)
+ *   [196, 200) uint32 rows produced by a fused step's CTAs (zero between steps)
  *   [256, ...) fp32 logits [2][d_total], then (at the next 16-byte boundary)
  *              the CTAs' (max, first index) partials int2 [2][8][512].
  * mli_gemv_rowshard's peer_logits[p] and mli_rowshard_wait_argmax's logits

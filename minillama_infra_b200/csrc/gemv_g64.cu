@@ -103,6 +103,7 @@ struct StreamArgs {
   long long* out;
   unsigned* step_rw;                   // this rank's step counter
   unsigned* ctas_done;                 // this rank's finished-CTA count (zero between launches)
+  unsigned* rows_done;                 // rows this launch's CTAs produced (zero between launches)
   const unsigned long long* my_rows;   // this rank's per-source row counters
   unsigned long long timeout_ns;
   int shard_rows[kMaxPeers];
@@ -345,14 +346,19 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_stream_kernel(const StreamAr
           *slot = make_int2(__float_as_int(s_best_v), s_best_i);
         }
       }
-      // The barrier orders every thread's stores before thread 0's
-      // system-scope release fence, which (being cumulative) publishes them
-      // before the increments.
+      // The barrier orders every thread's stores before thread 0's fence,
+      // which (being cumulative) publishes them before the count.
       __syncthreads();
       if (threadIdx.x == 0 && cta_rows > 0) {
-        fence_acq_rel_sys();
-        for (int p = 0; p < a.world; ++p)
-          atomicAdd_system(a.peer_rows[p] + a.rank, static_cast<unsigned long long>(cta_rows));
+        if (a.out == nullptr) {
+          // two-launch step: every CTA raises the ranks' counters itself
+          fence_acq_rel_sys();
+          for (int p = 0; p < a.world; ++p)
+            atomicAdd_system(a.peer_rows[p] + a.rank, static_cast<unsigned long long>(cta_rows));
+        } else {
+          // fused step: the launch's last CTA raises them once for all rows
+          atomicAdd(a.rows_done, static_cast<unsigned>(cta_rows));
+        }
       }
     }
     if (a.out == nullptr) return;
@@ -366,7 +372,18 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_stream_kernel(const StreamAr
     if (!s_last) return;
     __shared__ int s_fail;
     if (threadIdx.x == 0) {
+      // Every other CTA's stores and row count precede its finished-count
+      // increment (release at GPU scope), which this CTA has acquired; one
+      // system-scope fence then publishes all of them before the ranks'
+      // counters rise (a release chain: one fence per launch instead of one
+      // per CTA).  Rows a CTA did not produce are never counted.
+      __threadfence();
       *a.ctas_done = 0;  // every other CTA of this launch is done with it
+      const unsigned produced = atomicExch(a.rows_done, 0u);
+      fence_acq_rel_sys();
+      if (produced > 0)
+        for (int p = 0; p < a.world; ++p)
+          atomicAdd_system(a.peer_rows[p] + a.rank, static_cast<unsigned long long>(produced));
       s_fail = 0;
     }
     __syncthreads();
@@ -714,6 +731,7 @@ int mli_gemv_rowshard_argmax(int form, float* const* peer_logits,
   a.step = reinterpret_cast<const unsigned*>(blk + 128);
   a.step_rw = reinterpret_cast<unsigned*>(blk + 128);
   a.ctas_done = reinterpret_cast<unsigned*>(blk + 192);
+  a.rows_done = reinterpret_cast<unsigned*>(blk + 196);
   a.my_rows = reinterpret_cast<const unsigned long long*>(blk);
   a.out = out;
   a.timeout_ns = static_cast<unsigned long long>(timeout_us) * 1000ull;

@@ -102,13 +102,15 @@ class PeerShardedLinear:
         [0, 64)    uint64 row counters, one per source rank (raised over NVLink)
         [128, 132) uint32 step counter (local)
         [192, 196) uint32 finished-CTA count of a fused step (local)
+        [196, 200) uint32 rows produced by a fused step's CTAs (local)
         [256, ...) fp32 logits [2][d] (the half is the step's parity), then the
                    CTAs' (max, first index) partials
     and opens every other rank's block.  A step is one launch on the current
     stream, mli_gemv_rowshard_argmax: this rank's rows stored into every rank's
-    logits with the CTAs' partials, the counters raised, then the launch's last
-    CTA waits (bounded) for all ranks' rows, takes the argmax from the partials
-    and advances the step.  (forward(fused=False) runs the same as two launches,
+    logits with the CTAs' partials; the launch's last CTA raises every rank's
+    counter for this rank once (one system-scope fence per launch), waits
+    (bounded) for all ranks' rows, takes the argmax from the partials and
+    advances the step.  (forward(fused=False) runs the same as two launches,
     mli_gemv_rowshard + mli_rowshard_wait_argmax.)  The handles travel through torch.distributed (any
     backend); no collective runs on the data path.  world == 1 needs no
     process group (the single GPU then gets the fused GEMV + argmax).
