@@ -240,10 +240,13 @@ int mli_gemv_rowshard(int form, float* const* peer_logits,
                       int rows, int row_offset, int d_total, int rank, int world,
                       int group_size, void* stream);
 
-/* mli_gemv_rowshard and mli_rowshard_wait_argmax in one launch: the last
- * CTA of this rank's GEMV waits (bounded by timeout_us) for every rank's rows
- * of this step, reduces every rank's CTA partials to the argmax, writes it to
- * *out and advances the step -- one kernel per step instead of two.  own_block
+/* mli_gemv_rowshard and mli_rowshard_wait_argmax in one launch: the CTAs
+ * store their rows into every rank's logits as above, but the launch's last
+ * CTA raises peer_rows[p][rank] once for all of this rank's rows (one
+ * system-scope fence per launch instead of one per CTA), then waits (bounded
+ * by timeout_us) for every rank's rows of this step, reduces every rank's CTA
+ * partials to the argmax, writes it to *out and advances the step -- one
+ * kernel per step instead of two.  own_block
  * is this rank's peer block (its header holds the counters, the step and the
  * launch's finished-CTA count); shard_rows is a HOST array of `world` row
  * counts (every rank's `rows`) summing to d_total.  On expiry *out = -1 and
