@@ -8,20 +8,19 @@
 // 465-501); with m >= 16 tokens the op is a real dense contraction and runs
 // here.  One CTA computes a tile of 128 weight rows x BN tokens over a range of
 // K:
-//   * warp 0 streams 128-byte K chunks of the weight tile (128 x 128 B) into a
-//     deep ring (9-11 stages: the weights come from HBM), warp 2 the matching
-//     activation chunks (BN x 128 B, re-read from L2) into a shallow one,
-//     both with 2-D TMA loads (128-byte swizzle, the canonical K-major UMMA
-//     layout);
-//   * warp 1 owns the tensor memory and issues the MMAs from one thread: a
-//     64-column group is two K=32 MMAs accumulating into one of up to eight
-//     int32 accumulators, committed to an mbarrier;
-//   * warps 3.. are the epilogue (4 lane quarters x 2 token-column slices):
-//     each reads its 32 accumulator rows over its slice of the BN token
-//     columns (tcgen05.ld), recovers the exact int32 group dot as a float
-//     (the accumulators start at a bias that makes the int32 result the bits
-//     of 1.5 * 2^23 + I), adds ws[r][g] * I into fp32 registers (packed f32x2
-//     arithmetic) and refills the accumulator with the bias for its next use.
+//   * warp 0 streams 128-byte K chunks of the weight tile (128 x 128 B) and
+//     of the activation tile (BN x 128 B) with 2-D TMA loads (128-byte
+//     swizzle, the canonical K-major UMMA layout) into a ring of 6-10 stages;
+//   * warp 1 owns the tensor memory and issues the MMAs from one thread: per
+//     K chunk, four K=32 MMAs (two per 64-column group) into a pair of int32
+//     accumulator buffers, one commit for the pair and one for the stage;
+//   * warpgroups 1 and 2 are the epilogue, taking alternate chunks: each warp
+//     reads its 32 accumulator lanes over all BN token columns
+//     (tcgen05.ld), recovers the exact int32 group dot as a float (the
+//     accumulators start at a bias that makes the int32 result the bits of
+//     1.5 * 2^23 + I), adds ws[r][g] * I into fp32 registers (packed f32x2
+//     arithmetic) and refills the accumulator with the bias for its next
+//     use; the two warpgroups' sums are added in a fixed order at the end.
 // K is split over CTAs so a layer fills the GPU.  The splits of a tile run as
 // one thread-block cluster: each stages its partial tile in shared memory and
 // sums a share of the tile over the cluster's partials in split order
@@ -324,6 +323,7 @@ struct Smem {
 // loads instead of a dependent global load per group.
 constexpr int kWsWin = 48;
 constexpr int kWsStride = kWsWin + 1;
+static_assert(kWsWin % 4 == 0, "a window holds whole chunk pairs of both epilogue warpgroups");
 constexpr uint32_t kWsBytes = kBM * kWsStride * 4u;
 constexpr uint32_t kBarBytes = 512u;
 
@@ -519,7 +519,7 @@ __global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
     if constexpr (Shape<kBN>::kSplitRegs) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsEpilogue));
     // ---------------- epilogue (two warpgroups) ----------------
     const int quad = warp & 3;                                     // TMEM lanes 32*quad .. +31
-    const int role = (warp - Shape<kBN>::kFirstEpiWarp) >> 2;      // pairs p with p % 2 == role
+    const int role = (warp - Shape<kBN>::kFirstEpiWarp) >> 2;      // chunks c with c % 2 == role
     constexpr int kCols = Shape<kBN>::kCols;
     constexpr int kLd = Shape<kBN>::kLdCols;
     uint64_t acc[kCols / 2];  // fp32 pairs: columns 2j, 2j + 1
