@@ -209,6 +209,25 @@ int mli_gemm_w8a8_noalloc(float* y, const int8_t* xq, const float* xs,
 int mli_gemm_w8a8_cuda_core(float* y, const int8_t* xq, const float* xs,
                             const int8_t* w_q, const float* w_s, int m, int n,
                             int d, int group_size, void* stream);
+/* Several independent batched W8A8 GEMMs with the same token count m in one
+ * launch (no reference counterpart): op i computes y = W_i x_i as
+ * mli_gemm_w8a8 would (within the W8A8 tolerance; K is split differently, so
+ * not bit for bit), deterministic from call to call.  One launch instead of
+ * one per matrix: no launch gaps between the matrices, and the small ones
+ * share the GPU with the large ones.  1 <= count <= MLI_GEMM_GROUP_MAX,
+ * m >= 16, group_size 64, every n % 128 == 0, xq and w_q 16-byte aligned
+ * (MLI_ERR_UNSUPPORTED otherwise); no workspace; outputs must not overlap
+ * any op's inputs or another op's output.  `ops` is a HOST array. */
+#define MLI_GEMM_GROUP_MAX 8
+typedef struct mli_gemm_op {
+  float* y;            /* [m][d] */
+  const int8_t* xq;    /* [m][n] */
+  const float* xs;     /* [m] */
+  const int8_t* w_q;   /* [d][n] */
+  const float* w_s;    /* [d][n / 64] */
+  int n, d;
+} mli_gemm_op;
+int mli_gemm_w8a8_group(const mli_gemm_op* ops, int count, int m, int group_size, void* stream);
 /* Tensor-core plan of mli_gemm_w8a8 on the current device (queries it; no
  * launch).  out[5] = tokens per tile, output tiles, K splits, cluster size
  * (1: none), 1 when the splits sum through the workspace.  Returns

@@ -38,6 +38,11 @@ class GemvOp(ctypes.Structure):
 
 
 _OPS = ctypes.POINTER(GemvOp)
+
+
+class GemmOp(ctypes.Structure):
+    """struct mli_gemm_op (include/mli_gemv.h): one GEMM of a group launch."""
+    _fields_ = [("y", _P), ("xq", _P), ("xs", _P), ("w_q", _P), ("w_s", _P), ("n", _I), ("d", _I)]
 SIGNATURES = {
     "mli_status_string": (ctypes.c_char_p, [_I]),
     "mli_last_status": (_I, []),
@@ -74,6 +79,7 @@ SIGNATURES = {
     "mli_chain_destroy": (_I, [_P]),
     "mli_debug_plan_chain": (_I, [_OPS, _I, _I, _I, ctypes.POINTER(_I)]),
     "mli_debug_plan_gemm": (_I, [_I, _I, _I, ctypes.c_size_t, ctypes.POINTER(_I)]),
+    "mli_gemm_w8a8_group": (_I, [ctypes.POINTER(GemmOp), _I, _I, _I, _P]),
 }
 
 # The drop-in shim's C++ symbols (include/mli_gemv.h, reference include/model.h:62-64).

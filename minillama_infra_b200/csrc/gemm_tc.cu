@@ -390,17 +390,19 @@ __device__ __forceinline__ void epi_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
 }
 
+// One CTA's tile and K range: block `blk` of a launch of `a` (split blk %
+// splits of tile blk / splits).  The tensor maps live in kernel parameter
+// space (grid constants).
 template <int kBN>
-__global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
-    gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap map_w,
-                        const __grid_constant__ CUtensorMap map_x, const Args a) {
+__device__ __forceinline__ void gemm_tile(const CUtensorMap* map_w, const CUtensorMap* map_x, const Args& a,
+                                          int blk) {
   extern __shared__ unsigned char smem_raw[];
   Smem sm = carve(smem_raw, kBN);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   // tile / split of this CTA
-  const int split = blockIdx.x % a.splits;
-  const int tile = blockIdx.x / a.splits;
+  const int split = blk % a.splits;
+  const int tile = blk / a.splits;
   const int tile_n = tile % a.tiles_n;
   const int tile_m = tile / a.tiles_n;
   const int row0 = tile_m * kBM;
@@ -450,10 +452,10 @@ __global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
       const int first = nchunks < kS ? nchunks : kS;
       for (int c = 0; c < first; ++c) {
         mbar_arrive_expect_tx(&sm.full[c], stage_bytes(kBN));
-        tma_load_2d(stage_a(sm, c), &map_w, (c_begin + c) * kChunk, row0, &sm.full[c]);
+        tma_load_2d(stage_a(sm, c), map_w, (c_begin + c) * kChunk, row0, &sm.full[c]);
       }
       griddep_wait();
-      for (int c = 0; c < first; ++c) tma_load_2d(stage_b(sm, c), &map_x, (c_begin + c) * kChunk, tok0, &sm.full[c]);
+      for (int c = 0; c < first; ++c) tma_load_2d(stage_b(sm, c), map_x, (c_begin + c) * kChunk, tok0, &sm.full[c]);
       for (int c = kS; c < nchunks; ++c) {
         const int st = c % kS;
         if (!mbar_wait_bounded(&sm.empty[st], ((c / kS) - 1) & 1, kWaitLimitNs)) {
@@ -463,8 +465,8 @@ __global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
         }
         mbar_arrive_expect_tx(&sm.full[st], stage_bytes(kBN));
         const int kx = (c_begin + c) * kChunk;
-        tma_load_2d(stage_a(sm, st), &map_w, kx, row0, &sm.full[st]);
-        tma_load_2d(stage_b(sm, st), &map_x, kx, tok0, &sm.full[st]);
+        tma_load_2d(stage_a(sm, st), map_w, kx, row0, &sm.full[st]);
+        tma_load_2d(stage_b(sm, st), map_x, kx, tok0, &sm.full[st]);
       }
     }
   } else if (warp == 1) {
@@ -682,6 +684,33 @@ __global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
   }
 }
 
+template <int kBN>
+__global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
+    gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
+                        const __grid_constant__ Args a) {
+  gemm_tile<kBN>(&map_w, &map_x, a, static_cast<int>(blockIdx.x));
+}
+
+// Several independent GEMMs with the same token count in one launch: op o
+// owns blocks [base[o], base[o + 1]) (a multiple of its split count, so a
+// cluster never spans two ops).
+constexpr int kMaxGroupOps = 8;
+struct GroupArgs {
+  CUtensorMap mw[kMaxGroupOps];
+  CUtensorMap mx[kMaxGroupOps];
+  Args op[kMaxGroupOps];
+  int base[kMaxGroupOps + 1];
+  int count;
+};
+
+template <int kBN>
+__global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
+    gemm_w8a8_tc_group_kernel(const __grid_constant__ GroupArgs g) {
+  int o = 0;
+  while (o + 1 < g.count && static_cast<int>(blockIdx.x) >= g.base[o + 1]) ++o;
+  gemm_tile<kBN>(&g.mw[o], &g.mx[o], g.op[o], static_cast<int>(blockIdx.x) - g.base[o]);
+}
+
 // Split-K: y[t][r] = xs[t] * sum_s partial[s][t][r], the splits summed in split
 // order (deterministic), over the whole GPU at once.  Launched right after
 // the GEMM (programmatic dependent launch): the partials are read only after
@@ -871,11 +900,11 @@ Plan choose(int m, int n, int d, const DeviceInfo& dev, bool have_ws) {
 // The setmaxnreg split must fit the registers the block is launched with:
 // an increase beyond them would wait forever.  Checked once per kernel
 // against the compiled register count.
-template <int kBN>
-bool register_split_fits() {
-  static const bool fits = []() {
+template <int kBN, typename K>
+bool register_split_fits(K kernel) {
+  static const bool fits = [kernel]() {
     cudaFuncAttributes fa;
-    if (cudaFuncGetAttributes(&fa, gemm_w8a8_tc_kernel<kBN>) != cudaSuccess) {
+    if (cudaFuncGetAttributes(&fa, kernel) != cudaSuccess) {
       cudaGetLastError();
       return false;
     }
@@ -887,7 +916,7 @@ bool register_split_fits() {
 template <int kBN>
 cudaError_t launch_bn(const CUtensorMap& mw, const CUtensorMap& mx, const Args& a, int grid,
                       cudaStream_t stream) {
-  if (!register_split_fits<kBN>()) return cudaErrorInvalidConfiguration;
+  if (!register_split_fits<kBN>(gemm_w8a8_tc_kernel<kBN>)) return cudaErrorInvalidConfiguration;
   cudaError_t e = prepare_bn<kBN>();
   if (e != cudaSuccess) return e;
   if (a.cluster > 8) {
@@ -897,6 +926,15 @@ cudaError_t launch_bn(const CUtensorMap& mw, const CUtensorMap& mx, const Args& 
   }
   return launch_clustered(gemm_w8a8_tc_kernel<kBN>, dim3(grid), dim3(Shape<kBN>::kThreads), smem_bytes(kBN),
                           stream, true, static_cast<unsigned>(a.cluster), mw, mx, a);
+}
+
+template <int kBN>
+cudaError_t launch_group_bn(const GroupArgs& g, int grid, int cluster, cudaStream_t stream) {
+  if (!register_split_fits<kBN>(gemm_w8a8_tc_group_kernel<kBN>)) return cudaErrorInvalidConfiguration;
+  cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(gemm_w8a8_tc_group_kernel<kBN>), smem_bytes(kBN));
+  if (e != cudaSuccess) return e;
+  return launch_clustered(gemm_w8a8_tc_group_kernel<kBN>, dim3(grid), dim3(Shape<kBN>::kThreads), smem_bytes(kBN),
+                          stream, true, static_cast<unsigned>(cluster), g);
 }
 
 }  // namespace tc
@@ -955,7 +993,92 @@ int gemm_w8a8_tc(float* y, const int8_t* xq, const float* xs, const int8_t* w_q,
                            y, static_cast<const float*>(a.partial), xs, p.splits, m, d, a.vec4));
 }
 
+// Several independent GEMMs of m tokens in one launch (mli_gemm_w8a8_group).
+// Ops run largest K first; every op splits K the same number of ways (a
+// cluster of that many blocks per tile): the fewest splits that keep one
+// block's K range within three quarters of the average work per SM.
+int gemm_w8a8_tc_group(const mli_gemm_op* ops, int count, int m, cudaStream_t stream) {
+  cudaError_t err = cudaSuccess;
+  const DeviceInfo& dev = current_device(&err);
+  if (err != cudaSuccess) return set_status(MLI_ERR_CUDA, err);
+  int order[tc::kMaxGroupOps];
+  for (int i = 0; i < count; ++i) order[i] = i;
+  for (int i = 1; i < count; ++i)  // insertion sort, largest n first (stable)
+    for (int j = i; j > 0 && ops[order[j]].n > ops[order[j - 1]].n; --j) {
+      const int t = order[j];
+      order[j] = order[j - 1];
+      order[j - 1] = t;
+    }
+  tc::Plan plans[tc::kMaxGroupOps];
+  long long work = 0;
+  int max_chunks = 0, min_chunks = 1 << 30;
+  for (int i = 0; i < count; ++i) {
+    plans[i] = tc::plan(m, ops[i].n, ops[i].d, dev.sm_count);
+    work += static_cast<long long>(plans[i].tiles_m) * plans[i].tiles_n * plans[i].chunks;
+    max_chunks = plans[i].chunks > max_chunks ? plans[i].chunks : max_chunks;
+    min_chunks = plans[i].chunks < min_chunks ? plans[i].chunks : min_chunks;
+  }
+  const double per_sm = static_cast<double>(work) / dev.sm_count;
+  int splits = 1;
+  while (splits < 4 && min_chunks / (2 * splits) >= 2 &&
+         static_cast<double>((max_chunks + splits - 1) / splits) > 0.75 * per_sm)
+    splits *= 2;
+  tc::GroupArgs g = {};
+  g.count = count;
+  int blocks = 0;
+  unsigned int* err_word = device_error_word();
+  for (int k = 0; k < count; ++k) {
+    const mli_gemm_op& op = ops[order[k]];
+    const tc::Plan& p = plans[order[k]];
+    if (!tc::make_map(&g.mw[k], op.w_q, op.d, op.n, tc::kBM) || !tc::make_map(&g.mx[k], op.xq, m, op.n, p.bn))
+      return set_status(MLI_ERR_UNSUPPORTED);
+    tc::Args& a = g.op[k];
+    a.y = op.y;
+    a.xs = op.xs;
+    a.ws = op.w_s;
+    a.m = m;
+    a.n = op.n;
+    a.d = op.d;
+    a.G = op.n / 64;
+    a.bn = p.bn;
+    a.tiles_m = p.tiles_m;
+    a.tiles_n = p.tiles_n;
+    a.splits = splits;
+    a.chunks = p.chunks;
+    a.cluster = splits;
+    a.err = err_word;
+    a.vec4 = op.d % 4 == 0 && aligned(op.y, 16);
+    g.base[k] = blocks;
+    blocks += p.tiles_m * p.tiles_n * splits;
+  }
+  g.base[count] = blocks;
+  switch (plans[0].bn) {
+    case 16: err = tc::launch_group_bn<16>(g, blocks, splits, stream); break;
+    case 32: err = tc::launch_group_bn<32>(g, blocks, splits, stream); break;
+    case 64: err = tc::launch_group_bn<64>(g, blocks, splits, stream); break;
+    default: err = tc::launch_group_bn<128>(g, blocks, splits, stream); break;
+  }
+  return check_cuda(err);
+}
+
 }  // namespace mli
+
+extern "C" int mli_gemm_w8a8_group(const mli_gemm_op* ops, int count, int m, int group_size, void* stream) {
+  using namespace mli;
+  if (!ops || count <= 0 || m <= 0 || group_size <= 0) return set_status(MLI_ERR_INVALID_ARG);
+  if (count > tc::kMaxGroupOps) return set_status(MLI_ERR_UNSUPPORTED);
+  for (int i = 0; i < count; ++i) {
+    const mli_gemm_op& op = ops[i];
+    if (!op.y || !op.xq || !op.xs || !op.w_q || !op.w_s || op.n <= 0 || op.d <= 0)
+      return set_status(MLI_ERR_INVALID_ARG);
+  }
+  // the tensor-core shapes only; anything else is refused rather than run elsewhere
+  if (group_size != 64 || m < 16) return set_status(MLI_ERR_UNSUPPORTED);
+  for (int i = 0; i < count; ++i)
+    if (ops[i].n % tc::kChunk != 0 || !aligned(ops[i].xq, 16) || !aligned(ops[i].w_q, 16))
+      return set_status(MLI_ERR_UNSUPPORTED);
+  return gemm_w8a8_tc_group(ops, count, m, static_cast<cudaStream_t>(stream));
+}
 
 extern "C" int mli_debug_plan_gemm(int m, int n, int d, size_t workspace_bytes, int* out) {
   using namespace mli;

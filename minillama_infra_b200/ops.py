@@ -91,6 +91,17 @@ def gemm_w8a8(y, xq, xs, w_q, w_s, m: int, n: int, d: int, group_size: int = 64,
                               group_size, ws_ptr, ws_bytes, _stream(stream)), "gemm_w8a8")
 
 
+def gemm_w8a8_group(items, m: int, group_size: int = 64, stream=None):
+    """Several independent batched W8A8 GEMMs of m tokens in one launch.
+    items: (y, xq, xs, w_q, w_s, n, d) tuples, at most 8."""
+    from ._lib import GemmOp
+
+    arr = (GemmOp * len(items))()
+    for i, (y, xq, xs, w_q, w_s, n, d) in enumerate(items):
+        arr[i] = GemmOp(_ptr(y), _ptr(xq), _ptr(xs), _ptr(w_q), _ptr(w_s), n, d)
+    check(lib().mli_gemm_w8a8_group(arr, len(items), m, group_size, _stream(stream)), "gemm_w8a8_group")
+
+
 def gemm_w8a8_cuda_core(y, xq, xs, w_q, w_s, m: int, n: int, d: int, group_size: int = 64, stream=None):
     check(lib().mli_gemm_w8a8_cuda_core(_ptr(y), _ptr(xq), _ptr(xs), _ptr(w_q), _ptr(w_s), m, n, d,
                                         group_size, _stream(stream)), "gemm_w8a8_cuda_core")

@@ -254,6 +254,63 @@ def test_gemm_split_k_cluster_and_workspace_paths(m, n, d):
     assert ops.device_error() == 0
 
 
+# mli_gemm_w8a8_group: several independent GEMMs of m tokens in one launch,
+# ragged shapes (partial row tiles, K from 2 to 64 chunks, padded tokens).
+@pytest.mark.parametrize("m,shapes", [
+    (16, [(640, 3072), (128, 256), (300, 1024), (1024, 8192)]),
+    (100, [(384, 2048), (200, 1024), (256, 3072)]),
+    (256, [(512, 3072), (1024, 3072), (128, 8192), (1024, 3072), (512, 3072), (256, 1024), (640, 2048)]),
+])
+def test_gemm_w8a8_group_parity(m, shapes):
+    items, refs = [], []
+    for i, (d, n) in enumerate(shapes):
+        seed = 900 + 17 * i + m
+        w_q, w_s = orc.quantize_weights(synth.weights_np(d, n, seed))
+        x = synth.activation_np(n, seed + 1, m=m, outliers=True)
+        xq_ref, xs_ref = orc.quantize_activation(x)
+        xq = torch.empty((m, n), dtype=torch.int8, device=dev())
+        xs = torch.empty(m, dtype=torch.float32, device=dev())
+        ops.quantize_activation_rows(xq, xs, up(x), m, n)
+        y = Guarded(m * d)
+        items.append((y, xq, xs, up(w_q), up(w_s), n, d))
+        refs.append((w_q, w_s, xq_ref, xs_ref))
+    ops.gemm_w8a8_group([(y.t, xq, xs, tw, ts, n, d) for (y, xq, xs, tw, ts, n, d) in items], m)
+    torch.cuda.synchronize()
+    firsts = []
+    for (y, xq, xs, tw, ts, n, d), (w_q, w_s, xq_ref, xs_ref) in zip(items, refs):
+        got = y.check().reshape(m, d)
+        firsts.append(got.copy())
+        for t in sorted({0, 1, m // 2, m - 1}):
+            ref = orc.gemv_w8a8_f64(xq_ref[t], xs_ref[t:t + 1], w_q, w_s)
+            assert orc.max_abs_rel(got[t], ref) <= TOL_W8A8, (d, n, t)
+    # deterministic: a second launch gives the same bits
+    outs = [torch.empty(m * d, dtype=torch.float32, device=dev()) for (_, _, _, _, _, n, d) in items]
+    ops.gemm_w8a8_group([(o, xq, xs, tw, ts, n, d) for o, (_, xq, xs, tw, ts, n, d) in zip(outs, items)], m)
+    torch.cuda.synchronize()
+    for o, f, (_, _, _, _, _, n, d) in zip(outs, firsts, items):
+        assert np.array_equal(o.cpu().numpy().reshape(m, d).view(np.uint32), f.view(np.uint32))
+    assert ops.device_error() == 0
+
+
+def test_gemm_w8a8_group_rejects_bad_arguments():
+    m, n, d = 16, 1024, 128
+    xq = torch.zeros((m, n), dtype=torch.int8, device=dev())
+    xs = torch.ones(m, dtype=torch.float32, device=dev())
+    w_q = torch.zeros((d, n), dtype=torch.int8, device=dev())
+    w_s = torch.ones((d, n // 64), dtype=torch.float32, device=dev())
+    y = torch.empty(m * d, dtype=torch.float32, device=dev())
+    item = (y, xq, xs, w_q, w_s, n, d)
+    with pytest.raises(MliError):
+        ops.gemm_w8a8_group([], m)                      # no op
+    with pytest.raises(MliError):
+        ops.gemm_w8a8_group([item] * 9, m)              # more than MLI_GEMM_GROUP_MAX
+    with pytest.raises(MliError):
+        ops.gemm_w8a8_group([item], 8)                  # fewer than 16 tokens
+    with pytest.raises(MliError):
+        ops.gemm_w8a8_group([(y, xq, xs, w_q, w_s, 1000, d)], m)  # n % 128 != 0
+    assert ops.device_error() == 0
+
+
 def test_rows_are_independent_of_sharding():
     """Row r's result is bit-identical whether computed in the full matrix or
     in any row slice (the property the sharded classifier relies on)."""
