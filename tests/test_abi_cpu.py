@@ -91,6 +91,26 @@ def test_invalid_arguments_rejected_without_gpu(call):
     assert l.mli_last_status() == _lib.MLI_ERR_INVALID_ARG
 
 
+def test_gemm_group_arguments_checked_without_gpu():
+    """mli_gemm_w8a8_group: an empty or null op list and null operands are
+    invalid, more than MLI_GEMM_GROUP_MAX ops or shapes off the tensor-core
+    path unsupported -- all decided before any CUDA call."""
+    l = _lib.lib()
+    ops = (_lib.GemmOp * 9)()
+    assert l.mli_gemm_w8a8_group(None, 1, 16, 64, None) == _lib.MLI_ERR_INVALID_ARG
+    assert l.mli_gemm_w8a8_group(ops, 0, 16, 64, None) == _lib.MLI_ERR_INVALID_ARG
+    assert l.mli_gemm_w8a8_group(ops, 1, 16, 64, None) == _lib.MLI_ERR_INVALID_ARG  # null pointers
+    assert l.mli_gemm_w8a8_group(ops, 9, 16, 64, None) == _lib.MLI_ERR_UNSUPPORTED
+    for i in range(2):
+        ops[i] = _lib.GemmOp(256, 256, 256, 256, 256, 1024, 128)  # 256-byte aligned stand-ins
+    assert l.mli_gemm_w8a8_group(ops, 2, 8, 64, None) == _lib.MLI_ERR_UNSUPPORTED    # m < 16
+    assert l.mli_gemm_w8a8_group(ops, 2, 16, 32, None) == _lib.MLI_ERR_UNSUPPORTED   # group 32
+    ops[1] = _lib.GemmOp(256, 256, 256, 256, 256, 1000, 128)
+    assert l.mli_gemm_w8a8_group(ops, 2, 16, 64, None) == _lib.MLI_ERR_UNSUPPORTED   # n % 128
+    ops[1] = _lib.GemmOp(256, 257, 256, 256, 256, 1024, 128)
+    assert l.mli_gemm_w8a8_group(ops, 2, 16, 64, None) == _lib.MLI_ERR_UNSUPPORTED   # xq misaligned
+
+
 def test_oracle_library_is_not_linked_by_product():
     """The product library must not depend on the oracle."""
     out = subprocess.run(["ldd", _lib.LIB_PATH], capture_output=True, text=True).stdout
