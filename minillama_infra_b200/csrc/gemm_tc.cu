@@ -11,9 +11,11 @@
 //   * warp 0 streams 128-byte K chunks of the weight tile (128 x 128 B) and
 //     of the activation tile (BN x 128 B) with 2-D TMA loads (128-byte
 //     swizzle, the canonical K-major UMMA layout) into a ring of 6-10 stages;
-//   * warp 1 owns the tensor memory and issues the MMAs from one thread: per
-//     K chunk, four K=32 MMAs (two per 64-column group) into a pair of int32
-//     accumulator buffers, one commit for the pair and one for the stage;
+//   * warp 1 owns the tensor memory and issues the MMAs from one thread (two
+//     threads, warps 1 and 2 on alternate chunks, for tiles of 32 tokens or
+//     fewer): per K chunk, four K=32 MMAs (two per 64-column group) into a
+//     pair of int32 accumulator buffers, one commit for the pair and one for
+//     the stage;
 //   * warpgroups 1 and 2 are the epilogue, taking alternate chunks: each warp
 //     reads its 32 accumulator lanes over all BN token columns
 //     (tcgen05.ld), recovers the exact int32 group dot as a float (the
@@ -415,6 +417,7 @@ __device__ __forceinline__ void gemm_tile(const CUtensorMap* map_w, const CUtens
   constexpr int kEpiWarps = Shape<kBN>::kEpiWarps;
   constexpr int kS = stages(kBN);
   constexpr int kPairs = kAccBufs / 2;
+  constexpr bool kTwoIssuers = kBN <= 32;
   constexpr uint32_t kTmemCols = kAccBufs * kBN;  // 128, 256 or 512: a power of two
 
   if (threadIdx.x == 0) {
@@ -469,15 +472,22 @@ __device__ __forceinline__ void gemm_tile(const CUtensorMap* map_w, const CUtens
         tma_load_2d(stage_b(sm, st), map_x, kx, tok0, &sm.full[st]);
       }
     }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    // Per chunk: one wait for its stage, one for its pair of accumulator
-    // buffers, four MMAs (two K=32 steps per group), one commit for the
-    // pair and one for the stage.
+  } else if (warp == 1 || (kTwoIssuers && warp == 2)) {
+    // ---------------- MMA issuer(s) ----------------
+    // Narrow tiles (kTwoIssuers) have two issuing threads, warp 1 the even
+    // chunks and warp 2 the odd ones: one thread's instruction issue (about
+    // 90 cycles per tcgen05.mma) bounds them.  The chunks of the two use
+    // disjoint accumulator pairs (kPairs is even); a stage passes between
+    // them through its full and empty barriers, and a commit tracks only its
+    // own thread's MMAs.  Wide tiles are bound by the epilogue, where a
+    // second issuer only takes issue slots.  Per chunk: one wait for its
+    // stage, one for its pair of accumulator buffers, four MMAs (two K=32
+    // steps per group), one commit for the pair and one for the stage.
     if (lane == 0) {
       const uint32_t idesc = i8_idesc(kBN);
       bool ok = true;
-      for (int c = 0; c < nchunks; ++c) {
+      constexpr int kIssuers = kTwoIssuers ? 2 : 1;
+      for (int c = warp - 1; c < nchunks; c += kIssuers) {
         const int st = c % kS, pb = c % kPairs;
         // use u of a pair waits for phase u: the epilogue's bias fill
         // (phase 0) or its read of use u - 1
