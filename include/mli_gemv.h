@@ -178,11 +178,12 @@ int mli_quantize_activation_rows(int8_t* xq, float* xs, const float* x, int m,
  * mli_gemv_w8a8 on that token.  The tensor-core path splits K over CTAs to
  * fill the GPU.  The splits of a tile run as one thread-block cluster and
  * sum their partials in split order over shared memory, when clusters of
- * that size fit the GPU in one wave; otherwise `workspace` (device, may be
- * NULL; mli_gemm_w8a8_workspace_bytes(m, n, d) bytes, any contents) holds
- * the splits' partial sums, summed in split order by a second launch on the
- * same stream, and without it K is split only as far as clusters allow.
- * Calls that share a workspace must not overlap on the GPU. */
+ * that size fit the GPU in one wave.  Otherwise the library takes the faster
+ * (by its estimate) of the largest cluster that fits and, if `workspace`
+ * (device, may be NULL; mli_gemm_w8a8_workspace_bytes(m, n, d) bytes, any
+ * contents) is given, the full split with its partial sums in the workspace,
+ * summed in split order by a second launch on the same stream.  Calls that
+ * share a workspace must not overlap on the GPU. */
 size_t mli_gemm_w8a8_workspace_bytes(int m, int n, int d);
 int mli_gemm_w8a8(float* y, const int8_t* xq, const float* xs,
                   const int8_t* w_q, const float* w_s, int m, int n, int d,
