@@ -254,6 +254,33 @@ def test_gemm_split_k_cluster_and_workspace_paths(m, n, d):
     assert ops.device_error() == 0
 
 
+@pytest.mark.parametrize("m,n,d", [(16, 3072, 1024), (256, 3072, 1024), (256, 8192, 3072), (64, 2048, 8192)])
+def test_gemm_plan_is_consistent(m, n, d):
+    """mli_gemm_w8a8's plan on this GPU: K splits within [1, K chunks / 2],
+    clusters of at most 16 that are the splits themselves, the workspace used
+    only when given, and MLI_LAUNCH_NO_CLUSTER turning clusters off."""
+    import ctypes
+
+    out = (ctypes.c_int * 5)()
+    need = ops.gemm_workspace_bytes(m, n, d)
+    for ws_bytes in (0, need):
+        assert lib().mli_debug_plan_gemm(m, n, d, ws_bytes, out) == 0
+        bn, tiles, splits, cluster, via_ws = list(out)
+        assert bn == (16 if m <= 16 else 32 if m <= 32 else 64 if m <= 64 else 128)
+        assert tiles == -(-d // 128) * -(-m // bn)
+        assert 1 <= splits <= max(1, n // 128 // 2)
+        assert via_ws in (0, 1) and (via_ws == 0 or ws_bytes > 0)
+        assert cluster == (1 if via_ws else splits) and cluster <= 16
+    try:
+        ops.set_gemm_clusters(False)
+        assert lib().mli_debug_plan_gemm(m, n, d, need, out) == 0
+        assert out[3] == 1
+        assert lib().mli_debug_plan_gemm(m, n, d, 0, out) == 0
+        assert out[2] == 1 and out[3] == 1 and out[4] == 0  # no workspace, no cluster: K is not split
+    finally:
+        ops.set_gemm_clusters(True)
+
+
 # mli_gemm_w8a8_group: several independent GEMMs of m tokens in one launch,
 # ragged shapes (partial row tiles, K from 2 to 64 chunks, padded tokens).
 @pytest.mark.parametrize("m,shapes", [
