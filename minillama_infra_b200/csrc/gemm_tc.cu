@@ -960,7 +960,7 @@ size_t gemm_tc_workspace_bytes(int m, int n, int d, int sm_count) {
 int gemm_w8a8_tc(float* y, const int8_t* xq, const float* xs, const int8_t* w_q, const float* w_s,
                  int m, int n, int d, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   if (m < 16 || n % tc::kChunk != 0 || !aligned(xq, 16) || !aligned(w_q, 16))
-    return MLI_ERR_UNSUPPORTED;
+    return set_status(MLI_ERR_UNSUPPORTED);
   cudaError_t err = cudaSuccess;
   const DeviceInfo& dev = current_device(&err);
   if (err != cudaSuccess) return set_status(MLI_ERR_CUDA, err);
@@ -969,7 +969,7 @@ int gemm_w8a8_tc(float* y, const int8_t* xq, const float* xs, const int8_t* w_q,
   const tc::Plan p = tc::choose(m, n, d, dev, have_ws);
   CUtensorMap mw, mx;
   if (!tc::make_map(&mw, w_q, d, n, tc::kBM) || !tc::make_map(&mx, xq, m, n, p.bn))
-    return MLI_ERR_UNSUPPORTED;
+    return set_status(MLI_ERR_UNSUPPORTED);
   tc::Args a = {};
   a.y = y;
   a.xs = xs;

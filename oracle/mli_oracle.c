@@ -192,6 +192,47 @@ void oracle_gemv_w8a8_f64(double* y, const int8_t* xq, const float* xs,
   }
 }
 
+/* Batched fp64 recompute for m tokens (y [m][d] token-major): token t's row r
+ * is sum_g I_t[r][g] * ws[r][g], times xs[t], in double from the exact int32
+ * partials -- the same value oracle_gemv_w8a8_f64 gives for that token.  One
+ * weight row is read once for all tokens (OpenMP over rows), so the full
+ * Llama-3.2-3B shapes at m = 256 finish in about a second. */
+void oracle_gemm_w8a8_f64(double* y, const int8_t* xq, const float* xs,
+                          const int8_t* w, const float* s, long m, long n,
+                          long d, int gs) {
+  long ng = n / gs;
+#pragma omp parallel for schedule(dynamic, 8)
+  for (long r = 0; r < d; ++r) {
+    const int8_t* wr = w + r * n;
+    const float* sr = s + r * ng;
+    for (long t = 0; t < m; ++t) {
+      const int8_t* xt = xq + t * n;
+      double acc = 0.0;
+      for (long g = 0; g < ng; ++g)
+        acc += (double)group_dot(wr + g * gs, xt + g * gs, gs) * (double)sr[g];
+      y[t * d + r] = acc * (double)xs[t];
+    }
+  }
+}
+
+/* Exact int64 sums of the int32 group dots weighted by integer scales:
+ * y[t][r] = sum_g I_t[r][g] * k[r][g].  With k one-hot per row this reads one
+ * group dot per row; the GPU parity tests use it to check the production
+ * kernels' group dots bit for bit. */
+void oracle_group_dot_sums(int64_t* y, const int8_t* xq, const int8_t* w,
+                           const int32_t* k, long m, long n, long d, int gs) {
+  long ng = n / gs;
+#pragma omp parallel for schedule(static)
+  for (long r = 0; r < d; ++r)
+    for (long t = 0; t < m; ++t) {
+      int64_t acc = 0;
+      for (long g = 0; g < ng; ++g)
+        acc += (int64_t)group_dot(w + r * n + g * gs, xq + t * n + g * gs, gs) *
+               (int64_t)k[r * ng + g];
+      y[t * d + r] = acc;
+    }
+}
+
 /* CPU baseline: float32 dequant-then-matvec of the same quantised data,
  * OpenMP over rows, the plain loop a host implementation would write. */
 void oracle_dequant_matvec(float* y, const float* x, const int8_t* w,

@@ -38,6 +38,7 @@ _f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
 _f64p = np.ctypeslib.ndpointer(dtype=np.float64, flags="C_CONTIGUOUS")
 _i8p = np.ctypeslib.ndpointer(dtype=np.int8, flags="C_CONTIGUOUS")
 _i32p = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
+_i64p = np.ctypeslib.ndpointer(dtype=np.int64, flags="C_CONTIGUOUS")
 _L = ctypes.c_long
 _I = ctypes.c_int
 
@@ -63,6 +64,8 @@ def lib():
             "oracle_gemm_w8a8": (None, [_f32p, _i8p, _f32p, _i8p, _f32p, _L, _L, _L, _I]),
             "oracle_gemv_w8a32_f64": (None, [_f64p, _f32p, _i8p, _f32p, _L, _L, _I]),
             "oracle_gemv_w8a8_f64": (None, [_f64p, _i8p, _f32p, _i8p, _f32p, _L, _L, _I]),
+            "oracle_gemm_w8a8_f64": (None, [_f64p, _i8p, _f32p, _i8p, _f32p, _L, _L, _L, _I]),
+            "oracle_group_dot_sums": (None, [_i64p, _i8p, _i8p, _i32p, _L, _L, _L, _I]),
             "oracle_dequant_matvec": (None, [_f32p, _f32p, _i8p, _f32p, _L, _L, _I]),
             "oracle_num_threads": (_I, []),
             "oracle_set_num_threads": (None, [_I]),
@@ -152,12 +155,51 @@ def gemv_w8a8_f64(xq, xs, w_q, w_s, group_size: int = 64):
     return y
 
 
+def gemm_w8a8_f64(xq, xs, w_q, w_s, group_size: int = 64):
+    """fp64 recompute of m tokens at once (y [m][d]); token t equals
+    gemv_w8a8_f64(xq[t], xs[t:t+1], ...)."""
+    d, n = w_q.shape
+    xq = _c(xq, np.int8).reshape(-1, n)
+    m = xq.shape[0]
+    y = np.empty((m, d), np.float64)
+    lib().oracle_gemm_w8a8_f64(y, xq, _c(xs, np.float32).reshape(-1), _c(w_q, np.int8), _c(w_s, np.float32),
+                               m, n, d, group_size)
+    return y
+
+
+def group_dot_sums(xq, w_q, k, group_size: int = 64):
+    """Exact int64 y[t][r] = sum_g I_t[r][g] * k[r][g] (k integer, [d][n/gs])."""
+    d, n = w_q.shape
+    xq = _c(xq, np.int8).reshape(-1, n)
+    m = xq.shape[0]
+    y = np.empty((m, d), np.int64)
+    lib().oracle_group_dot_sums(y, xq, _c(w_q, np.int8), _c(k, np.int32), m, n, d, group_size)
+    return y
+
+
 def dequant_matvec(x, w_q, w_s, group_size: int = 64, out=None):
     """CPU baseline: float32 dequant-then-matvec, OpenMP over rows."""
     d, n = w_q.shape
     y = np.empty(d, np.float32) if out is None else out
     lib().oracle_dequant_matvec(y, x, w_q, w_s, n, d, group_size)
     return y
+
+
+_CPU_BASELINE = os.path.join(_HERE, "cpu_baseline.c")
+
+
+def cpu_baseline_lib(out_dir: str):
+    """Compiles cpu_baseline.c with -O3 -march=native for the host that calls
+    this (into out_dir) and returns its ctypes handle."""
+    so = os.path.join(out_dir, "libcpu_baseline.so")
+    cc = "/usr/bin/gcc" if os.path.exists("/usr/bin/gcc") else "gcc"
+    subprocess.run([cc, "-O3", "-march=native", "-fopenmp", "-fPIC", "-shared", "-std=c11",
+                    _CPU_BASELINE, "-o", so], check=True)
+    l = ctypes.CDLL(so)
+    l.cpu_dequant_matvec.argtypes = [_f32p, _f32p, _i8p, _f32p, _L, _L, _I]
+    l.cpu_dequant_matvec.restype = None
+    l.cpu_num_threads.restype = _I
+    return l
 
 
 def num_threads() -> int:

@@ -11,8 +11,8 @@ output.  The inputs include groups that are all zero (the 1e-9 guard of :59),
 exact rounding ties (w / scale = k + 0.5, half-to-even at :63) and values at
 +-amax (the clip of :64).
 
-Run it where the reference tree exists:
-    python tests/golden/make_golden_quant.py [/path/to/reference]
+Run it where the reference tree exists (the path is required):
+    python tests/golden/make_golden_quant.py /path/to/reference
 """
 import os
 import struct
@@ -106,4 +106,7 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("MLI_REF_ROOT")
+    if not root:
+        sys.exit("usage: make_golden_quant.py <reference tree> (or set MLI_REF_ROOT)")
+    main(root)
