@@ -79,6 +79,42 @@ def weights_gpu(rows: int, cols: int, seed: int, device, std: float = 0.02):
     return q, s
 
 
+def quantize_torch(w, group: int = GROUP):
+    """The reference weight quantiser (scripts/quantize_int8_group.py:55-64) in
+    plain torch ops, on whatever device `w` lives: amax per (row, group), zero
+    amax -> float32(1e-9), scale = amax / 127 (fp32), q = clip(round-half-even(
+    w / scale), +-127).  IEEE fp32 division and torch.round (ties to even) make
+    it bit-identical to the script and to mli_quantize_weights; the bench
+    builds its workloads with it so that the reference arm never loads this
+    repository's library."""
+    import torch
+
+    rows, cols = w.shape
+    g = w.reshape(rows, cols // group, group)
+    amax = g.abs().amax(dim=-1)
+    amax = torch.where(amax == 0, torch.full_like(amax, 1e-9), amax)
+    scale = amax / 127.0
+    q = torch.round(g / scale.unsqueeze(-1)).clamp_(-127.0, 127.0).to(torch.int8)
+    return q.reshape(rows, cols), scale
+
+
+def weights_torch(rows: int, cols: int, seed: int, device, std: float = 0.02):
+    """The same (int8, fp32 scales) as weights_gpu, from the same seeded
+    normal draws, quantised with quantize_torch (no library call)."""
+    import torch
+
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    q = torch.empty((rows, cols), dtype=torch.int8, device=device)
+    s = torch.empty((rows, cols // GROUP), dtype=torch.float32, device=device)
+    block = max(1, (64 << 20) // (cols * 4))
+    for r0 in range(0, rows, block):
+        r1 = min(rows, r0 + block)
+        w = torch.randn((r1 - r0, cols), generator=g, device=device, dtype=torch.float32) * std
+        q[r0:r1], s[r0:r1] = quantize_torch(w)
+    return q, s
+
+
 def activation_gpu(n: int, seed: int, device, m: int | None = None, outliers: bool = False):
     import torch
 

@@ -182,13 +182,14 @@ def test_group_dots_batch1_bit_exact(d, n, kind):
     ops.matmul_dp4a(y, up(xq[0]), one, tw, tk, n, d, 64)
     yf = torch.full((d,), float("nan"), dtype=torch.float32, device=dev())
     xs_out = torch.empty(1, dtype=torch.float32, device=dev())
-    ops.matmul_dp4a_fused(yf, up(xq[0].astype(np.float32)), tw, tk, n, d, 64, xs_out=xs_out)
+    xq_out = torch.empty(n, dtype=torch.int8, device=dev())
+    ops.matmul_dp4a_fused(yf, up(xq[0].astype(np.float32)), tw, tk, n, d, 64, xq_out=xq_out, xs_out=xs_out)
     yc = torch.full((d,), float("nan"), dtype=torch.float32, device=dev())
     chain = ops.GemvChain([dict(form="w8a8", n=n, d=d, wait=0, xq=up(xq[0]), xs=one, y=yc, w_q=tw, w_s=tk)])
     chain.run()
     torch.cuda.synchronize()
     chain.close()
-    assert xs_out.item() == 1.0
+    assert xs_out.item() == 1.0 and np.array_equal(xq_out.cpu().numpy(), xq[0])
     for out in (y, yf, yc):
         assert np.array_equal(out.cpu().numpy(), expect[0])  # exact (+0 and -0 compare equal)
 
