@@ -102,6 +102,14 @@ int mli_gemv_w8a8_fused(float* y, int8_t* xq_out, float* xs_out,
                         const float* x, const int8_t* w_q, const float* w_s,
                         int n, int d, int group_size, void* stream);
 
+/* fp32 GEMV y = W x, W fp32 [d][n] row-major.  Replaces the reference's
+ * matmul (include/model.h:61; src/model_cuda_v2_shared.cu:10-25), which its
+ * forward passes use for the tied-embedding classifier (:418, :564): one warp
+ * per row with 512-byte coalesced loads instead of one thread per row.
+ * Within max|y - y_ref| / max|y_ref| <= 1e-5 of the reference (a different
+ * summation order). */
+int mli_gemv_f32(float* y, const float* x, const float* w, int n, int d, void* stream);
+
 /* ---- chained decode step (no reference counterpart) -------------------- */
 
 /* Row epilogues of a chained GEMV.  ADD adds each row into y (the residual add
@@ -334,7 +342,7 @@ int mli_debug_plan_gemv(int form, int n, int d, int sm_count, int smem_per_sm,
 } /* extern "C" */
 
 /* ---- drop-in shim (libmli_dropin.so, C++ linkage) --------------------------
- * Exactly the reference's launch signatures (include/model.h:62-64), so the
+ * Exactly the reference's launch signatures (include/model.h:61-64), so the
  * reference's forward_cuda / forward_cuda_dp4a (src/model_cuda_v2_shared.cu:370-421,
  * 514-566) link against this library unchanged once the reference's own
  * definitions of these three functions are removed.  They launch on the legacy
@@ -346,6 +354,9 @@ void matmul_dp4a(float* xout, const int8_t* x_q, const float* x_s,
                  const int8_t* w_q, const float* w_s, int n, int d,
                  int group_size);
 void quantize_activation(int8_t* xq, float* xs, const float* x, int n);
+/* The fp32 launcher of include/model.h:61 (the classifier's), optional for a
+ * maintainer: remove it from the shim's link to keep the reference's own. */
+void matmul(float* xout, float* x, float* w, int n, int d);
 #endif /* __cplusplus */
 
 #endif /* MLI_GEMV_H */

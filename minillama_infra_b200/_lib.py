@@ -74,6 +74,7 @@ SIGNATURES = {
                                       _I, _I, _I, _I, ctypes.POINTER(_I), _P, _I, _P]),
     "mli_rowshard_block_bytes": (ctypes.c_size_t, [_I]),
     "mli_argmax": (_I, [_P, _I, _P, _P]),
+    "mli_gemv_f32": (_I, [_P, _P, _P, _I, _I, _P]),
     "mli_chain_create": (_I, [_OPS, _I, ctypes.POINTER(_P)]),
     "mli_chain_run": (_I, [_P, _P]),
     "mli_chain_destroy": (_I, [_P]),
@@ -87,6 +88,7 @@ DROPIN_SYMBOLS = {
     "matmul_int8": "_Z11matmul_int8PfS_PaS_iii",
     "matmul_dp4a": "_Z11matmul_dp4aPfPKaPKfS1_S3_iii",
     "quantize_activation": "_Z19quantize_activationPaPfPKfi",
+    "matmul": "_Z6matmulPfS_S_ii",
 }
 
 _lib = None
@@ -133,6 +135,8 @@ def dropin():
         f.argtypes, f.restype = [P, P, P, P, P, _I, _I, _I], None
         f = getattr(l, DROPIN_SYMBOLS["quantize_activation"])
         f.argtypes, f.restype = [P, P, P, _I], None
+        f = getattr(l, DROPIN_SYMBOLS["matmul"])
+        f.argtypes, f.restype = [P, P, P, _I, _I], None
         _dropin = l
     return _dropin
 

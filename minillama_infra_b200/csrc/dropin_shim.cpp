@@ -1,8 +1,8 @@
-// dropin_shim.cpp -- libmli_dropin.so: the reference's three launchers with
-// their exact C++ signatures (include/model.h:62-64 of MiniLlama-Infra),
+// dropin_shim.cpp -- libmli_dropin.so: the reference's GEMV launchers with
+// their exact C++ signatures (include/model.h:61-64 of MiniLlama-Infra),
 // forwarding to the C ABI on the legacy default stream.
 //
-// The reference launchers (src/model_cuda_v2_shared.cu:64-69, 457-460,
+// The reference launchers (src/model_cuda_v2_shared.cu:21-25, 64-69, 457-460,
 // 503-509) return void and check nothing.  These keep the void signature and
 // leave the call's status in mli_last_status() for callers that want it.
 #include "../../include/mli_gemv.h"
@@ -20,4 +20,8 @@ void matmul_dp4a(float* xout, const int8_t* x_q, const float* x_s,
 
 void quantize_activation(int8_t* xq, float* xs, const float* x, int n) {
   (void)mli_quantize_activation(xq, xs, x, n, nullptr);
+}
+
+void matmul(float* xout, float* x, float* w, int n, int d) {
+  (void)mli_gemv_f32(xout, x, w, n, d, nullptr);
 }

@@ -19,7 +19,7 @@ import ctypes
 from ._lib import GemvOp, check, lib
 
 __all__ = [
-    "matmul_int8", "matmul_dp4a", "quantize_activation", "matmul_dp4a_fused",
+    "matmul", "matmul_int8", "matmul_dp4a", "quantize_activation", "matmul_dp4a_fused",
     "quantize_activation_rows", "gemm_w8a8", "gemm_w8a8_cuda_core", "gemm_workspace_bytes",
     "quantize_weights", "group_dots",
     "device_error", "set_pdl", "copy_from_ptr", "GemvChain", "DECODE_LAYER_WAITS",
@@ -45,6 +45,11 @@ def _stream(stream):
     if isinstance(stream, int):
         return stream
     return stream.cuda_stream
+
+
+def matmul(xout, x, w, n: int, d: int, stream=None):
+    """fp32 GEMV, xout[d] = w[d][n] @ x[n] (reference :10-25, the classifier's launcher)."""
+    check(lib().mli_gemv_f32(_ptr(xout), _ptr(x), _ptr(w), n, d, _stream(stream)), "matmul")
 
 
 def matmul_int8(xout, x, w_q, w_s, n: int, d: int, group_size: int = 64, stream=None):

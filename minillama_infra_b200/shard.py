@@ -210,3 +210,108 @@ class PeerShardedLinear:
         if self._own.value:
             self.lib.mli_peer_free(self._own.value)
             self._own.value = None
+
+
+class ShardedFFN:
+    """One rank's share of a row-sharded Llama FFN block: gate/up/down.
+
+    The reference runs the block on one GPU (src/model_cuda_v2_shared.cu:408-412 W8A32,
+    :551-558 W8A8): hb = gate(xb), hb2 = up(xb), hb = silu(hb) * hb2, xb = down(hb).
+    Sharded over `world` ranks by output rows:
+
+      1. gate/up rows [r0, r1) of the hidden dimension (hidden / world rows each):
+         hb_local = silu(gate_local x) * (up_local x), in ONE launch (a two-op chain whose
+         SwiGLU epilogue streams both matrices' rows together);
+      2. all-gather hb (hidden fp32) so every rank holds the whole vector;
+      3. down rows [r0', r1') of the model dimension (dim / world rows, K = hidden);
+      4. all-gather xb (dim fp32).
+
+    Every row is a full-K dot whose arithmetic depends only on K, so the gathered hb and xb
+    are bit-identical to the single-GPU block for any world size.  `gate_q` ... `down_s` are
+    this rank's rows only.  `form`: "w8a32" or "w8a8" (activation quantisation fused into
+    each GEMV, as mli_gemv_w8a8_fused).  `compute_gateup(hb_local, x)` and
+    `compute_down(y_local, hb)` default to the CUDA kernels; the CPU tests pass the oracle.
+    """
+
+    def __init__(self, gate_q, gate_s, up_q, up_s, down_q, down_s, dim: int, hidden: int,
+                 rank: int, world: int, form: str = "w8a32", group=None,
+                 compute_gateup=None, compute_down=None, device=None):
+        import torch
+
+        if form not in ("w8a32", "w8a8"):
+            raise ValueError(f"unknown form {form}")
+        self.hs = row_shard(hidden, world, rank)   # gate/up rows
+        self.ds = row_shard(dim, world, rank)      # down rows
+        for name, t, rows, cols in (("gate", gate_q, self.hs.rows, dim), ("up", up_q, self.hs.rows, dim),
+                                    ("down", down_q, self.ds.rows, hidden)):
+            if tuple(t.shape) != (rows, cols):
+                raise ValueError(f"{name} shard {tuple(t.shape)} != ({rows}, {cols})")
+        self.gate_q, self.gate_s, self.up_q, self.up_s = gate_q, gate_s, up_q, up_s
+        self.down_q, self.down_s = down_q, down_s
+        self.dim, self.hidden, self.world, self.form, self.group = dim, hidden, world, form, group
+        self.device = gate_q.device if device is None else device
+        f32 = dict(dtype=torch.float32, device=self.device)
+        self.hb_local = torch.zeros(self.hs.chunk, **f32)
+        self.hb_full = torch.zeros(self.hs.chunk * world, **f32)
+        self.xb_local = torch.zeros(self.ds.chunk, **f32)
+        self.xb_full = torch.zeros(self.ds.chunk * world, **f32)
+        self._x = None
+        self._chain = None
+        self.compute_gateup = compute_gateup if compute_gateup is not None else self._gateup_cuda
+        self.compute_down = compute_down if compute_down is not None else self._down_cuda
+
+    def _gateup_cuda(self, hb_local, x):
+        from . import ops
+
+        if self.hs.rows == 0:
+            return
+        if self._chain is None or self._x is not x:
+            if self._chain is not None:
+                self._chain.close()
+            form = "w8a32" if self.form == "w8a32" else "w8a8_fused"
+            rows = self.hs.rows
+            self._chain = ops.GemvChain([
+                dict(form=form, n=self.dim, d=rows, wait=0, x=x, y=hb_local, w_q=self.gate_q, w_s=self.gate_s,
+                     epilogue="swiglu"),
+                dict(form=form, n=self.dim, d=rows, wait=0, x=x, y=None, w_q=self.up_q, w_s=self.up_s),
+            ])
+            self._x = x
+        self._chain.run()
+
+    def _down_cuda(self, y_local, hb):
+        from . import ops
+
+        if self.ds.rows == 0:
+            return
+        if self.form == "w8a32":
+            ops.matmul_int8(y_local, hb, self.down_q, self.down_s, self.hidden, self.ds.rows, 64)
+        else:
+            ops.matmul_dp4a_fused(y_local, hb, self.down_q, self.down_s, self.hidden, self.ds.rows, 64)
+
+    def _gather(self, full, local, shard):
+        import torch.distributed as dist
+
+        if self.world == 1:
+            full.copy_(local)
+        elif dist.get_backend(self.group) == "nccl":
+            dist.all_gather_into_tensor(full, local, group=self.group)
+        else:
+            parts = list(full.view(self.world, shard.chunk).unbind(0))
+            dist.all_gather(parts, local, group=self.group)
+
+    def forward(self, x):
+        """xb = down(silu(gate x) * (up x)) over all ranks; returns the dim-vector."""
+        self.compute_gateup(self.hb_local[: self.hs.rows], x)
+        self._gather(self.hb_full, self.hb_local, self.hs)
+        self.compute_down(self.xb_local[: self.ds.rows], self.hb_full[: self.hidden])
+        self._gather(self.xb_full, self.xb_local, self.ds)
+        return self.xb_full[: self.dim]
+
+    def hidden_vector(self):
+        """The gathered silu(gate x) * (up x) of the last forward."""
+        return self.hb_full[: self.hidden]
+
+    def close(self):
+        if self._chain is not None:
+            self._chain.close()
+            self._chain = None

@@ -136,3 +136,81 @@ def read_int8_classifier(path: str):
     w_s = np.memmap(path, dtype=np.float32, mode="r", offset=off, shape=(rows, cols // group))
     w_q = np.memmap(path, dtype=np.int8, mode="r", offset=off + n_s * 4, shape=(rows, cols))
     return w_q, w_s
+
+
+# ---------------------------------------------------------------------------
+# synthetic model and tokenizer files (no checkpoint is available offline)
+# ---------------------------------------------------------------------------
+LLAMA_1B = ModelConfig(dim=2048, hidden_dim=8192, n_layers=16, n_heads=32, n_kv_heads=8,
+                       vocab_size=128256, seq_len=131072)
+
+
+def write_synthetic_model(path: str, c: ModelConfig = LLAMA_1B, seed: int = 0, device="cpu",
+                          std: float = 0.02) -> int:
+    """Writes a group-64 weight file in the reference exporter's layout
+    (scripts/quantize_int8_group.py:41-74; the loader is src/main_cuda.cpp:340-393):
+    the 28-byte config, the fp32 token embedding, the norms (all ones), every
+    layer's matrices quantised with the reference scheme (fp32 scales of all
+    layers, then their int8 rows), the final norm and the fp32 classifier (the
+    embedding again: the 1B model ties them).  Weights are N(0, std) from a
+    seeded torch generator on `device`.  Returns the file size."""
+    import torch
+
+    from .synth import quantize_torch
+
+    L, d, h, kv = c.n_layers, c.dim, c.hidden_dim, c.kv_dim
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+
+    def randn(rows, cols):
+        return torch.randn((rows, cols), generator=g, device=device, dtype=torch.float32) * std
+
+    ones = np.ones(L * d, np.float32).tobytes()
+    with open(path, "wb") as f:
+        f.write(HEADER.pack(c.dim, c.hidden_dim, c.n_layers, c.n_heads, c.n_kv_heads, c.vocab_size,
+                            c.seq_len))
+        emb_off = f.tell()
+        for r0 in range(0, c.vocab_size, 8192):
+            f.write(randn(min(8192, c.vocab_size - r0), d).cpu().numpy().tobytes())
+        f.write(ones)  # rms_att_weight
+        for name, rows, cols in (("wq", d, d), ("wk", kv, d), ("wv", kv, d), ("wo", d, d), (None, 0, 0),
+                                 ("w1", h, d), ("w2", d, h), ("w3", h, d)):
+            if name is None:
+                f.write(ones)  # rms_ffn_weight
+                continue
+            qs, ss = [], []
+            for _ in range(L):
+                q, s = quantize_torch(randn(rows, cols))
+                qs.append(q.cpu().numpy())
+                ss.append(s.cpu().numpy())
+            for s in ss:
+                f.write(s.tobytes())
+            for q in qs:
+                f.write(q.tobytes())
+        f.write(np.ones(d, np.float32).tobytes())  # rms_final_weight
+        emb_bytes = c.vocab_size * d * 4
+        f.flush()
+        with open(path, "rb") as src:  # wcls: the embedding again
+            src.seek(emb_off)
+            for done in range(0, emb_bytes, 1 << 26):
+                f.write(src.read(min(1 << 26, emb_bytes - done)))
+        size = f.tell()
+    expected = HEADER.size + sum(sz for _, sz in reference_sections(c))
+    if size != expected:
+        raise AssertionError(f"wrote {size} bytes, the layout needs {expected}")
+    return size
+
+
+def write_tokenizer(path: str, vocab_size: int, tokens=None) -> None:
+    """A tokenizer.bin in the reference's format (src/tokenizer.cpp:7-16):
+    int32 max_len, then per token fp32 score, int32 length, bytes.  Token i is
+    the text `<i>` unless `tokens` ({id: text}) names it."""
+    import struct as _s
+
+    tokens = tokens or {}
+    texts = [tokens.get(i, f"<{i}>").encode() for i in range(vocab_size)]
+    with open(path, "wb") as f:
+        f.write(_s.pack("<i", max(len(t) for t in texts)))
+        for i, t in enumerate(texts):
+            f.write(_s.pack("<fi", 0.0, len(t)))
+            f.write(t)

@@ -12,6 +12,7 @@
  *   oracle_quantize_activation src/model_cuda_v2_shared.cu:429-455
  *   oracle_gemv_w8a32         src/model_cuda_v2_shared.cu:36-62 (+ warpReduceSum :30-34)
  *   oracle_gemv_w8a8          src/model_cuda_v2_shared.cu:465-501
+ *   oracle_matmul_f32         src/model_cuda_v2_shared.cu:10-19 (fp32 classifier)
  *   oracle_group_dots         the exact int32 group partials of :483-494
  *   oracle_dequant_matvec     float32 dequant-then-matvec (CPU baseline, OpenMP)
  *   oracle_gemv_*_f64         fp64 recomputes used as tolerance anchors
@@ -189,6 +190,26 @@ void oracle_gemv_w8a8_f64(double* y, const int8_t* xq, const float* xs,
       acc += (double)group_dot(w + r * n + g * gs, xq + g * gs, gs) *
              (double)s[r * ng + g];
     y[r] = acc * (double)*xs;
+  }
+}
+
+/* src/model_cuda_v2_shared.cu:10-19: one thread per row, sequentially over
+ * the columns, `val += w * x` contracted into an FFMA by nvcc. */
+void oracle_matmul_f32(float* y, const float* x, const float* w, long n, long d) {
+#pragma omp parallel for schedule(static)
+  for (long r = 0; r < d; ++r) {
+    float val = 0.0f;
+    for (long j = 0; j < n; ++j) val = fmaf(w[r * n + j], x[j], val);
+    y[r] = val;
+  }
+}
+
+void oracle_matmul_f64(double* y, const float* x, const float* w, long n, long d) {
+#pragma omp parallel for schedule(static)
+  for (long r = 0; r < d; ++r) {
+    double val = 0.0;
+    for (long j = 0; j < n; ++j) val += (double)w[r * n + j] * (double)x[j];
+    y[r] = val;
   }
 }
 

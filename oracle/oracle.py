@@ -9,6 +9,7 @@ import it.  It wraps ``liboracle.so`` (built from ``mli_oracle.c`` by
     quantize_activation     src/model_cuda_v2_shared.cu:429-455
     gemv_w8a32              src/model_cuda_v2_shared.cu:36-62
     gemv_w8a8               src/model_cuda_v2_shared.cu:465-501
+    matmul_f32              src/model_cuda_v2_shared.cu:10-19 (fp32 classifier)
     group_dots              the int32 group partials of :483-494
 
 Parity pins: ``tests/golden/`` holds the reference quantiser script's own
@@ -64,6 +65,8 @@ def lib():
             "oracle_gemm_w8a8": (None, [_f32p, _i8p, _f32p, _i8p, _f32p, _L, _L, _L, _I]),
             "oracle_gemv_w8a32_f64": (None, [_f64p, _f32p, _i8p, _f32p, _L, _L, _I]),
             "oracle_gemv_w8a8_f64": (None, [_f64p, _i8p, _f32p, _i8p, _f32p, _L, _L, _I]),
+            "oracle_matmul_f32": (None, [_f32p, _f32p, _f32p, _L, _L]),
+            "oracle_matmul_f64": (None, [_f64p, _f32p, _f32p, _L, _L]),
             "oracle_gemm_w8a8_f64": (None, [_f64p, _i8p, _f32p, _i8p, _f32p, _L, _L, _L, _I]),
             "oracle_group_dot_sums": (None, [_i64p, _i8p, _i8p, _i32p, _L, _L, _L, _I]),
             "oracle_dequant_matvec": (None, [_f32p, _f32p, _i8p, _f32p, _L, _L, _I]),
@@ -152,6 +155,21 @@ def gemv_w8a8_f64(xq, xs, w_q, w_s, group_size: int = 64):
     y = np.empty(d, np.float64)
     lib().oracle_gemv_w8a8_f64(y, _c(xq, np.int8), _c(xs, np.float32).reshape(-1), _c(w_q, np.int8),
                                _c(w_s, np.float32), n, d, group_size)
+    return y
+
+
+def matmul_f32(x, w):
+    """The reference's fp32 matmul, in its order (one sequential FMA chain per row)."""
+    d, n = w.shape
+    y = np.empty(d, np.float32)
+    lib().oracle_matmul_f32(y, _c(x, np.float32), _c(w, np.float32), n, d)
+    return y
+
+
+def matmul_f64(x, w):
+    d, n = w.shape
+    y = np.empty(d, np.float64)
+    lib().oracle_matmul_f64(y, _c(x, np.float32), _c(w, np.float32), n, d)
     return y
 
 

@@ -499,3 +499,38 @@ def test_invalid_arguments_raise():
 
 def test_no_device_errors_recorded():
     assert ops.device_error() == 0
+
+
+# fp32 GEMV (the reference's `matmul`, the classifier's launcher): the
+# classifier shape, config shapes, the generic path (n % 4 != 0, misaligned).
+@pytest.mark.parametrize("d,n,offset", [(128256, 2048, 0), (2048, 2048, 0), (300, 8192, 0), (37, 100, 0),
+                                        (64, 2048, 1), (5, 12288, 0), (3, 12800, 0)])
+def test_f32_gemv_parity(d, n, offset):
+    w = synth.weights_np(d, n, d + n)
+    x = synth.activation_np(n, d + n + 1)
+    wb = torch.zeros(d * n + offset, dtype=torch.float32, device=dev())
+    wb[offset:] = up(w.reshape(-1))
+    xb = torch.zeros(n + offset, dtype=torch.float32, device=dev())
+    xb[offset:] = up(x)
+    y = Guarded(d)
+    ops.matmul(y.t, xb.data_ptr() + 4 * offset, wb.data_ptr() + 4 * offset, n, d)
+    torch.cuda.synchronize()
+    got = y.check()
+    assert orc.max_abs_rel(got, orc.matmul_f32(x, w)) <= TOL_W8A32
+    assert orc.max_abs_rel(got, orc.matmul_f64(x, w)) <= TOL_W8A32
+
+
+def test_f32_gemv_through_dropin_shim():
+    import ctypes
+
+    from minillama_infra_b200._lib import DROPIN_SYMBOLS, dropin
+    d, n = 1000, 2048
+    w = synth.weights_np(d, n, 3)
+    x = synth.activation_np(n, 4)
+    tw, tx = up(w), up(x)
+    y = Guarded(d)
+    getattr(dropin(), DROPIN_SYMBOLS["matmul"])(ctypes.c_void_p(y.t.data_ptr()), ctypes.c_void_p(tx.data_ptr()),
+                                               ctypes.c_void_p(tw.data_ptr()), n, d)
+    torch.cuda.synchronize()
+    assert lib().mli_last_status() == 0
+    assert orc.max_abs_rel(y.check(), orc.matmul_f32(x, w)) <= TOL_W8A32

@@ -87,3 +87,115 @@ def test_sharded_classifier_bit_exact_two_gpus(form, fused):
         assert same, f"rank {rank}: gathered logits differ from the single-GPU GEMV"
         assert arg, f"rank {rank}: argmax differs"
         assert err == 0
+
+
+def _ffn_full(dev, form, dim, hidden):
+    """Weights of one Llama-3.2-1B FFN block, the same on every rank."""
+    from minillama_infra_b200 import synth
+
+    gate = synth.weights_gpu(hidden, dim, seed=301, device=dev)
+    up = synth.weights_gpu(hidden, dim, seed=302, device=dev)
+    down = synth.weights_gpu(dim, hidden, seed=303, device=dev)
+    x = synth.activation_gpu(dim, 304, dev, outliers=(form == "w8a8"))
+    return gate, up, down, x
+
+
+def _ffn_single_gpu(gate, up, down, x, form, dim, hidden):
+    from minillama_infra_b200.shard import ShardedFFN
+
+    ffn = ShardedFFN(gate[0], gate[1], up[0], up[1], down[0], down[1], dim, hidden, 0, 1, form=form)
+    xb = ffn.forward(x).clone()
+    hb = ffn.hidden_vector().clone()
+    torch.cuda.synchronize()
+    ffn.close()
+    return hb, xb
+
+
+@pytest.mark.parametrize("form", ["w8a32", "w8a8"])
+def test_ffn_block_one_gpu_matches_single_calls(form):
+    """The FFN block (world 1) against single GEMV calls and the reference's
+    elementwise silu_mul (src/model_cuda_v2_shared.cu:220-227) in fp32."""
+    import numpy as np
+
+    from minillama_infra_b200 import ops
+    from oracle import oracle as orc
+
+    dev = torch.device("cuda", 0)
+    dim, hidden = 2048, 8192
+    gate, up, down, x = _ffn_full(dev, form, dim, hidden)
+    hb, xb = _ffn_single_gpu(gate, up, down, x, form, dim, hidden)
+
+    def single(y, xv, w, n, d):
+        if form == "w8a32":
+            ops.matmul_int8(y, xv, w[0], w[1], n, d, 64)
+        else:
+            ops.matmul_dp4a_fused(y, xv, w[0], w[1], n, d, 64)
+
+    g = torch.empty(hidden, device=dev)
+    u = torch.empty(hidden, device=dev)
+    single(g, x, gate, dim, hidden)
+    single(u, x, up, dim, hidden)
+    h_ref = (g * (1.0 / (1.0 + torch.exp(-g)))) * u
+    xb_ref = torch.empty(dim, device=dev)
+    single(xb_ref, hb, down, hidden, dim)  # down on the block's own hb: identical input
+    torch.cuda.synchronize()
+    assert orc.max_abs_rel(hb.cpu().numpy(), h_ref.cpu().numpy()) <= 1e-6
+    assert np.array_equal(xb.cpu().numpy().view(np.uint32), xb_ref.cpu().numpy().view(np.uint32))
+    assert ops.device_error() == 0
+
+
+def _ffn_worker(rank, world, port, form, q):
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from minillama_infra_b200 import ops
+    from minillama_infra_b200.shard import ShardedFFN, row_shard
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        dim, hidden = 2048, 8192
+        gate, up, down, x = _ffn_full(dev, form, dim, hidden)
+        hb1, xb1 = _ffn_single_gpu(gate, up, down, x, form, dim, hidden)
+        hs, ds = row_shard(hidden, world, rank), row_shard(dim, world, rank)
+        ffn = ShardedFFN(gate[0][hs.r0:hs.r1].clone(), gate[1][hs.r0:hs.r1].clone(),
+                         up[0][hs.r0:hs.r1].clone(), up[1][hs.r0:hs.r1].clone(),
+                         down[0][ds.r0:ds.r1].clone(), down[1][ds.r0:ds.r1].clone(),
+                         dim, hidden, rank, world, form=form)
+        ok = True
+        for _ in range(3):
+            xb = ffn.forward(x)
+            torch.cuda.synchronize()
+            ok = ok and bool(torch.equal(xb.view(torch.int32), xb1.view(torch.int32)))
+            ok = ok and bool(torch.equal(ffn.hidden_vector().view(torch.int32), hb1.view(torch.int32)))
+        ffn.close()
+        q.put((rank, ok, ops.device_error()))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("form", ["w8a32", "w8a8"])
+def test_sharded_ffn_bit_exact_two_gpus(form):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ffn_worker, args=(r, world, port, form, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, ok, err in results:
+        assert ok, f"rank {rank}: gathered hb / xb differ from the single-GPU block"
+        assert err == 0
