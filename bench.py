@@ -190,35 +190,38 @@ def build_chain_independent(wl, form):
 
 
 def build_chain_decode(wl, form, device):
-    """The same weights in decode order, with the decode step's dependencies:
-    q/k/v read the attention norm's output, o reads q's output (standing in
-    for attention), gate/up run as one SwiGLU pair on the FFN norm's output
-    after o, and down reads the SwiGLU output and adds into the residual
-    stream; the next layer starts after down.  The two norms are outside this
-    path: fixed normalised vectors stand in for their outputs (each op still
-    waits for the ops its real input depends on)."""
+    """The same weights in decode order, as the GEMV part of a decode step of
+    the reference's forward pass (src/model_cuda_v2_shared.cu:380-415) with
+    its norms and residual adds fused in: q/k/v read RMSNorm(resid) (the norm
+    in their prologue), o reads q's output (standing in for attention, the one
+    piece of the layer outside this path) and adds into the residual stream,
+    gate/up read RMSNorm(resid) as one SwiGLU pair, down reads the SwiGLU
+    output and adds into the residual stream; the next layer waits for down.
+    One chain launch per step; every activation is handed over inside it."""
     names = ["q", "k", "v", "o", "gate", "up", "down"]
     calls = wl["calls"]
-    att_in = torch.from_numpy(synth.activation_np(2048, 4242, outliers=(form == "w8a8"))).to(device)
-    ffn_in = torch.from_numpy(synth.activation_np(2048, 4243, outliers=(form == "w8a8"))).to(device)
-    resid = torch.zeros(2048, dtype=torch.float32, device=device)
+    resid = torch.from_numpy(synth.activation_np(2048, 4242)).to(device)
+    rng = np.random.default_rng(4243)
+    norms = [[torch.from_numpy((1.0 + 0.1 * rng.standard_normal(2048)).astype(np.float32)).to(device)
+              for _ in range(2)] for _ in range(synth.LLAMA_1B_LAYERS)]
     outs = {nm: torch.empty(d, dtype=torch.float32, device=device) for nm, (_, d, _) in zip(names, synth.LLAMA_1B)}
-    src = {"q": att_in, "k": att_in, "v": att_in, "o": outs["q"], "gate": ffn_in, "up": ffn_in,
-           "down": outs["gate"]}
     chain = []
     for l in range(synth.LLAMA_1B_LAYERS):
         for i, nm in enumerate(names):
             _, d, n, q, s = calls[7 * l + i]
-            op = dict(form=chain_form(form), n=n, d=d, wait=7 * l + ops.DECODE_LAYER_WAITS[i], x=src[nm],
-                      y=outs.get(nm), w_q=q, w_s=s)
-            if nm == "gate":
-                op["epilogue"] = "swiglu"   # y = silu(gate) * up
+            op = dict(form=chain_form(form), n=n, d=d, wait=7 * l + ops.DECODE_LAYER_WAITS[i], w_q=q, w_s=s)
+            if nm in ("q", "k", "v"):
+                op.update(x=resid, norm_w=norms[l][0], y=outs[nm])
+            elif nm == "o":
+                op.update(x=outs["q"], y=resid, epilogue="add")
+            elif nm == "gate":
+                op.update(x=resid, norm_w=norms[l][1], y=outs["gate"], epilogue="swiglu")
             elif nm == "up":
-                op["y"] = None              # its rows feed the gate's SwiGLU
-            elif nm == "down":
-                op.update(y=resid, epilogue="add")
+                op.update(x=resid, norm_w=norms[l][1], y=None)
+            else:
+                op.update(x=outs["gate"], y=resid, epilogue="add")
             chain.append(op)
-    return ops.GemvChain(chain), resid
+    return ops.GemvChain(chain), (resid, norms, outs)
 
 
 class PipelinedSteps:
@@ -931,9 +934,10 @@ def llama1b_measure(args, wl, form, device, rank, world, sampler=None, side=True
                          "steps": side_steps}
         out["decode_chain"]["tok_s_gemv_only"] = round(1000.0 / out["decode_chain"]["ms_per_step"], 1)
         out["decode_chain"]["dependencies"] = (
-            "decode order: o after q/k/v, gate/up after o, down after gate/up, next layer after down; "
-            "gate/up run as one SwiGLU pair, down adds into the residual stream; fixed normalised "
-            "vectors stand in for the two RMSNorm outputs (not part of this path)")
+            "a decode step's layers without attention: q/k/v read RMSNorm(resid), o reads q's output "
+            "(standing in for attention) and adds into resid, gate/up read RMSNorm(resid) as one SwiGLU "
+            "pair, down adds into resid, the next layer after down; norms, SwiGLU and residual adds fused "
+            "into the GEMVs, activations handed over inside one launch")
         out["percall_graph"]["launch"] = "112 single-GEMV C-ABI calls in a CUDA graph, programmatic dependent launch"
         torch.cuda.synchronize()
         del g

@@ -130,7 +130,20 @@ int mli_gemv_f32(float* y, const float* x, const float* w, int n, int d, void* s
  * op reads its activation or writes its output (0 <= wait <= own index).  A
  * decode layer q, k, v, o, gate, up, down at chain index b..b+6 uses waits
  * b, b, b, b+3, b+4, b+4, b+6 (o after the attention of q/k/v, gate/up after
- * o, down after gate/up, the next layer after down). */
+ * o, down after gate/up, the next layer after down).
+ *
+ * An op whose x is the y of an earlier op of the chain reads that op's rows
+ * of this launch (the earlier op must lie in its wait prefix); any other x is
+ * read as it is when the launch starts.  An ADD op's y likewise starts from
+ * the latest earlier op writing the same y (in its wait prefix), else from
+ * y's contents at launch.
+ *
+ * norm_w (forms 0 and 2, may be NULL): the op's activation is
+ * norm_w[i] * (x[i] / sqrt(mean(x^2) + 1e-5)) -- the reference's
+ * rmsnorm_cuda (src/model_cuda_v2_shared.cu:74-96), and with an ADD op
+ * writing x the fused add + RMSNorm of :99-123 -- computed by every CTA from
+ * the whole of x (n <= 8192).  Within fp32 rounding of the reference (its sum
+ * of squares runs in another order). */
 typedef struct mli_gemv_op {
   int form;       /* 0 W8A32, 1 W8A8 (xq, xs given), 2 W8A8 quantising x */
   int n;          /* in-features: a multiple of 256 */
@@ -144,6 +157,7 @@ typedef struct mli_gemv_op {
   const float* xs;   /* form 1 */
   const int8_t* w_q;
   const float* w_s;
+  const float* norm_w; /* RMSNorm weights [n] of the activation, or NULL */
 } mli_gemv_op;
 
 typedef struct mli_chain mli_chain; /* opaque */

@@ -34,7 +34,7 @@ class GemvOp(ctypes.Structure):
     """struct mli_gemv_op (include/mli_gemv.h): one GEMV of a chain."""
     _fields_ = [("form", _I), ("n", _I), ("d", _I), ("group_size", _I), ("wait", _I),
                 ("epilogue", _I), ("y", _P), ("x", _P), ("xq", _P), ("xs", _P), ("w_q", _P),
-                ("w_s", _P)]
+                ("w_s", _P), ("norm_w", _P)]
 
 
 _OPS = ctypes.POINTER(GemvOp)

@@ -4,10 +4,10 @@
 // A Llama decode step is a chain of small GEMVs (per layer: q, k, v, o, gate,
 // up, down) whose activations depend on one another: o reads the attention
 // output of q/k/v, gate/up the normalised residual after o, down the SwiGLU of
-// gate/up, the next layer's q/k/v the residual after down.  Launched one by
-// one, every GEMV pays a kernel boundary (the previous grid drains, the next
-// one fills its pipeline), and a 1-4 MB GEMV streams for well under a
-// microsecond, so the boundaries, not HBM, set the step time.
+// gate/up, the next layer's q/k/v the normalised residual after down.
+// Launched one by one, every GEMV pays a kernel boundary (the previous grid
+// drains, the next one fills its pipeline), and a 1-4 MB GEMV streams for well
+// under a microsecond, so the boundaries, not HBM, set the step time.
 //
 // Here one CTA per SM streams the weights of the whole chain without a
 // kernel boundary:
@@ -15,35 +15,44 @@
 //  * Work units.  Every GEMV is cut into stages of whole rows (64 row slices
 //    of 1024 columns for W8A32, 32 of 2048 for W8A8: 64 KB of weights plus
 //    their scales), the stages of all GEMVs are numbered in chain order, and
-//    CTA c takes units c, c + G, c + 2G, ... (G = CTAs).  Each CTA moves its
-//    units through a ring of shared-memory slots with 1-D bulk copies;
-//    weights never depend on an activation, so the ring runs ahead across
-//    GEMV boundaries and across dependency waits.
-//  * Dependencies.  Op i names a prefix of the chain, ops [0, wait), that must
-//    be complete before it reads its activation (and before it writes its
-//    output).  Each op has a device counter of finished rows; a CTA adds its
-//    rows of an op once it has passed its last unit of that op (gpu-scope
-//    fence, atomic add), and before the first unit of an op whose prefix is
-//    not yet known to be complete it polls the counters with acquire loads,
-//    bounded by a time limit.  Units are processed in chain order by every
-//    CTA, so the earliest unfinished op never waits: with all CTAs resident
-//    (cooperative launch) the chain cannot deadlock.
-//  * Activations.  When the activation changes (a new "epoch": another
-//    vector, or the same vector after a dependency wait), the consumers read
-//    it with L2-coherent loads and prepare it: W8A32 as four int8 digit
-//    planes (digit_quad), fused W8A8 quantised (quant_quad) -- once per CTA
-//    into shared memory, or, when every warp owns its own slice of the row
-//    (W8A32 with n = 8192), by each warp in registers without a barrier.
-//    q/k/v (and gate/up) read one vector: one preparation.
-//  * Warp roles: consumer warps compute rows from the ring; a producer warp
-//    issues the bulk copies; a publisher warp accounts finished units, makes
-//    the rows visible (gpu-scope fence, counter add) and polls the counters an
-//    op waits for, so no consumer ever stalls on a global memory fence.
+//    each run of ops that adds no new dependency (a "phase") is spread over
+//    all CTAs.  Each CTA moves its units through a ring of shared-memory
+//    slots with 1-D bulk copies; weights never depend on an activation, so the
+//    ring runs ahead across GEMV boundaries and across dependency waits.
+//  * Dependencies travel with the data.  Every op writes each finished row
+//    twice: into its y, and into the chain's mirror of that op as one 8-byte
+//    word {value, tag}, tag = (launch sequence << 16) | op index, with a
+//    single relaxed 64-bit store (single-copy atomic: a reader sees the value
+//    and its tag together, and no fence is needed).  An op whose activation
+//    is an earlier op's output reads that op's mirror and retries every word
+//    until it carries the producer's tag: readiness and data arrive in the
+//    same L2 load.  An op waits for ops [0, wait) of the chain; the ones not
+//    implied by its activation's producer (whose rows were written only after
+//    ITS wait was met) are checked the same way, by their mirrors' tags (o
+//    waits for k and v, for instance).  Every wait is bounded in time and
+//    records a device error instead of hanging.
+//  * Activations.  When the activation changes the consumers load it
+//    (tag-checked, or plainly for an input that is ready at launch) and
+//    prepare it: an optional RMSNorm (weight * (x / sqrt(mean(x^2) + 1e-5)),
+//    the reference's rmsnorm_cuda / fused_add_rmsnorm_cuda before the q/k/v
+//    and gate/up projections, recomputed by every CTA from the whole vector),
+//    then W8A32 digit planes (digit_quad) or the fused W8A8 quantisation
+//    (quant_quad) -- once per CTA into shared memory, or, when every warp owns
+//    its own slice of the row (W8A32 with n = 8192, no norm), by each warp in
+//    registers without a barrier.
+//  * Every warp computes rows from the ring; the last one to finish with a
+//    slot stores its rows and refills the slot with the CTA's unit `ring`
+//    places ahead (eight warps of up to 255 registers, no producer warp).
 //  * Rows are computed exactly as in gemv_stream_kernel (same row kernels,
-//    same slice order), so each op's output is bit-identical to the
-//    corresponding mli_gemv_* call.
-//  * The last CTA to finish returns every counter to zero, so the next launch
-//    (or graph replay) starts clean without a host-side reset.
+//    same slice order), so an op without a norm prologue gives bit-identical
+//    output to the corresponding mli_gemv_* call.
+//  * Every CTA processes its units in chain order and a unit only waits for
+//    earlier ops, so the earliest unfinished op never waits: with all CTAs
+//    resident (cooperative launch) the chain cannot deadlock.  The last CTA to
+//    finish advances the launch sequence, so the next launch (or graph
+//    replay) needs no host-side reset and never takes an old row for a new
+//    one.
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 
@@ -58,46 +67,57 @@ constexpr int kMaxRing = 6;
 constexpr int kHeader = 256;
 constexpr int kMaxSlices = 8;
 constexpr int kMaxOps = 1 << 16;
+constexpr unsigned kSeqPeriod = 65535;  // the launch sequence runs 1 .. 65535
 
-// Row epilogues: store y = v; add into y (the residual add that follows the
-// reference's down projection, src/model_cuda_v2_shared.cu:215-218, :414);
-// SwiGLU with the next op (gate = this op, up = the next one, stored as
-// (g * (1 / (1 + expf(-g)))) * u, :220-227, :410); the companion up op of a
-// SwiGLU pair (no units of its own).
+// Row epilogues: store y = v; add into y (the residual adds after the
+// reference's o and down projections, src/model_cuda_v2_shared.cu:99-118,
+// :215-218, :414); SwiGLU with the next op (gate = this op, up = the next one,
+// stored as (g * (1 / (1 + expf(-g)))) * u, :220-227, :410); the companion up
+// op of a SwiGLU pair (no units of its own).
 constexpr int kEpiStore = 0, kEpiAdd = 1, kEpiSwiglu = 2, kEpiCompanion = 3;
 
-// Device-side descriptor of one GEMV of the chain, 64 bytes (geometry
+// Device-side descriptor of one GEMV of the chain, 96 bytes (geometry
 // precomputed on the host, as plan_stream does for the single-GEMV kernel).
 // Kernels copy the table into shared memory when it fits.
 struct Op {
   float* y;
-  const void* act;   // fp32 x (W8A32, fused W8A8) or int8 xq (W8A8)
-  const float* xs;   // W8A8 activation scale
+  const void* act;       // fp32 x (W8A32, fused W8A8) or int8 xq (W8A8)
+  const float* xs;       // W8A8 activation scale
   const int8_t* w;
   const float* s;
-  int n, d;          // in / out features
-  int unit_base;     // first work unit of this op
-  int wait;          // ops [0, wait) complete before this op reads its activation
-  int epoch;         // ops of one epoch read the same activation
-  uint8_t S;         // slices per row
-  uint8_t epi;       // kEpi*: how a finished row is stored
-  uint16_t R;        // rows per stage (a SwiGLU stage: R/2 gate rows, then the R/2 up rows)
+  const float* norm_w;   // RMSNorm weights of the activation (nullptr: none)
+  int n, d;              // in / out features
+  int unit_base;         // first work unit of this op
+  int wait;              // ops [0, wait) complete before this op reads its activation
+  int epoch;             // ops of one epoch read the same prepared activation
+  int src;               // op whose mirror holds the activation (-1: `act`, ready at launch)
+  int base;              // ADD: op whose mirror holds y before this op (-1: y itself)
+  int mirror;            // word offset of this op's mirror (-1: none)
+  int poll_first;        // other ops of the wait prefix to check: polls[poll_first, +poll_count)
+  int poll_count;
+  uint8_t S;             // slices per row
+  uint8_t epi;           // kEpi*: how a finished row is stored
+  uint16_t R;            // rows per stage (a SwiGLU stage: R/2 gate rows, then the R/2 up rows)
+  uint32_t pad;
   __host__ __device__ const float* x() const { return static_cast<const float*>(act); }
   // output rows per work unit
   __host__ __device__ int Ru() const { return epi == kEpiSwiglu ? R / 2 : R; }
   __host__ __device__ const int8_t* xq() const { return static_cast<const int8_t*>(act); }
   __host__ __device__ int G() const { return n / kGroup; }
 };
-static_assert(sizeof(Op) == 64, "chain op descriptor is 64 bytes");
+static_assert(sizeof(Op) == 96, "chain op descriptor is 96 bytes");
 
 struct Args {
   const Op* ops;        // global copy of the table
   const int* phases;    // [n_phases + 1] first unit of every phase, then the unit count
-  uint32_t table_off;   // shared-memory copy of ops, then phases (0: read them from global)
+  const int* polls;     // [n_polls] op indices checked by tag (see Op::poll_first)
+  uint32_t table_off;   // shared-memory copy of ops, phases, polls (0: read them from global)
   int n_phases;
   int count;
+  int n_polls;
   int units;            // stages of all ops
-  unsigned* done;       // [count] finished rows per op (zero between launches)
+  uint64_t* mirror;     // every op's rows as {value, tag} words
+  unsigned* seq;        // launch sequence, 1 .. kSeqPeriod (advanced by the last CTA)
   unsigned* finished;   // CTAs finished in this launch
   int ring;
   uint32_t slot_bytes;  // ring slot: the largest stage of the chain
@@ -105,44 +125,80 @@ struct Args {
   int part_stride;      // floats of split-K partials per slot
 };
 
-// Shared-memory header: full[6] @0, empty[6] @48, free[6] @96, per-slot
-// warp counters @144, flags @176, reduction scratch (one float per consumer
-// warp) @192.
+// Shared-memory header: full[6] @0, free[6] @48, per-slot warp counters @96,
+// flags @128..140, the launch sequence @140, two reduction arrays of one
+// float per consumer warp @160 (quantiser) and @208 (RMSNorm).
 struct Smem {
   uint64_t* full;   // weights of the slot's unit landed (bulk copy)
-  uint64_t* empty;  // consumers finished the slot's unit and stored its rows
-  uint64_t* free;   // the publisher has accounted for it: the slot may be refilled
+  uint64_t* free;   // (unused: the last warp of a slot refills it)
   int* counters;
   volatile int* broken;
   int* issued;
   int* last_cta;
-  int* dep_known;   // ops [0, *dep_known) are known complete (publisher -> consumers)
+  unsigned* seq;
   float* red;
+  float* red2;
   __device__ explicit Smem(unsigned char* b)
       : full(reinterpret_cast<uint64_t*>(b)),
-        empty(reinterpret_cast<uint64_t*>(b + 48)),
-        free(reinterpret_cast<uint64_t*>(b + 96)),
-        counters(reinterpret_cast<int*>(b + 144)),
-        broken(reinterpret_cast<volatile int*>(b + 176)),
-        issued(reinterpret_cast<int*>(b + 180)),
-        last_cta(reinterpret_cast<int*>(b + 184)),
-        dep_known(reinterpret_cast<int*>(b + 188)),
-        red(reinterpret_cast<float*>(b + 192)) {}
+        free(reinterpret_cast<uint64_t*>(b + 48)),
+        counters(reinterpret_cast<int*>(b + 96)),
+        broken(reinterpret_cast<volatile int*>(b + 128)),
+        issued(reinterpret_cast<int*>(b + 132)),
+        last_cta(reinterpret_cast<int*>(b + 136)),
+        seq(reinterpret_cast<unsigned*>(b + 140)),
+        red(reinterpret_cast<float*>(b + 160)),
+        red2(reinterpret_cast<float*>(b + 208)) {}
 };
+static_assert(208 + 12 * 4 <= kHeader, "shared-memory header");
 
-__device__ __forceinline__ void st_release_cta(int* p, int v) {
-  asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
-}
-__device__ __forceinline__ int ld_acquire_cta(const int* p) {
-  int v;
-  asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
-  return v;
+__host__ __device__ __forceinline__ uint32_t row_tag(unsigned seq, int op) {
+  return (seq << 16) | static_cast<uint32_t>(op & 0xffff);
 }
 
-__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ void ld_relaxed_v2(const uint64_t* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_relaxed_b64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
+}
+__device__ __forceinline__ void st_relaxed_b64(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t tagged(float v, uint32_t tag) {
+  return (static_cast<uint64_t>(tag) << 32) | __float_as_uint(v);
+}
+__device__ __forceinline__ bool has_tag(uint64_t w, uint32_t tag) {
+  return static_cast<uint32_t>(w >> 32) == tag;
+}
+__device__ __forceinline__ float word_value(uint64_t w) {
+  return __uint_as_float(static_cast<uint32_t>(w));
+}
+
+// Four consecutive tagged words already loaded: their values when all four
+// carry `tag`; otherwise they are reloaded (16-byte aligned p) until they do,
+// false once `kWaitLimitNs` have passed since t0.
+__device__ __forceinline__ bool all_tagged4(uint64_t w0, uint64_t w1, uint64_t w2, uint64_t w3, uint32_t tag) {
+  return has_tag(w0, tag) && has_tag(w1, tag) && has_tag(w2, tag) && has_tag(w3, tag);
+}
+__device__ __noinline__ bool reload_tagged4(const uint64_t* p, uint32_t tag, float4* v, uint64_t t0) {
+  uint64_t w0, w1, w2, w3;
+  do {
+    if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+    ld_relaxed_v2(p, w0, w1);
+    ld_relaxed_v2(p + 2, w2, w3);
+  } while (!all_tagged4(w0, w1, w2, w3, tag));
+  *v = make_float4(word_value(w0), word_value(w1), word_value(w2), word_value(w3));
+  return true;
+}
+__device__ __forceinline__ bool finish_tagged4(const uint64_t* p, uint64_t w0, uint64_t w1, uint64_t w2,
+                                               uint64_t w3, uint32_t tag, float4& v, uint64_t t0) {
+  if (all_tagged4(w0, w1, w2, w3, tag)) {
+    v = make_float4(word_value(w0), word_value(w1), word_value(w2), word_value(w3));
+    return true;
+  }
+  return reload_tagged4(p, tag, &v, t0);
 }
 
 // Op holding global unit u, searching forward from op `o` (units grow).
@@ -216,41 +272,96 @@ __device__ __forceinline__ void issue_unit(const Args& a, const Op* ops, unsigne
   }
 }
 
-__device__ __forceinline__ void fence_acq_rel_gpu() {
-  asm volatile("fence.acq_rel.gpu;" ::: "memory");
-}
-__device__ __forceinline__ void red_add_relaxed_gpu(unsigned* p, unsigned v) {
-  asm volatile("red.relaxed.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// Publisher lane: waits until ops [from, to) have all their rows (acquire
-// loads), bounded in time.
-__device__ __forceinline__ bool wait_ops(const Args& a, const Op* ops, int from, int to) {
+// Consumer threads check, by their mirrors' tags, that every row of the ops
+// polls[first, first + count) was written in this launch.  False if a row did
+// not arrive in time.
+template <int kT>
+__device__ __forceinline__ bool poll_ops(const Args& a, const Op* ops, const int* polls, int first, int count,
+                                         unsigned seq) {
   const uint64_t t0 = global_timer_ns();
-  for (int j = from; j < to; ++j) {
-    const unsigned target = static_cast<unsigned>(ops[j].d);
-    while (ld_acquire_gpu(a.done + j) < target)
-      if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+  for (int p = first; p < first + count; ++p) {
+    const int j = polls[p];
+    const Op& q = ops[j];
+    const uint32_t tag = row_tag(seq, j);
+    const uint64_t* m = a.mirror + q.mirror;
+    for (int r = threadIdx.x; r < q.d; r += kT)
+      while (!has_tag(ld_relaxed_b64(m + r), tag))
+        if (global_timer_ns() - t0 > kWaitLimitNs) return false;
   }
   return true;
 }
 
 // ---------------------------------------------------------------------------
-// Activation preparation.  The activation was written by other SMs of this
-// launch (or before it): L2-coherent loads, every load of a thread in flight
-// before the first is used.
+// Activation preparation.  A produced activation is read from its producer's
+// mirror with tag checks, one that is ready at launch with L2 loads; every
+// load of a thread is in flight before the first is used.
 // ---------------------------------------------------------------------------
 constexpr int kPre = 8;  // float4 of activation held per consumer thread
 
 // Shared preparation: consumer thread t holds columns 4t + 4 kT j, j < kPre
-// (the whole activation for n <= 4 kT kPre).
+// (the whole activation for n <= 4 kT kPre).  False on a timeout.
 template <int kT>
-__device__ __forceinline__ void cta_x_load(const float* x, int n, float4 (&v)[kPre]) {
+__device__ __forceinline__ bool cta_x_load(const Op& op, const uint64_t* m, uint32_t tag, float4 (&v)[kPre]) {
   const int t = static_cast<int>(threadIdx.x);
+  const int n = op.n;
+  if (m == nullptr) {
+#pragma unroll
+    for (int j = 0; j < kPre; ++j) {
+      const int c = 4 * kT * j + 4 * t;
+      v[j] = c < n ? __ldcg(reinterpret_cast<const float4*>(op.x() + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    return true;
+  }
+  uint64_t w[kPre][4];
 #pragma unroll
   for (int j = 0; j < kPre; ++j) {
     const int c = 4 * kT * j + 4 * t;
-    v[j] = c < n ? __ldcg(reinterpret_cast<const float4*>(x + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (c < n) {
+      ld_relaxed_v2(m + c, w[j][0], w[j][1]);
+      ld_relaxed_v2(m + c + 2, w[j][2], w[j][3]);
+    }
+  }
+  const uint64_t t0 = global_timer_ns();
+  bool ok = true;
+#pragma unroll
+  for (int j = 0; j < kPre; ++j) {
+    const int c = 4 * kT * j + 4 * t;
+    v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (c < n && !finish_tagged4(m + c, w[j][0], w[j][1], w[j][2], w[j][3], tag, v[j], t0)) ok = false;
+  }
+  return ok;
+}
+
+// RMSNorm of the held activation (the reference's rmsnorm_kernel,
+// src/model_cuda_v2_shared.cu:74-89): ss = 1 / sqrt(sum(x^2) / n + 1e-5),
+// x = weight * (ss * x).  The sum runs in one fixed order (per thread, the
+// warp butterfly, warps in order), so every CTA normalises identically.
+template <int kT>
+__device__ __forceinline__ void cta_rmsnorm(float4 (&v)[kPre], int n, const float* weight, float* red) {
+  constexpr int kW = kT / 32;
+  const int t = static_cast<int>(threadIdx.x);
+  float ssq = 0.f;
+#pragma unroll
+  for (int j = 0; j < kPre; ++j) {
+    ssq = fmaf(v[j].x, v[j].x, ssq);
+    ssq = fmaf(v[j].y, v[j].y, ssq);
+    ssq = fmaf(v[j].z, v[j].z, ssq);
+    ssq = fmaf(v[j].w, v[j].w, ssq);
+  }
+  ssq = warp_sum(ssq);
+  if ((t & 31) == 0) red[t >> 5] = ssq;
+  named_sync<kT>();
+  float sum = red[0];
+#pragma unroll
+  for (int w = 1; w < kW; ++w) sum += red[w];
+  const float ss = 1.0f / sqrtf(sum / static_cast<float>(n) + 1e-5f);
+#pragma unroll
+  for (int j = 0; j < kPre; ++j) {
+    const int c = 4 * kT * j + 4 * t;
+    if (c < n) {
+      const float4 g = __ldg(reinterpret_cast<const float4*>(weight + c));
+      v[j] = make_float4(g.x * (ss * v[j].x), g.y * (ss * v[j].y), g.z * (ss * v[j].z), g.w * (ss * v[j].w));
+    }
   }
 }
 
@@ -267,7 +378,8 @@ __device__ __forceinline__ void cta_digits(const float4 (&v)[kPre], int n, int8_
 }
 
 // Fused W8A8: the quantised activation into shared memory, bit-identical to
-// x_quant_prologue; from the held values when they cover n, else read twice.
+// x_quant_prologue; from the held values when they cover n, else (an input
+// ready at launch, n > 4 kT kPre) read a second time.
 template <int kT>
 __device__ __forceinline__ float cta_quant(const float4 (&v)[kPre], const float* x, int n, int8_t* xq,
                                            float* red) {
@@ -308,14 +420,42 @@ __device__ __forceinline__ float cta_quant(const float4 (&v)[kPre], const float*
 
 // Per-warp preparation (W8A32, when no two warps share a slice): the lane's
 // chunks k = 0, 1 of its slice, 16 columns each at col0 + 512k, as
-// v[4k + j] = columns col0 + 512k + 4j .. + 3.
-__device__ __forceinline__ void warp_x_load(const float* x, int col0, unsigned vmask, float4 (&v)[kPre]) {
+// v[4k + j] = columns col0 + 512k + 4j .. + 3.  False on a timeout.
+__device__ __forceinline__ bool warp_x_load(const Op& op, const uint64_t* m, uint32_t tag, int col0,
+                                            unsigned vmask, float4 (&v)[kPre]) {
+  if (m == nullptr) {
+#pragma unroll
+    for (int k = 0; k < 2; ++k)
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        v[4 * k + j] = ((vmask >> k) & 1u)
+                           ? __ldcg(reinterpret_cast<const float4*>(op.x() + col0 + 512 * k + 4 * j))
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+    return true;
+  }
+  uint64_t w[kPre][4];
 #pragma unroll
   for (int k = 0; k < 2; ++k)
 #pragma unroll
     for (int j = 0; j < 4; ++j)
-      v[4 * k + j] = ((vmask >> k) & 1u) ? __ldcg(reinterpret_cast<const float4*>(x + col0 + 512 * k + 4 * j))
-                                        : make_float4(0.f, 0.f, 0.f, 0.f);
+      if ((vmask >> k) & 1u) {
+        const uint64_t* p = m + col0 + 512 * k + 4 * j;
+        ld_relaxed_v2(p, w[4 * k + j][0], w[4 * k + j][1]);
+        ld_relaxed_v2(p + 2, w[4 * k + j][2], w[4 * k + j][3]);
+      }
+  const uint64_t t0 = global_timer_ns();
+  bool ok = true;
+#pragma unroll
+  for (int k = 0; k < 2; ++k)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[4 * k + j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      const uint64_t(&q)[4] = w[4 * k + j];
+      if (((vmask >> k) & 1u) &&
+          !finish_tagged4(m + col0 + 512 * k + 4 * j, q[0], q[1], q[2], q[3], tag, v[4 * k + j], t0))
+        ok = false;
+    }
+  return ok;
 }
 
 // The lane's digit planes of chunks 0, 1 in registers.  The quad of lanes
@@ -391,12 +531,10 @@ struct Role {
   }
 };
 
-// Warps 0 .. kW-1 consume (kRB rows per warp per stage), warp kW is the
-// producer (bulk copies), warp kW + 1 the publisher (completion counters and
-// dependency polls).  Consumers never wait on global memory ordering: the
-// gpu-scope fences and the polls run on the publisher warp.
+// kW warps, kRB rows per warp per stage; the last warp to finish with a slot
+// refills it.
 template <Form F, int kW, int kRB, bool kEpi>
-__global__ void __launch_bounds__((kW + 2) * 32, 1) gemv_chain_kernel(const Args a) {
+__global__ void __launch_bounds__(kW * 32, 1) gemv_chain_kernel(const Args a) {
   constexpr int kT = kW * 32;  // consumer threads
   extern __shared__ __align__(1024) unsigned char smem[];
   Smem sm(smem);
@@ -408,102 +546,50 @@ __global__ void __launch_bounds__((kW + 2) * 32, 1) gemv_chain_kernel(const Args
   if (threadIdx.x == 0) {
     for (int i = 0; i < a.ring; ++i) {
       mbar_init(&sm.full[i], 1);
-      mbar_init(&sm.empty[i], 1);
-      mbar_init(&sm.free[i], 1);
       sm.counters[i] = 0;
     }
     *sm.broken = 0;
     *sm.last_cta = 0;
     *sm.issued = 0;
-    *sm.dep_known = 0;
+    *sm.seq = __ldcg(a.seq);
     fence_barrier_init();
   }
   if (a.table_off != 0) {
     const uint4* src = reinterpret_cast<const uint4*>(a.ops);
     uint4* dst = reinterpret_cast<uint4*>(smem + a.table_off);
-    for (int i = threadIdx.x; i < a.count * 4; i += blockDim.x) dst[i] = __ldg(src + i);
+    for (int i = threadIdx.x; i < a.count * 6; i += blockDim.x) dst[i] = __ldg(src + i);
     int* pdst = reinterpret_cast<int*>(smem + a.table_off + sizeof(Op) * a.count);
     for (int i = threadIdx.x; i <= a.n_phases; i += blockDim.x) pdst[i] = __ldg(a.phases + i);
+    for (int i = threadIdx.x; i < a.n_polls; i += blockDim.x) pdst[a.n_phases + 1 + i] = __ldg(a.polls + i);
   }
   __syncthreads();
   const Op* ops = a.table_off != 0 ? reinterpret_cast<const Op*>(smem + a.table_off) : a.ops;
   const int* phases =
       a.table_off != 0 ? reinterpret_cast<const int*>(smem + a.table_off + sizeof(Op) * a.count) : a.phases;
+  const int* polls = a.table_off != 0 ? phases + a.n_phases + 1 : a.polls;
   const int cnt = cta_units(phases, a.n_phases, cta, grid);
+  const unsigned seq = *sm.seq;
 
-  if (warp == kW) {
-    // ---- producer: unit i into slot i % ring once the publisher freed it
-    if (lane == 0) {
-      int o = 0;
-      Cursor cur(phases, a.n_phases, cta, grid);
-      for (int i = 0; i < cnt; ++i, cur.next()) {
-        const int slot = i % a.ring;
-        if (i >= a.ring && !mbar_wait_bounded(&sm.free[slot], ((i / a.ring) - 1) & 1, kWaitLimitNs)) {
-          record_device_error(kDevStageTimeout);
-          *sm.broken = 1;
-        }
-        if (*sm.broken) break;
-        const int u = cur.u;
-        o = find_op(ops, a.count, u, o);
-        fence_proxy_async_smem();  // consumers' reads of the slot precede the copy's writes
-        issue_unit<kEpi>(a, ops, ring, sm.full, o, u, slot);
-        *sm.issued = i + 1;
-      }
+  if (threadIdx.x == 0) {
+    // the first `ring` units; every later one is issued by the warp that frees its slot
+    int o = 0;
+    Cursor cur(phases, a.n_phases, cta, grid);
+    for (int i = 0; i < cnt && i < a.ring; ++i, cur.next()) {
+      o = find_op(ops, a.count, cur.u, o);
+      issue_unit<kEpi>(a, ops, ring, sm.full, o, cur.u, i);
+      *sm.issued = i + 1;
     }
-  } else if (warp == kW + 1) {
-    // ---- publisher: per unit in order, the dependency of its op (if the
-    // consumers will wait for one), then its completion; a CTA's rows of an
-    // op are published once it has passed its last unit of that op.
-    int o = 0, cur = -1, known = 0;
-    unsigned pending = 0;
-    Cursor it(phases, a.n_phases, cta, grid);
-    for (int i = 0; i < cnt; ++i) {
-      const int u = it.u;
-      it.next();  // now at the CTA's next unit (if any)
-      o = find_op(ops, a.count, u, o);
-      const Op& op = ops[o];
-      if (o != cur) {
-        cur = o;
-        if (op.wait > known) {
-          if (lane == 0 && !*sm.broken && !wait_ops(a, ops, known, op.wait)) {
-            record_device_error(kDevChainTimeout);
-            *sm.broken = 1;
-          }
-          known = op.wait;
-          __syncwarp();
-          if (lane == 0) st_release_cta(sm.dep_known, known);
-        }
-      }
-      if (lane == 0) {
-        const int slot = i % a.ring;
-        if (!mbar_wait_bounded(&sm.empty[slot], (i / a.ring) & 1, kWaitLimitNs)) {
-          record_device_error(kDevStageTimeout);
-          *sm.broken = 1;
-        }
-        mbar_arrive(&sm.free[slot]);
-        const int ru = kEpi ? op.Ru() : static_cast<int>(op.R);
-        pending += static_cast<unsigned>(min(ru, op.d - (u - op.unit_base) * ru));
-        // the CTA's next unit belongs to a later op, or there is none
-        const bool last_of_op = i + 1 == cnt || (o + 1 < a.count && ops[o + 1].unit_base <= it.u);
-        if (last_of_op) {
-          if (!*sm.broken) {
-            fence_acq_rel_gpu();  // with the add: release of the rows (stored by consumer warps)
-            red_add_relaxed_gpu(a.done + o, pending);
-            if (kEpi && op.epi == kEpiSwiglu) red_add_relaxed_gpu(a.done + o + 1, pending);  // its companion
-          }
-          pending = 0;
-        }
-      }
-      __syncwarp();
-    }
-  } else {
-    // ---- consumers
+  }
+  {
     constexpr int K = chunks_per_lane(F);
     constexpr int kSlice = slice_cols(F);
     constexpr int kLanesPerRow = 32 / kRB;
     int o = 0, cur = -1, known = 0, epoch = -1;
     int n = 0, d = 0, Gr = 0, S = 1, R = 0, Ru = 0, epi = kEpiStore, base = 0;
     float* y = nullptr;
+    uint64_t* my_mirror = nullptr;
+    const uint64_t* base_mirror = nullptr;
+    uint32_t my_tag = 0, base_tag = 0;
     int sl = 0, wj = 0;
     bool warp_on = false;
     unsigned vmask = 0;
@@ -514,27 +600,26 @@ __global__ void __launch_bounds__((kW + 2) * 32, 1) gemv_chain_kernel(const Args
     float4 pre[kPre];  // the activation's loads while it is prepared
 
     Cursor it(phases, a.n_phases, cta, grid);
-    for (int i = 0; i < cnt; ++i, it.next()) {
+    Cursor ahead(phases, a.n_phases, cta, grid);  // unit i + ring, the slot's next
+    for (int i = 0; i < a.ring; ++i) ahead.next();
+    int o_ahead = 0;
+    for (int i = 0; i < cnt; ++i, it.next(), ahead.next()) {
       const int u = it.u;
       o = find_op(ops, a.count, u, o);
       if (o != cur) {
         const Op& op = ops[o];
         const int wait = op.wait, ep = op.epoch;
-        if (wait > known) {
-          // The publisher polls the counters; each warp waits for its word.
-          if (lane == 0) {
-            const uint64_t t0 = global_timer_ns();
-            while (ld_acquire_cta(sm.dep_known) < wait && !*sm.broken) {
-              if (global_timer_ns() - t0 > 2 * kWaitLimitNs) {
-                record_device_error(kDevChainTimeout);
-                *sm.broken = 1;
-              }
-            }
-          }
-          __syncwarp();
-          known = wait;
+        bool fail = false;
+        if (wait > known && op.poll_count > 0) {
+          // ops of the wait prefix that the activation's producer does not imply
+          fail = !poll_ops<kT>(a, ops, polls, op.poll_first, op.poll_count, seq);
+          fail = named_sync_or<kT>(fail);
         }
         n = op.n; d = op.d; Gr = op.G(); R = op.R; base = op.unit_base; y = op.y;
+        my_mirror = op.mirror >= 0 ? a.mirror + op.mirror : nullptr;
+        my_tag = row_tag(seq, o);
+        base_mirror = op.base >= 0 ? a.mirror + ops[op.base].mirror : nullptr;
+        base_tag = row_tag(seq, op.base);
         if constexpr (kEpi) {
           Ru = op.Ru();
           epi = op.epi;
@@ -546,6 +631,8 @@ __global__ void __launch_bounds__((kW + 2) * 32, 1) gemv_chain_kernel(const Args
           const Role<F, kW> role(op, warp, lane);
           S = op.S; sl = role.sl; wj = role.wj; warp_on = role.on; vmask = role.vmask;
           const int col0 = role.col0;
+          const uint64_t* src_m = op.src >= 0 ? a.mirror + ops[op.src].mirror : nullptr;
+          const uint32_t src_tag = row_tag(seq, op.src);
           if constexpr (F == Form::kW8A8) {
             xscale = __ldcg(op.xs);
 #pragma unroll
@@ -553,13 +640,14 @@ __global__ void __launch_bounds__((kW + 2) * 32, 1) gemv_chain_kernel(const Args
               xv[k] = ((vmask >> k) & 1u)
                           ? __ldcg(reinterpret_cast<const uint4*>(op.xq() + col0 + 512 * k))
                           : make_uint4(0, 0, 0, 0);
-          } else if (F == Form::kW8A32 && op.S == kW) {
+          } else if (F == Form::kW8A32 && op.S == kW && op.norm_w == nullptr) {
             // every warp owns its slice: prepare it in registers, no barrier
-            warp_x_load(op.x(), col0, vmask, pre);
+            if (!warp_x_load(op, src_m, src_tag, col0, vmask, pre)) fail = true;
             if constexpr (F == Form::kW8A32) warp_digits(pre, vmask, xd, fac);
           } else {
-            cta_x_load<kT>(op.x(), n, pre);
-            named_sync<kT>();  // every consumer is done reading the shared region
+            if (!cta_x_load<kT>(op, src_m, src_tag, pre)) fail = true;
+            fail = named_sync_or<kT>(fail);  // also: every consumer is done reading the shared region
+            if (op.norm_w != nullptr) cta_rmsnorm<kT>(pre, n, op.norm_w, sm.red2);
             if constexpr (F == Form::kW8A32) {
               int8_t* planes = reinterpret_cast<int8_t*>(smem + a.x_off);
               float* facs = reinterpret_cast<float*>(planes + 4 * n);
@@ -585,6 +673,11 @@ __global__ void __launch_bounds__((kW + 2) * 32, 1) gemv_chain_kernel(const Args
             }
           }
         }
+        if (fail) {
+          record_device_error(kDevChainTimeout);
+          *sm.broken = 1;
+        }
+        if (wait > known) known = wait;
         cur = o;
       }
       const int slot = i % a.ring;
@@ -618,7 +711,8 @@ __global__ void __launch_bounds__((kW + 2) * 32, 1) gemv_chain_kernel(const Args
         }
       }
       // The last warp to finish with this slot sums the slices of its rows in
-      // slice order, stores them and hands the slot to the publisher.
+      // slice order, stores them (into y and, tagged, into the op's mirror)
+      // and frees the slot.
       __syncwarp();
       int last = 0;
       if (lane == 0) {
@@ -629,6 +723,8 @@ __global__ void __launch_bounds__((kW + 2) * 32, 1) gemv_chain_kernel(const Args
       }
       if (__shfl_sync(0xffffffffu, last, 0)) {
         if (!*sm.broken) {
+          bool late = false;
+          const uint64_t t0 = global_timer_ns();
           for (int rr = lane; rr < rows; rr += 32) {
             float v = part[rr * S];
             for (int s2 = 1; s2 < S; ++s2) v += part[rr * S + s2];
@@ -639,19 +735,40 @@ __global__ void __launch_bounds__((kW + 2) * 32, 1) gemv_chain_kernel(const Args
               v *= (1.0f / (1.0f + expf(-v)));
               v *= up;
             } else if (kEpi && epi == kEpiAdd) {
-              v = __ldcg(y + row0 + rr) + v;
+              float b;
+              if (base_mirror != nullptr) {
+                uint64_t w = ld_relaxed_b64(base_mirror + row0 + rr);
+                while (!has_tag(w, base_tag) && !late) {
+                  late = global_timer_ns() - t0 > kWaitLimitNs;
+                  w = ld_relaxed_b64(base_mirror + row0 + rr);
+                }
+                b = word_value(w);
+              } else {
+                b = __ldcg(y + row0 + rr);
+              }
+              v = b + v;
             }
             y[row0 + rr] = v;
+            if (my_mirror != nullptr) st_relaxed_b64(my_mirror + row0 + rr, tagged(v, my_tag));
+          }
+          if (late) {
+            record_device_error(kDevChainTimeout);
+            *sm.broken = 1;
           }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.empty[slot]);
+        if (lane == 0 && i + a.ring < cnt && !*sm.broken) {
+          o_ahead = find_op(ops, a.count, ahead.u, o_ahead);
+          fence_proxy_async_smem();  // the warps' reads of the slot precede the copy's writes
+          issue_unit<kEpi>(a, ops, ring, sm.full, o_ahead, ahead.u, slot);
+          *sm.issued = i + a.ring + 1;
+        }
       }
     }
   }
 
   __syncthreads();
-  if (threadIdx.x == kW * 32) {
+  if (threadIdx.x == 0) {
     // After an error, copies still in flight land before the CTA exits.
     const int iss = *sm.issued;
     for (int s = 0; s < a.ring && s < iss; ++s) {
@@ -662,11 +779,11 @@ __global__ void __launch_bounds__((kW + 2) * 32, 1) gemv_chain_kernel(const Args
     *sm.last_cta = atomicAdd(a.finished, 1u) == gridDim.x - 1;
   }
   __syncthreads();
-  // The last CTA returns the counters to zero for the next launch: every
-  // other CTA has left its loops, so nobody reads them any more.
-  if (*sm.last_cta) {
-    for (int j = threadIdx.x; j < a.count; j += (kW + 2) * 32) a.done[j] = 0;
-    if (threadIdx.x == 0) *a.finished = 0;
+  // The last CTA advances the launch sequence for the next launch: every
+  // other CTA has read this launch's value and left its loops.
+  if (*sm.last_cta && threadIdx.x == 0) {
+    *a.finished = 0;
+    *a.seq = seq % kSeqPeriod + 1;
   }
 }
 
@@ -684,6 +801,8 @@ struct Variant {
 struct Plan {
   std::vector<Op> ops;
   std::vector<int> phases;  // first unit of every phase, then the unit count
+  std::vector<int> polls;   // ops checked by tag, per op a run (Op::poll_first)
+  size_t mirror_words = 0;
   Args args = {};
   Variant v = {};
   size_t smem = 0;
@@ -706,6 +825,10 @@ Variant pick_variant(int form, unsigned flags) {
   return {8, a32 ? 8 : 4, 1, false};
 }
 
+// The activation held by the consumers (4 kT kPre columns) bounds ops that
+// prepare the whole vector in shared memory.
+constexpr int kMaxHeldCols = 4 * 8 * 32 * kPre;
+
 // Validates the op list and lays out the chain.  Returns MLI_OK,
 // MLI_ERR_INVALID_ARG or MLI_ERR_UNSUPPORTED (without touching the device).
 int plan_chain(const mli_gemv_op* in, int count, int sm_count, int smem_per_sm, int smem_optin,
@@ -721,20 +844,23 @@ int plan_chain(const mli_gemv_op* in, int count, int sm_count, int smem_per_sm, 
   p->v = var;
   p->ops.assign(count, Op{});
   p->phases.clear();
+  p->polls.clear();
+  std::vector<char> is_comp(count, 0);  // op i is the up projection of the SwiGLU pair at i - 1
   int max_wait = -1;
   long long units = 0;
-  size_t slot = 0, xbytes = 0;
+  size_t slot = 0, xbytes = 0, mirror = 0;
   int part_stride = 0, epoch = -1;
-  bool companion = false;  // op i is the up projection of the SwiGLU pair started at op i - 1
-  for (int i = 0; i < count; ++i, companion = !companion && in[i - 1].epilogue == kEpiSwiglu) {
+  for (int i = 0; i < count; ++i) {
     const mli_gemv_op& s = in[i];
+    const bool companion = i > 0 && in[i - 1].epilogue == kEpiSwiglu && !is_comp[i - 1];
+    is_comp[i] = companion;
     if (s.form != form) return MLI_ERR_INVALID_ARG;
     if (s.epilogue < kEpiStore || s.epilogue > kEpiSwiglu) return MLI_ERR_INVALID_ARG;
     if (companion) {
-      // same activation, shape and dependencies as its gate; no output of its own
+      // same activation, norm, shape and dependencies as its gate; no output of its own
       const mli_gemv_op& g = in[i - 1];
       if (s.epilogue != kEpiStore || s.n != g.n || s.d != g.d || s.wait != g.wait || s.x != g.x ||
-          s.xq != g.xq || s.xs != g.xs)
+          s.xq != g.xq || s.xs != g.xs || s.norm_w != g.norm_w)
         return MLI_ERR_INVALID_ARG;
     } else if (!s.y) {
       return MLI_ERR_INVALID_ARG;
@@ -744,9 +870,11 @@ int plan_chain(const mli_gemv_op* in, int count, int sm_count, int smem_per_sm, 
     if (f == Form::kW8A8 ? (!s.xq || !s.xs) : !s.x) return MLI_ERR_INVALID_ARG;
     if (s.wait < 0 || s.wait > i) return MLI_ERR_INVALID_ARG;
     if (!companion && f != Form::kW8A8 && overlaps(s.y, 4u * s.d, s.x, 4u * s.n)) return MLI_ERR_INVALID_ARG;
+    if (s.norm_w != nullptr && f == Form::kW8A8) return MLI_ERR_INVALID_ARG;  // int8 input: nothing to norm
     if (s.group_size != kGroup || s.n % 256 != 0) return MLI_ERR_UNSUPPORTED;
     if (!aligned(s.w_q, 16) || !aligned(s.w_s, 16) ||
-        !aligned(f == Form::kW8A8 ? static_cast<const void*>(s.xq) : s.x, 16))
+        !aligned(f == Form::kW8A8 ? static_cast<const void*>(s.xq) : s.x, 16) ||
+        (s.norm_w != nullptr && !aligned(s.norm_w, 16)))
       return MLI_ERR_UNSUPPORTED;
     Op& op = p->ops[i];
     op.y = s.y;
@@ -754,10 +882,14 @@ int plan_chain(const mli_gemv_op* in, int count, int sm_count, int smem_per_sm, 
     op.xs = s.xs;
     op.w = s.w_q;
     op.s = s.w_s;
+    op.norm_w = s.norm_w;
     op.n = s.n;
     op.d = s.d;
     const int S = (s.n + slice_cols(f) - 1) / slice_cols(f);
     if (S > kMaxSlices) return MLI_ERR_UNSUPPORTED;
+    // the whole vector is prepared in shared memory when some warps share a
+    // slice or a norm needs the whole row
+    const bool shared_prep = f == Form::kW8A8Fused || (f == Form::kW8A32 && (S < var.warps || s.norm_w));
     const int R = var.rb * (var.warps / S);
     op.S = static_cast<uint8_t>(S);
     op.R = static_cast<uint16_t>(R);
@@ -774,9 +906,70 @@ int plan_chain(const mli_gemv_op* in, int count, int sm_count, int smem_per_sm, 
     units += n_stages;
     if (units > (1ll << 30)) return MLI_ERR_UNSUPPORTED;
     op.wait = s.wait;
+    // The activation's producer: the latest earlier op writing the buffer this
+    // op reads (fp32 activations only; nothing in a chain writes int8).  It
+    // must lie in the wait prefix, and the reader takes its rows from the
+    // producer's mirror.
+    op.src = -1;
+    if (f != Form::kW8A8) {
+      for (int j = i - 1; j >= 0; --j)
+        if (!is_comp[j] && in[j].y == s.x) {
+          op.src = j;
+          break;
+        }
+      if (op.src >= 0 && (op.src >= s.wait || in[op.src].d != s.n)) return MLI_ERR_INVALID_ARG;
+      if (companion) op.src = p->ops[i - 1].src;
+    }
+    // More columns than the consumers hold: only an input ready at launch,
+    // without a norm, can be read a second time (fused W8A8 quantisation).
+    if (shared_prep && s.n > kMaxHeldCols && !(f == Form::kW8A8Fused && op.src < 0 && s.norm_w == nullptr))
+      return MLI_ERR_UNSUPPORTED;
+    // The ADD epilogue's base: the latest earlier op writing the same y.
+    op.base = -1;
+    if (s.epilogue == kEpiAdd) {
+      for (int j = i - 1; j >= 0; --j)
+        if (!is_comp[j] && in[j].y == s.y) {
+          op.base = j;
+          break;
+        }
+      if (op.base >= 0 && (op.base >= s.wait || in[op.base].d != s.d)) return MLI_ERR_INVALID_ARG;
+    }
+    op.mirror = -1;
+    if (!companion) {
+      op.mirror = static_cast<int>(mirror);
+      mirror += align_up(static_cast<size_t>(s.d), 2);  // 16-byte aligned runs
+      if (mirror > (1u << 30)) return MLI_ERR_UNSUPPORTED;
+    }
+    // Ops of the wait prefix [0, wait) that must be checked by tag: all but
+    // those implied by an op whose rows this op reads anyway (that op was
+    // written only after its own prefix [0, wait_j) had completed).  A
+    // SwiGLU pair completes together.
+    op.poll_first = static_cast<int>(p->polls.size());
+    {
+      int prefix = 0;  // ops [0, prefix) implied
+      std::vector<int> implied;
+      auto imply = [&](int j) {
+        const int g = is_comp[j] ? j - 1 : j;
+        implied.push_back(g);
+        if (!is_comp[g] && in[g].epilogue == kEpiSwiglu) implied.push_back(g + 1);
+        if (in[g].wait > prefix) prefix = in[g].wait;
+      };
+      if (op.src >= 0) imply(op.src);
+      if (op.base >= 0) imply(op.base);
+      for (int j = s.wait - 1; j >= prefix; --j) {
+        bool done = false;
+        for (int k : implied) done |= k == j;
+        if (done) continue;
+        const int g = is_comp[j] ? j - 1 : j;
+        p->polls.push_back(g);
+        imply(g);
+      }
+    }
+    op.poll_count = static_cast<int>(p->polls.size()) - op.poll_first;
     // Same activation as the previous op, with the same prefix to wait for:
     // the CTA keeps its prepared copy.
-    const bool same = i > 0 && s.n == in[i - 1].n && s.wait == in[i - 1].wait &&
+    const bool same = i > 0 && s.n == in[i - 1].n && s.wait == in[i - 1].wait && s.norm_w == in[i - 1].norm_w &&
+                      op.src == p->ops[i - 1].src &&
                       (f == Form::kW8A8 ? (s.xq == in[i - 1].xq && s.xs == in[i - 1].xs)
                                         : s.x == in[i - 1].x);
     if (!same) ++epoch;
@@ -784,33 +977,35 @@ int plan_chain(const mli_gemv_op* in, int count, int sm_count, int smem_per_sm, 
     const size_t stage = static_cast<size_t>(R) * s.n + static_cast<size_t>(R) * op.G() * 4u;
     if (stage > slot) slot = stage;
     // shared activation region: fused W8A8 its int8 copy; W8A32 its digit
-    // planes and group factors, unless every warp owns a slice (prepared in
-    // registers)
+    // planes and group factors when prepared per CTA
     const size_t xb = f == Form::kW8A8Fused ? static_cast<size_t>(s.n)
-                      : (f == Form::kW8A32 && S < var.warps) ? 4u * s.n + op.G() * 4u : 0u;
+                      : (f == Form::kW8A32 && shared_prep) ? 4u * s.n + op.G() * 4u : 0u;
     if (xb > xbytes) xbytes = xb;
     if (R * S > part_stride) part_stride = R * S;
   }
   p->phases.push_back(static_cast<int>(units));
+  p->mirror_words = mirror;
   Args& a = p->args;
   a.count = count;
   a.n_phases = static_cast<int>(p->phases.size()) - 1;
+  a.n_polls = static_cast<int>(p->polls.size());
   a.units = static_cast<int>(units);
   a.slot_bytes = static_cast<uint32_t>(align_up(slot, 128));
   a.part_stride = part_stride;
   const size_t budget = var.per_sm == 1 ? static_cast<size_t>(smem_optin)
                                         : static_cast<size_t>(smem_per_sm) / var.per_sm - 1024;
   const size_t per_slot = a.slot_bytes + static_cast<size_t>(part_stride) * 4u;
-  // Layout: header | op table (when it fits) | activation region | ring | partials.
+  // Layout: header | tables (when they fit) | activation region | ring | partials.
   auto ring_for = [&](size_t table) -> int {
     const size_t ring_off = align_up(kHeader + table + xbytes, 128);
     if (budget <= ring_off) return 0;
     const size_t r = (budget - ring_off) / per_slot;
     return static_cast<int>(r < kMaxRing ? r : kMaxRing);
   };
-  const size_t table = align_up(sizeof(Op) * count + sizeof(int) * p->phases.size(), 128);
+  const size_t table =
+      align_up(sizeof(Op) * count + sizeof(int) * (p->phases.size() + p->polls.size()), 128);
   const int ring_global = ring_for(0), ring_shared = ring_for(table);
-  // Keep the table in shared memory unless that costs a ring slot the chain
+  // Keep the tables in shared memory unless that costs a ring slot the chain
   // needs (three slots keep the stream going across an op switch).
   const bool shared_table = table <= 16384 && ring_shared >= (ring_global < 3 ? ring_global : 3);
   a.table_off = shared_table ? kHeader : 0u;
@@ -860,7 +1055,7 @@ struct mli_chain {
   int threads;
   mli::chain::KernelFn kernel;
   mli::chain::Args args;
-  void* dev_mem;  // op table, then the counters
+  void* dev_mem;  // op table, phases, polls, mirrors, then the launch words
 };
 
 using namespace mli;
@@ -879,25 +1074,34 @@ int mli_chain_create(const mli_gemv_op* ops, int count, mli_chain** chain_out) {
                                    launch_flags(), &p);
   if (rc != MLI_OK) return set_status(rc);
   const chain::KernelFn kfn = chain::kernel_for(ops[0].form, p.v);
-  const int threads = (p.v.warps + 2) * 32;
+  const int threads = p.v.warps * 32;
   err = ensure_dynamic_smem(reinterpret_cast<const void*>(kfn), p.smem);
   if (err != cudaSuccess) return check_cuda(err);
   int per_sm = 0;
   err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, threads, p.smem);
   if (err != cudaSuccess) return check_cuda(err);
   if (per_sm < p.v.per_sm) return set_status(MLI_ERR_UNSUPPORTED);
-  // device block: op table | phases | counters
+  // device block: op table | phases | polls | mirrors | launch sequence, finished count
   const size_t table = chain::align_up(sizeof(chain::Op) * count, 256);
   const size_t phases = chain::align_up(sizeof(int) * p.phases.size(), 256);
-  const size_t counters = sizeof(unsigned) * (static_cast<size_t>(count) + 1);
+  const size_t polls = chain::align_up(sizeof(int) * (p.polls.size() + 1), 256);
+  const size_t mirror = chain::align_up(sizeof(uint64_t) * p.mirror_words, 256);
+  const size_t words = 256;
   void* mem = nullptr;
-  err = cudaMalloc(&mem, table + phases + counters);
+  err = cudaMalloc(&mem, table + phases + polls + mirror + words);
   if (err != cudaSuccess) return set_status(MLI_ERR_CUDA, err);
   char* base = static_cast<char*>(mem);
   err = cudaMemcpy(base, p.ops.data(), sizeof(chain::Op) * count, cudaMemcpyHostToDevice);
   if (err == cudaSuccess)
     err = cudaMemcpy(base + table, p.phases.data(), sizeof(int) * p.phases.size(), cudaMemcpyHostToDevice);
-  if (err == cudaSuccess) err = cudaMemset(base + table + phases, 0, counters);
+  if (err == cudaSuccess && !p.polls.empty())
+    err = cudaMemcpy(base + table + phases, p.polls.data(), sizeof(int) * p.polls.size(),
+                     cudaMemcpyHostToDevice);
+  // zeroed mirrors carry tag 0, which no launch uses; the sequence starts at 1
+  if (err == cudaSuccess) err = cudaMemset(base + table + phases + polls, 0, mirror + words);
+  const unsigned first_seq = 1;
+  if (err == cudaSuccess)
+    err = cudaMemcpy(base + table + phases + polls + mirror, &first_seq, sizeof(first_seq), cudaMemcpyHostToDevice);
   if (err != cudaSuccess) {
     cudaFree(mem);
     return set_status(MLI_ERR_CUDA, err);
@@ -912,8 +1116,10 @@ int mli_chain_create(const mli_gemv_op* ops, int count, mli_chain** chain_out) {
   c->args = p.args;
   c->args.ops = reinterpret_cast<const chain::Op*>(base);
   c->args.phases = reinterpret_cast<const int*>(base + table);
-  c->args.done = reinterpret_cast<unsigned*>(base + table + phases);
-  c->args.finished = c->args.done + count;
+  c->args.polls = reinterpret_cast<const int*>(base + table + phases);
+  c->args.mirror = reinterpret_cast<uint64_t*>(base + table + phases + polls);
+  c->args.seq = reinterpret_cast<unsigned*>(base + table + phases + polls + mirror);
+  c->args.finished = c->args.seq + 1;
   c->dev_mem = mem;
   *chain_out = c;
   return set_status(MLI_OK);

@@ -118,6 +118,13 @@ __device__ __forceinline__ void bulk_copy_g2s(void* dst_smem, const void* src,
       : "memory");
 }
 
+// Asks the TMA engine to bring `bytes` (multiple of 16; 16-byte aligned
+// source) into L2 without a destination or completion: a later bulk copy of
+// the same bytes then reads L2 instead of HBM.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(

@@ -179,9 +179,12 @@ class GemvChain:
     (matmul_int8 / matmul_dp4a / matmul_dp4a_fused).  Optional "epilogue":
     "store" (default), "add" (y += the op's rows: the residual add), or
     "swiglu" (this op is the gate and the NEXT op the up projection, same n, d,
-    x and wait; y = silu(gate) * up; the next op's y may be None).  The
-    buffers must outlive the chain; the chain keeps references to the tensors
-    given.
+    x and wait; y = silu(gate) * up; the next op's y may be None).  Optional
+    "norm_w": the activation is RMSNorm(x) * norm_w (the reference's
+    rmsnorm_cuda), computed in the op's prologue.  An op reading the y of an
+    earlier op takes that op's rows of the same launch; an "add" op adds into
+    the latest earlier op's output of the same y.  The buffers must outlive
+    the chain; the chain keeps references to the tensors given.
     """
 
     def __init__(self, ops, group_size: int = 64):
@@ -192,7 +195,7 @@ class GemvChain:
             e.form = _FORMS[o["form"]]
             e.n, e.d, e.group_size, e.wait = o["n"], o["d"], group_size, o.get("wait", 0)
             e.epilogue = _EPILOGUES[o.get("epilogue", "store")]
-            for key in ("y", "x", "xq", "xs", "w_q", "w_s"):
+            for key in ("y", "x", "xq", "xs", "w_q", "w_s", "norm_w"):
                 t = o.get(key)
                 setattr(e, key, _ptr(t))
                 if t is not None and not isinstance(t, int):

@@ -13,6 +13,7 @@
  *   oracle_gemv_w8a32         src/model_cuda_v2_shared.cu:36-62 (+ warpReduceSum :30-34)
  *   oracle_gemv_w8a8          src/model_cuda_v2_shared.cu:465-501
  *   oracle_matmul_f32         src/model_cuda_v2_shared.cu:10-19 (fp32 classifier)
+ *   oracle_rmsnorm_chain      src/model_cuda_v2_shared.cu:74-89 in the chained prologue's order
  *   oracle_group_dots         the exact int32 group partials of :483-494
  *   oracle_dequant_matvec     float32 dequant-then-matvec (CPU baseline, OpenMP)
  *   oracle_gemv_*_f64         fp64 recomputes used as tolerance anchors
@@ -191,6 +192,40 @@ void oracle_gemv_w8a8_f64(double* y, const int8_t* xq, const float* xs,
              (double)s[r * ng + g];
     y[r] = acc * (double)*xs;
   }
+}
+
+/* RMSNorm as the chained GEMV's prologue computes it (the reference's
+ * rmsnorm_kernel, src/model_cuda_v2_shared.cu:74-89, whose own sum order is an
+ * atomicAdd race): 256 threads, thread t holding columns 1024 j + 4 t .. + 3
+ * (j < 8), each summing its squares with fmaf in that order; a warp
+ * butterfly over lane offsets 16, 8, 4, 2, 1; the 8 warp sums added in warp
+ * order; ss = 1 / sqrtf(sum / n + 1e-5); out = w * (ss * x).  n <= 8192. */
+void oracle_rmsnorm_chain(float* out, const float* x, const float* w, long n) {
+  float warp_tot[8];
+  for (int wp = 0; wp < 8; ++wp) {
+    float lane[32];
+    for (int l = 0; l < 32; ++l) {
+      const long t = wp * 32 + l;
+      float ssq = 0.0f;
+      for (long j = 0; j < 8; ++j)
+        for (long e = 0; e < 4; ++e) {
+          const long c = 1024 * j + 4 * t + e;
+          const float v = c < n ? x[c] : 0.0f;
+          ssq = fmaf(v, v, ssq);
+        }
+      lane[l] = ssq;
+    }
+    for (int off = 16; off > 0; off >>= 1) {
+      float nxt[32];
+      for (int l = 0; l < 32; ++l) nxt[l] = lane[l] + lane[l ^ off];
+      memcpy(lane, nxt, sizeof(lane));
+    }
+    warp_tot[wp] = lane[0];
+  }
+  float sum = warp_tot[0];
+  for (int wp = 1; wp < 8; ++wp) sum += warp_tot[wp];
+  const float ss = 1.0f / sqrtf(sum / (float)n + 1e-5f);
+  for (long c = 0; c < n; ++c) out[c] = w[c] * (ss * x[c]);
 }
 
 /* src/model_cuda_v2_shared.cu:10-19: one thread per row, sequentially over

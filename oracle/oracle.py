@@ -10,6 +10,7 @@ import it.  It wraps ``liboracle.so`` (built from ``mli_oracle.c`` by
     gemv_w8a32              src/model_cuda_v2_shared.cu:36-62
     gemv_w8a8               src/model_cuda_v2_shared.cu:465-501
     matmul_f32              src/model_cuda_v2_shared.cu:10-19 (fp32 classifier)
+    rmsnorm_chain           src/model_cuda_v2_shared.cu:74-89, in the chained prologue's order
     group_dots              the int32 group partials of :483-494
 
 Parity pins: ``tests/golden/`` holds the reference quantiser script's own
@@ -66,6 +67,7 @@ def lib():
             "oracle_gemv_w8a32_f64": (None, [_f64p, _f32p, _i8p, _f32p, _L, _L, _I]),
             "oracle_gemv_w8a8_f64": (None, [_f64p, _i8p, _f32p, _i8p, _f32p, _L, _L, _I]),
             "oracle_matmul_f32": (None, [_f32p, _f32p, _f32p, _L, _L]),
+            "oracle_rmsnorm_chain": (None, [_f32p, _f32p, _f32p, _L]),
             "oracle_matmul_f64": (None, [_f64p, _f32p, _f32p, _L, _L]),
             "oracle_gemm_w8a8_f64": (None, [_f64p, _i8p, _f32p, _i8p, _f32p, _L, _L, _L, _I]),
             "oracle_group_dot_sums": (None, [_i64p, _i8p, _i8p, _i32p, _L, _L, _L, _I]),
@@ -156,6 +158,15 @@ def gemv_w8a8_f64(xq, xs, w_q, w_s, group_size: int = 64):
     lib().oracle_gemv_w8a8_f64(y, _c(xq, np.int8), _c(xs, np.float32).reshape(-1), _c(w_q, np.int8),
                                _c(w_s, np.float32), n, d, group_size)
     return y
+
+
+def rmsnorm_chain(x, w):
+    """RMSNorm (src/model_cuda_v2_shared.cu:74-89) summed in the chained GEMV
+    prologue's fixed order: bit-identical to what the chain computes."""
+    x = _c(x, np.float32)
+    out = np.empty_like(x)
+    lib().oracle_rmsnorm_chain(out, x, _c(w, np.float32), x.shape[0])
+    return out
 
 
 def matmul_f32(x, w):

@@ -231,3 +231,93 @@ def test_chain_swiglu_and_residual_epilogues(form):
         assert orc.max_abs_rel(res.cpu().numpy(), res_ref.cpu().numpy()) <= 1e-5, rep
     c.close()
     assert ops.device_error() == 0
+
+
+def _norm_weights(n, seed):
+    rng = np.random.default_rng(seed)
+    return (1.0 + 0.1 * rng.standard_normal(n)).astype(np.float32)
+
+
+@pytest.mark.parametrize("form", ["w8a32", "w8a8_fused"])
+def test_chain_decode_layers_with_norm_prologue(form):
+    """Two Llama-3.2-1B decode layers as one chain, with everything of the
+    layer but attention: q/k/v read RMSNorm(resid) (the norm in the op's
+    prologue, src/model_cuda_v2_shared.cu:381), o reads q's output (standing
+    in for attention) and adds into resid (:402-405), gate/up read
+    RMSNorm(resid) as one SwiGLU pair (:405-410), down adds into resid
+    (:412-414).  Every activation is another op's output of the same launch,
+    handed over through the tagged mirrors.  Checked step by step against
+    single calls on the oracle's RMSNorm (restated in the prologue's sum
+    order): q/k/v, o, down and the final residual bit for bit, the SwiGLU
+    product within 1e-6 (expf)."""
+    layers, dim, hidden = 2, 2048, 8192
+    resid0 = synth.activation_np(dim, 500)
+    resid = torch.from_numpy(resid0.copy()).to(dev())
+    att_w = [_norm_weights(dim, 600 + l) for l in range(layers)]
+    ffn_w = [_norm_weights(dim, 700 + l) for l in range(layers)]
+    t_att = [torch.from_numpy(a).to(dev()) for a in att_w]
+    t_ffn = [torch.from_numpy(a).to(dev()) for a in ffn_w]
+    w = [[weights(d, n, 2000 * l + i) for i, (_, d, n) in enumerate(synth.LLAMA_1B)] for l in range(layers)]
+    bufs = [{nm: torch.full((d,), float("nan"), device=dev()) for nm, d in
+             (("q", dim), ("k", 512), ("v", 512), ("h", hidden))} for _ in range(layers)]
+    chain = []
+    for l in range(layers):
+        b, W, B = 7 * l, w[l], bufs[l]
+        chain += [
+            dict(form=form, n=dim, d=dim, wait=b, x=resid, norm_w=t_att[l], y=B["q"], w_q=W[0][0], w_s=W[0][1]),
+            dict(form=form, n=dim, d=512, wait=b, x=resid, norm_w=t_att[l], y=B["k"], w_q=W[1][0], w_s=W[1][1]),
+            dict(form=form, n=dim, d=512, wait=b, x=resid, norm_w=t_att[l], y=B["v"], w_q=W[2][0], w_s=W[2][1]),
+            dict(form=form, n=dim, d=dim, wait=b + 3, x=B["q"], y=resid, epilogue="add", w_q=W[3][0],
+                 w_s=W[3][1]),
+            dict(form=form, n=dim, d=hidden, wait=b + 4, x=resid, norm_w=t_ffn[l], y=B["h"], epilogue="swiglu",
+                 w_q=W[4][0], w_s=W[4][1]),
+            dict(form=form, n=dim, d=hidden, wait=b + 4, x=resid, norm_w=t_ffn[l], y=None, w_q=W[5][0],
+                 w_s=W[5][1]),
+            dict(form=form, n=hidden, d=dim, wait=b + 6, x=B["h"], y=resid, epilogue="add", w_q=W[6][0],
+                 w_s=W[6][1]),
+        ]
+    c = ops.GemvChain(chain)
+    for rep in range(3):  # the launch sequence advances: later runs must not take old rows
+        resid.copy_(torch.from_numpy(resid0))
+        for B in bufs:
+            for t in B.values():
+                t.fill_(float("nan"))
+        c.run()
+        torch.cuda.synchronize()
+        exp = resid0.copy()
+        for l in range(layers):
+            W, B = w[l], bufs[l]
+
+            def one(x_np, i, d, n):
+                y = torch.empty(d, device=dev())
+                single(form, y, torch.from_numpy(np.ascontiguousarray(x_np, np.float32)).to(dev()),
+                       W[i][0], W[i][1], n, d)
+                return y.cpu().numpy()
+
+            xa = orc.rmsnorm_chain(exp, att_w[l])
+            for i, nm in ((0, "q"), (1, "k"), (2, "v")):
+                got = B[nm].cpu().numpy()
+                assert np.array_equal(got.view(np.uint32), one(xa, i, got.size, dim).view(np.uint32)), (rep, l, nm)
+            exp = (exp + one(B["q"].cpu().numpy(), 3, dim, dim)).astype(np.float32)
+            xf = orc.rmsnorm_chain(exp, ffn_w[l])
+            g = torch.from_numpy(one(xf, 4, hidden, dim))
+            u = torch.from_numpy(one(xf, 5, hidden, dim))
+            h_ref = ((g * (1.0 / (1.0 + torch.exp(-g)))) * u).numpy()
+            h = B["h"].cpu().numpy()
+            assert not np.isnan(h).any()
+            assert orc.max_abs_rel(h, h_ref) <= 1e-6, (rep, l)
+            exp = (exp + one(h, 6, dim, hidden)).astype(np.float32)
+        assert np.array_equal(resid.cpu().numpy().view(np.uint32), exp.view(np.uint32)), rep
+    c.close()
+    assert ops.device_error() == 0
+
+
+def test_chain_rejects_reading_an_unawaited_producer():
+    """An op reading an earlier op's output must wait for it."""
+    q, s = weights(256, 256, 1)
+    x = torch.zeros(256, device=dev())
+    y = torch.zeros(256, device=dev())
+    z = torch.zeros(256, device=dev())
+    with pytest.raises(MliError):
+        ops.GemvChain([dict(form="w8a32", n=256, d=256, wait=0, x=x, y=y, w_q=q, w_s=s),
+                       dict(form="w8a32", n=256, d=256, wait=0, x=y, y=z, w_q=q, w_s=s)])
