@@ -40,9 +40,10 @@
 //    (quant_quad) -- once per CTA into shared memory, or, when every warp owns
 //    its own slice of the row (W8A32 with n = 8192, no norm), by each warp in
 //    registers without a barrier.
-//  * Every warp computes rows from the ring; the last one to finish with a
-//    slot stores its rows and refills the slot with the CTA's unit `ring`
-//    places ahead (eight warps of up to 255 registers, no producer warp).
+//  * Warp roles: consumer warps compute rows from the ring, and the last one
+//    to finish with a slot stores its rows and frees the slot; one producer
+//    warp refills freed slots (issuing a bulk copy takes long enough that it
+//    is kept off the consumers).
 //  * Rows are computed exactly as in gemv_stream_kernel (same row kernels,
 //    same slice order), so an op without a norm prologue gives bit-identical
 //    output to the corresponding mli_gemv_* call.
@@ -56,6 +57,10 @@
 #include <cstring>
 #include <vector>
 
+// Built as a device module of its own (no -rdc): ptxas then sizes the
+// out-of-line prologues within the kernel's register budget.  The library's
+// device error word is reached through a pointer (Args::err).
+#define MLI_SEPARATE_DEVICE_MODULE
 #include "gemv_rows.cuh"
 #include "mli_common.cuh"
 #include "mli_internal.h"
@@ -123,14 +128,19 @@ struct Args {
   uint32_t slot_bytes;  // ring slot: the largest stage of the chain
   uint32_t x_off, ring_off, part_off;
   int part_stride;      // floats of split-K partials per slot
+  unsigned* err;        // the library's device error word (first code wins)
 };
+
+__device__ __forceinline__ void record_error(const Args& a, unsigned code) {
+  if (a.err) atomicCAS(a.err, 0u, code);
+}
 
 // Shared-memory header: full[6] @0, free[6] @48, per-slot warp counters @96,
 // flags @128..140, the launch sequence @140, two reduction arrays of one
 // float per consumer warp @160 (quantiser) and @208 (RMSNorm).
 struct Smem {
   uint64_t* full;   // weights of the slot's unit landed (bulk copy)
-  uint64_t* free;   // (unused: the last warp of a slot refills it)
+  uint64_t* free;   // the consumers are done with the slot: it may be refilled
   int* counters;
   volatile int* broken;
   int* issued;
@@ -182,25 +192,13 @@ __device__ __forceinline__ float word_value(uint64_t w) {
 __device__ __forceinline__ bool all_tagged4(uint64_t w0, uint64_t w1, uint64_t w2, uint64_t w3, uint32_t tag) {
   return has_tag(w0, tag) && has_tag(w1, tag) && has_tag(w2, tag) && has_tag(w3, tag);
 }
-__device__ __noinline__ bool reload_tagged4(const uint64_t* p, uint32_t tag, float4* v, uint64_t t0) {
-  uint64_t w0, w1, w2, w3;
-  do {
-    if (global_timer_ns() - t0 > kWaitLimitNs) return false;
-    ld_relaxed_v2(p, w0, w1);
-    ld_relaxed_v2(p + 2, w2, w3);
-  } while (!all_tagged4(w0, w1, w2, w3, tag));
-  *v = make_float4(word_value(w0), word_value(w1), word_value(w2), word_value(w3));
-  return true;
+// Spinning readers back off between polls, so that thousands of threads
+// waiting for the same few kilobytes do not crowd the L2 slices their
+// producers are writing to.
+__device__ __forceinline__ void poll_backoff(unsigned& ns) {
+  __nanosleep(ns);
+  ns = ns < 256 ? 2 * ns : 256;
 }
-__device__ __forceinline__ bool finish_tagged4(const uint64_t* p, uint64_t w0, uint64_t w1, uint64_t w2,
-                                               uint64_t w3, uint32_t tag, float4& v, uint64_t t0) {
-  if (all_tagged4(w0, w1, w2, w3, tag)) {
-    v = make_float4(word_value(w0), word_value(w1), word_value(w2), word_value(w3));
-    return true;
-  }
-  return reload_tagged4(p, tag, &v, t0);
-}
-
 // Op holding global unit u, searching forward from op `o` (units grow).
 __device__ __forceinline__ int find_op(const Op* ops, int count, int u, int o) {
   while (o + 1 < count && ops[o + 1].unit_base <= u) ++o;
@@ -284,9 +282,25 @@ __device__ __forceinline__ bool poll_ops(const Args& a, const Op* ops, const int
     const Op& q = ops[j];
     const uint32_t tag = row_tag(seq, j);
     const uint64_t* m = a.mirror + q.mirror;
-    for (int r = threadIdx.x; r < q.d; r += kT)
-      while (!has_tag(ld_relaxed_b64(m + r), tag))
+    for (int r0 = threadIdx.x; r0 < q.d; r0 += 8 * kT) {
+      unsigned pending = 0;
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (r0 + k * kT < q.d) pending |= 1u << k;
+      unsigned ns = 32;
+      while (true) {
+        uint64_t w[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if ((pending >> k) & 1u) w[k] = ld_relaxed_b64(m + r0 + k * kT);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if (((pending >> k) & 1u) && has_tag(w[k], tag)) pending &= ~(1u << k);
+        if (pending == 0) break;
         if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+        poll_backoff(ns);
+      }
+    }
   }
   return true;
 }
@@ -312,24 +326,34 @@ __device__ __forceinline__ bool cta_x_load(const Op& op, const uint64_t* m, uint
     }
     return true;
   }
-  uint64_t w[kPre][4];
+  // two groups (float4) at a time, both reloaded every round until tagged:
+  // few registers in flight, so the row loop around it keeps its own
+  const uint64_t t0 = global_timer_ns();
 #pragma unroll
-  for (int j = 0; j < kPre; ++j) {
-    const int c = 4 * kT * j + 4 * t;
-    if (c < n) {
-      ld_relaxed_v2(m + c, w[j][0], w[j][1]);
-      ld_relaxed_v2(m + c + 2, w[j][2], w[j][3]);
+  for (int j = 0; j < kPre; j += 2) {
+    v[j] = v[j + 1] = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int c0 = 4 * kT * j + 4 * t, c1 = c0 + 4 * kT;
+    if (c0 >= n) continue;
+    const bool two = c1 < n;
+    unsigned ns = 32;
+    while (true) {
+      uint64_t a0, a1, a2, a3, b0 = 0, b1 = 0, b2 = 0, b3 = 0;
+      ld_relaxed_v2(m + c0, a0, a1);
+      ld_relaxed_v2(m + c0 + 2, a2, a3);
+      if (two) {
+        ld_relaxed_v2(m + c1, b0, b1);
+        ld_relaxed_v2(m + c1 + 2, b2, b3);
+      }
+      if (all_tagged4(a0, a1, a2, a3, tag) && (!two || all_tagged4(b0, b1, b2, b3, tag))) {
+        v[j] = make_float4(word_value(a0), word_value(a1), word_value(a2), word_value(a3));
+        if (two) v[j + 1] = make_float4(word_value(b0), word_value(b1), word_value(b2), word_value(b3));
+        break;
+      }
+      if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+      poll_backoff(ns);
     }
   }
-  const uint64_t t0 = global_timer_ns();
-  bool ok = true;
-#pragma unroll
-  for (int j = 0; j < kPre; ++j) {
-    const int c = 4 * kT * j + 4 * t;
-    v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (c < n && !finish_tagged4(m + c, w[j][0], w[j][1], w[j][2], w[j][3], tag, v[j], t0)) ok = false;
-  }
-  return ok;
+  return true;
 }
 
 // RMSNorm of the held activation (the reference's rmsnorm_kernel,
@@ -370,7 +394,7 @@ __device__ __forceinline__ void cta_rmsnorm(float4 (&v)[kPre], int n, const floa
 template <int kT>
 __device__ __forceinline__ void cta_digits(const float4 (&v)[kPre], int n, int8_t* planes, float* fac) {
   const int lane = threadIdx.x & 31;
-#pragma unroll
+#pragma unroll 1  // rolled: keeps the prologue's registers below the row loop's
   for (int j = 0; j < kPre; ++j) {
     const int c = 4 * kT * j + 4 * static_cast<int>(threadIdx.x);
     if (4 * kT * j < n) digit_quad(v[j], c < n, c, n, planes, fac, lane);  // CTA-uniform
@@ -433,29 +457,32 @@ __device__ __forceinline__ bool warp_x_load(const Op& op, const uint64_t* m, uin
                            : make_float4(0.f, 0.f, 0.f, 0.f);
     return true;
   }
-  uint64_t w[kPre][4];
-#pragma unroll
-  for (int k = 0; k < 2; ++k)
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-      if ((vmask >> k) & 1u) {
-        const uint64_t* p = m + col0 + 512 * k + 4 * j;
-        ld_relaxed_v2(p, w[4 * k + j][0], w[4 * k + j][1]);
-        ld_relaxed_v2(p + 2, w[4 * k + j][2], w[4 * k + j][3]);
-      }
+  // two groups (float4) at a time, both reloaded every round until tagged:
+  // few registers in flight, so the row loop around it keeps its own
   const uint64_t t0 = global_timer_ns();
-  bool ok = true;
 #pragma unroll
-  for (int k = 0; k < 2; ++k)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      v[4 * k + j] = make_float4(0.f, 0.f, 0.f, 0.f);
-      const uint64_t(&q)[4] = w[4 * k + j];
-      if (((vmask >> k) & 1u) &&
-          !finish_tagged4(m + col0 + 512 * k + 4 * j, q[0], q[1], q[2], q[3], tag, v[4 * k + j], t0))
-        ok = false;
+  for (int q = 0; q < kPre; q += 2) {
+    v[q] = v[q + 1] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (!((vmask >> (q >> 2)) & 1u)) continue;
+    const uint64_t* p0 = m + col0 + 512 * (q >> 2) + 4 * (q & 3);
+    const uint64_t* p1 = p0 + 4;
+    unsigned ns = 32;
+    while (true) {
+      uint64_t a0, a1, a2, a3, b0, b1, b2, b3;
+      ld_relaxed_v2(p0, a0, a1);
+      ld_relaxed_v2(p0 + 2, a2, a3);
+      ld_relaxed_v2(p1, b0, b1);
+      ld_relaxed_v2(p1 + 2, b2, b3);
+      if (all_tagged4(a0, a1, a2, a3, tag) && all_tagged4(b0, b1, b2, b3, tag)) {
+        v[q] = make_float4(word_value(a0), word_value(a1), word_value(a2), word_value(a3));
+        v[q + 1] = make_float4(word_value(b0), word_value(b1), word_value(b2), word_value(b3));
+        break;
+      }
+      if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+      poll_backoff(ns);
     }
-  return ok;
+  }
+  return true;
 }
 
 // The lane's digit planes of chunks 0, 1 in registers.  The quad of lanes
@@ -509,6 +536,30 @@ __device__ __forceinline__ void warp_digits(const float4 (&v)[kPre], unsigned vm
   }
 }
 
+// The activation prologue runs once per activation change.
+
+// Shared preparation into shared memory: W8A32 digit planes + group factors,
+// or the fused W8A8 int8 copy (its scale into *xscale).  All consumer threads
+// call it.  False (on every thread) when an input row did not arrive in time.
+template <Form F, int kT>
+__device__ __forceinline__ bool prep_cta(const Op& op, const uint64_t* m, uint32_t tag, unsigned char* xregion,
+                                      float* red, float* red2, float* xscale) {
+  float4 pre[kPre];
+  bool fail = !cta_x_load<kT>(op, m, tag, pre);
+  fail = named_sync_or<kT>(fail);  // also: every consumer is done reading the shared region
+  if (fail) return false;
+  const int n = op.n;
+  if (op.norm_w != nullptr) cta_rmsnorm<kT>(pre, n, op.norm_w, red2);
+  if constexpr (F == Form::kW8A32) {
+    int8_t* planes = reinterpret_cast<int8_t*>(xregion);
+    cta_digits<kT>(pre, n, planes, reinterpret_cast<float*>(planes + 4 * n));
+  } else {
+    *xscale = cta_quant<kT>(pre, op.x(), n, reinterpret_cast<int8_t*>(xregion), red);
+  }
+  named_sync<kT>();
+  return true;
+}
+
 // A consumer warp's role in an op: its slice, its rows of a stage, and the
 // chunks of its lanes that fall inside the row.
 template <Form F, int kW>
@@ -531,10 +582,10 @@ struct Role {
   }
 };
 
-// kW warps, kRB rows per warp per stage; the last warp to finish with a slot
-// refills it.
+// Warps 0 .. kW-1 consume (kRB rows per warp per stage), warp kW is the
+// producer (bulk copies).
 template <Form F, int kW, int kRB, bool kEpi>
-__global__ void __launch_bounds__(kW * 32, 1) gemv_chain_kernel(const Args a) {
+__global__ void __launch_bounds__((kW + 1) * 32, 1) gemv_chain_kernel(const Args a) {
   constexpr int kT = kW * 32;  // consumer threads
   extern __shared__ __align__(1024) unsigned char smem[];
   Smem sm(smem);
@@ -546,6 +597,7 @@ __global__ void __launch_bounds__(kW * 32, 1) gemv_chain_kernel(const Args a) {
   if (threadIdx.x == 0) {
     for (int i = 0; i < a.ring; ++i) {
       mbar_init(&sm.full[i], 1);
+      mbar_init(&sm.free[i], 1);
       sm.counters[i] = 0;
     }
     *sm.broken = 0;
@@ -570,26 +622,31 @@ __global__ void __launch_bounds__(kW * 32, 1) gemv_chain_kernel(const Args a) {
   const int cnt = cta_units(phases, a.n_phases, cta, grid);
   const unsigned seq = *sm.seq;
 
-  if (threadIdx.x == 0) {
-    // the first `ring` units; every later one is issued by the warp that frees its slot
-    int o = 0;
-    Cursor cur(phases, a.n_phases, cta, grid);
-    for (int i = 0; i < cnt && i < a.ring; ++i, cur.next()) {
-      o = find_op(ops, a.count, cur.u, o);
-      issue_unit<kEpi>(a, ops, ring, sm.full, o, cur.u, i);
-      *sm.issued = i + 1;
+  if (warp == kW) {
+    // ---- producer: unit i into slot i % ring once the consumers freed it
+    if (lane == 0) {
+      int o = 0;
+      Cursor cur(phases, a.n_phases, cta, grid);
+      for (int i = 0; i < cnt; ++i, cur.next()) {
+        const int slot = i % a.ring;
+        if (i >= a.ring && !mbar_wait_bounded(&sm.free[slot], ((i / a.ring) - 1) & 1, kWaitLimitNs)) {
+          record_error(a, kDevStageTimeout);
+          *sm.broken = 1;
+        }
+        if (*sm.broken) break;
+        o = find_op(ops, a.count, cur.u, o);
+        fence_proxy_async_smem();  // consumers' reads of the slot precede the copy's writes
+        issue_unit<kEpi>(a, ops, ring, sm.full, o, cur.u, slot);
+        *sm.issued = i + 1;
+      }
     }
-  }
-  {
+  } else {
     constexpr int K = chunks_per_lane(F);
     constexpr int kSlice = slice_cols(F);
     constexpr int kLanesPerRow = 32 / kRB;
     int o = 0, cur = -1, known = 0, epoch = -1;
     int n = 0, d = 0, Gr = 0, S = 1, R = 0, Ru = 0, epi = kEpiStore, base = 0;
     float* y = nullptr;
-    uint64_t* my_mirror = nullptr;
-    const uint64_t* base_mirror = nullptr;
-    uint32_t my_tag = 0, base_tag = 0;
     int sl = 0, wj = 0;
     bool warp_on = false;
     unsigned vmask = 0;
@@ -597,29 +654,24 @@ __global__ void __launch_bounds__(kW * 32, 1) gemv_chain_kernel(const Args a) {
     uint4 xd[2][4];  // W8A32 digit planes of chunks 0, 1
     float fac[2];
     uint4 xv[4];     // W8A8 int8 chunks 0..3
-    float4 pre[kPre];  // the activation's loads while it is prepared
 
     Cursor it(phases, a.n_phases, cta, grid);
-    Cursor ahead(phases, a.n_phases, cta, grid);  // unit i + ring, the slot's next
-    for (int i = 0; i < a.ring; ++i) ahead.next();
-    int o_ahead = 0;
-    for (int i = 0; i < cnt; ++i, it.next(), ahead.next()) {
+    for (int i = 0; i < cnt; ++i, it.next()) {
       const int u = it.u;
       o = find_op(ops, a.count, u, o);
       if (o != cur) {
         const Op& op = ops[o];
         const int wait = op.wait, ep = op.epoch;
         bool fail = false;
-        if (wait > known && op.poll_count > 0) {
+        // once a wait has expired in this CTA, later ops wait for nothing
+        // (their rows are not produced): the launch ends in bounded time
+        const bool broken = *sm.broken != 0;
+        if (wait > known && op.poll_count > 0 && !broken) {
           // ops of the wait prefix that the activation's producer does not imply
           fail = !poll_ops<kT>(a, ops, polls, op.poll_first, op.poll_count, seq);
           fail = named_sync_or<kT>(fail);
         }
         n = op.n; d = op.d; Gr = op.G(); R = op.R; base = op.unit_base; y = op.y;
-        my_mirror = op.mirror >= 0 ? a.mirror + op.mirror : nullptr;
-        my_tag = row_tag(seq, o);
-        base_mirror = op.base >= 0 ? a.mirror + ops[op.base].mirror : nullptr;
-        base_tag = row_tag(seq, op.base);
         if constexpr (kEpi) {
           Ru = op.Ru();
           epi = op.epi;
@@ -631,7 +683,8 @@ __global__ void __launch_bounds__(kW * 32, 1) gemv_chain_kernel(const Args a) {
           const Role<F, kW> role(op, warp, lane);
           S = op.S; sl = role.sl; wj = role.wj; warp_on = role.on; vmask = role.vmask;
           const int col0 = role.col0;
-          const uint64_t* src_m = op.src >= 0 ? a.mirror + ops[op.src].mirror : nullptr;
+          // (a broken CTA reads the activation as it stands, without waiting)
+          const uint64_t* src_m = op.src >= 0 && !broken ? a.mirror + ops[op.src].mirror : nullptr;
           const uint32_t src_tag = row_tag(seq, op.src);
           if constexpr (F == Form::kW8A8) {
             xscale = __ldcg(op.xs);
@@ -642,17 +695,16 @@ __global__ void __launch_bounds__(kW * 32, 1) gemv_chain_kernel(const Args a) {
                           : make_uint4(0, 0, 0, 0);
           } else if (F == Form::kW8A32 && op.S == kW && op.norm_w == nullptr) {
             // every warp owns its slice: prepare it in registers, no barrier
+            float4 pre[kPre];
             if (!warp_x_load(op, src_m, src_tag, col0, vmask, pre)) fail = true;
             if constexpr (F == Form::kW8A32) warp_digits(pre, vmask, xd, fac);
           } else {
-            if (!cta_x_load<kT>(op, src_m, src_tag, pre)) fail = true;
-            fail = named_sync_or<kT>(fail);  // also: every consumer is done reading the shared region
-            if (op.norm_w != nullptr) cta_rmsnorm<kT>(pre, n, op.norm_w, sm.red2);
+            float t_scale = 0.f;
+            if (!prep_cta<F, kT>(op, src_m, src_tag, smem + a.x_off, sm.red, sm.red2, &t_scale)) fail = true;
+            xscale = t_scale;
             if constexpr (F == Form::kW8A32) {
-              int8_t* planes = reinterpret_cast<int8_t*>(smem + a.x_off);
-              float* facs = reinterpret_cast<float*>(planes + 4 * n);
-              cta_digits<kT>(pre, n, planes, facs);
-              named_sync<kT>();
+              const int8_t* planes = reinterpret_cast<const int8_t*>(smem + a.x_off);
+              const float* facs = reinterpret_cast<const float*>(planes + 4 * n);
 #pragma unroll
               for (int k = 0; k < 2; ++k) {
                 const bool v = (vmask >> k) & 1u;
@@ -663,9 +715,7 @@ __global__ void __launch_bounds__(kW * 32, 1) gemv_chain_kernel(const Args a) {
                 fac[k] = v ? facs[(col0 + 512 * k) >> 6] : 0.f;
               }
             } else {
-              int8_t* q8 = reinterpret_cast<int8_t*>(smem + a.x_off);
-              xscale = cta_quant<kT>(pre, op.x(), n, q8, sm.red);
-              named_sync<kT>();
+              const int8_t* q8 = reinterpret_cast<const int8_t*>(smem + a.x_off);
 #pragma unroll
               for (int k = 0; k < 4; ++k)
                 xv[k] = ((vmask >> k) & 1u) ? *reinterpret_cast<const uint4*>(q8 + col0 + 512 * k)
@@ -674,7 +724,7 @@ __global__ void __launch_bounds__(kW * 32, 1) gemv_chain_kernel(const Args a) {
           }
         }
         if (fail) {
-          record_device_error(kDevChainTimeout);
+          record_error(a, kDevChainTimeout);
           *sm.broken = 1;
         }
         if (wait > known) known = wait;
@@ -685,7 +735,7 @@ __global__ void __launch_bounds__(kW * 32, 1) gemv_chain_kernel(const Args a) {
       const int rows = min(Ru, d - row0);
       bool ok = !*sm.broken;
       if (ok && !mbar_wait_bounded(&sm.full[slot], (i / a.ring) & 1, kWaitLimitNs)) {
-        record_device_error(kDevStageTimeout);
+        record_error(a, kDevStageTimeout);
         *sm.broken = 1;
         ok = false;
       }
@@ -723,6 +773,13 @@ __global__ void __launch_bounds__(kW * 32, 1) gemv_chain_kernel(const Args a) {
       }
       if (__shfl_sync(0xffffffffu, last, 0)) {
         if (!*sm.broken) {
+          // the op's mirror and the ADD base, from the table (kept out of the
+          // registers of the row loop)
+          const Op& op = ops[o];
+          uint64_t* my_mirror = op.mirror >= 0 ? a.mirror + op.mirror : nullptr;
+          const uint32_t my_tag = row_tag(seq, o);
+          const uint64_t* base_mirror = op.base >= 0 ? a.mirror + ops[op.base].mirror : nullptr;
+          const uint32_t base_tag = row_tag(seq, op.base);
           bool late = false;
           const uint64_t t0 = global_timer_ns();
           for (int rr = lane; rr < rows; rr += 32) {
@@ -736,10 +793,12 @@ __global__ void __launch_bounds__(kW * 32, 1) gemv_chain_kernel(const Args a) {
               v *= up;
             } else if (kEpi && epi == kEpiAdd) {
               float b;
-              if (base_mirror != nullptr) {
+              if (base_mirror != nullptr && !*sm.broken) {
                 uint64_t w = ld_relaxed_b64(base_mirror + row0 + rr);
+                unsigned ns = 32;
                 while (!has_tag(w, base_tag) && !late) {
                   late = global_timer_ns() - t0 > kWaitLimitNs;
+                  poll_backoff(ns);
                   w = ld_relaxed_b64(base_mirror + row0 + rr);
                 }
                 b = word_value(w);
@@ -752,23 +811,18 @@ __global__ void __launch_bounds__(kW * 32, 1) gemv_chain_kernel(const Args a) {
             if (my_mirror != nullptr) st_relaxed_b64(my_mirror + row0 + rr, tagged(v, my_tag));
           }
           if (late) {
-            record_device_error(kDevChainTimeout);
+            record_error(a, kDevChainTimeout);
             *sm.broken = 1;
           }
         }
         __syncwarp();
-        if (lane == 0 && i + a.ring < cnt && !*sm.broken) {
-          o_ahead = find_op(ops, a.count, ahead.u, o_ahead);
-          fence_proxy_async_smem();  // the warps' reads of the slot precede the copy's writes
-          issue_unit<kEpi>(a, ops, ring, sm.full, o_ahead, ahead.u, slot);
-          *sm.issued = i + a.ring + 1;
-        }
+        if (lane == 0) mbar_arrive(&sm.free[slot]);
       }
     }
   }
 
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == kW * 32) {
     // After an error, copies still in flight land before the CTA exits.
     const int iss = *sm.issued;
     for (int s = 0; s < a.ring && s < iss; ++s) {
@@ -934,12 +988,7 @@ int plan_chain(const mli_gemv_op* in, int count, int sm_count, int smem_per_sm, 
         }
       if (op.base >= 0 && (op.base >= s.wait || in[op.base].d != s.d)) return MLI_ERR_INVALID_ARG;
     }
-    op.mirror = -1;
-    if (!companion) {
-      op.mirror = static_cast<int>(mirror);
-      mirror += align_up(static_cast<size_t>(s.d), 2);  // 16-byte aligned runs
-      if (mirror > (1u << 30)) return MLI_ERR_UNSUPPORTED;
-    }
+    op.mirror = -1;  // assigned below to the ops some later op reads
     // Ops of the wait prefix [0, wait) that must be checked by tag: all but
     // those implied by an op whose rows this op reads anyway (that op was
     // written only after its own prefix [0, wait_j) had completed).  A
@@ -984,6 +1033,21 @@ int plan_chain(const mli_gemv_op* in, int count, int sm_count, int smem_per_sm, 
     if (R * S > part_stride) part_stride = R * S;
   }
   p->phases.push_back(static_cast<int>(units));
+  // Mirrors only for ops whose rows another op reads (as its activation, as
+  // its ADD base, or to check completion): a chain without dependencies
+  // writes none.
+  std::vector<char> read(count, 0);
+  for (int i = 0; i < count; ++i) {
+    if (p->ops[i].src >= 0) read[p->ops[i].src] = 1;
+    if (p->ops[i].base >= 0) read[p->ops[i].base] = 1;
+  }
+  for (int j : p->polls) read[j] = 1;
+  for (int i = 0; i < count; ++i)
+    if (read[i] && p->ops[i].epi != kEpiCompanion) {
+      p->ops[i].mirror = static_cast<int>(mirror);
+      mirror += align_up(static_cast<size_t>(p->ops[i].d), 2);  // 16-byte aligned runs
+      if (mirror > (1u << 30)) return MLI_ERR_UNSUPPORTED;
+    }
   p->mirror_words = mirror;
   Args& a = p->args;
   a.count = count;
@@ -1074,7 +1138,7 @@ int mli_chain_create(const mli_gemv_op* ops, int count, mli_chain** chain_out) {
                                    launch_flags(), &p);
   if (rc != MLI_OK) return set_status(rc);
   const chain::KernelFn kfn = chain::kernel_for(ops[0].form, p.v);
-  const int threads = p.v.warps * 32;
+  const int threads = (p.v.warps + 1) * 32;
   err = ensure_dynamic_smem(reinterpret_cast<const void*>(kfn), p.smem);
   if (err != cudaSuccess) return check_cuda(err);
   int per_sm = 0;
@@ -1120,6 +1184,7 @@ int mli_chain_create(const mli_gemv_op* ops, int count, mli_chain** chain_out) {
   c->args.mirror = reinterpret_cast<uint64_t*>(base + table + phases + polls);
   c->args.seq = reinterpret_cast<unsigned*>(base + table + phases + polls + mirror);
   c->args.finished = c->args.seq + 1;
+  c->args.err = device_error_word();
   c->dev_mem = mem;
   *chain_out = c;
   return set_status(MLI_OK);
