@@ -634,10 +634,10 @@ def classifier_measure(args, device, rank, world, form, allgather="p2p", sampler
         for _ in range(3):
             logits = forward()
     torch.cuda.synchronize()
-    if logits is None:  # fused: read back this rank's copy of the last step's logits
-        logits = torch.empty(d, dtype=torch.float32, device=device)
+    barrier(world)  # every rank's words of the last step have landed
+    if logits is None:  # fused: this rank's copy of the last step's logits (tags checked)
         last = lins[0]
-        ops.copy_from_ptr(logits, last.logits((last.steps - 1) & 1), d * 4)
+        logits = torch.from_numpy(last.read_logits(last.steps - 1)).to(device)
     ok_bits = bool(torch.equal(logits.view(torch.int32), y1.view(torch.int32)))
     ref_arg = int(torch.argmax(y1).item())
     ok_arg = int(idx.item()) == ref_arg

@@ -272,57 +272,54 @@ int mli_peer_free(void* ptr);
  * src/model_cuda_v2_shared.cu:418 / :564, on one GPU).  Rows
  * [row_offset, row_offset + rows) of the d_total-row layer are computed from
  * this rank's weight shard and stored over NVLink into every rank's logits
- * buffer peer_logits[p] (each [2][d_total] fp32; the half is *step & 1);
- * every CTA then adds its row count to peer_rows[p][rank] (uint64).
- * peer_logits / peer_rows are HOST arrays of `world` device pointers (this
- * rank's own buffers at index `rank`).  form: 0 W8A32, 2 fused W8A8. */
-int mli_gemv_rowshard(int form, float* const* peer_logits,
-                      unsigned long long* const* peer_rows, const unsigned* step,
-                      const float* x, const int8_t* w_q, const float* w_s, int n,
-                      int rows, int row_offset, int d_total, int rank, int world,
-                      int group_size, void* stream);
+ * words peer_logits[p] ([2][d_total]; the half is *step & 1), each row as one
+ * 8-byte word {fp32 value, tag of the step}; every CTA also stores its rows'
+ * (max, first index) as one tagged partial word into every rank's block.  No
+ * fence and no counter: a reader knows a word has arrived by its tag.
+ * peer_logits is a HOST array of `world` device pointers (offset 256 of
+ * every rank's peer block; this rank's own at index `rank`).  form: 0 W8A32,
+ * 2 fused W8A8.  d_total < 2^20. */
+int mli_gemv_rowshard(int form, unsigned long long* const* peer_logits, const unsigned* step,
+                      const float* x, const int8_t* w_q, const float* w_s, int n, int rows,
+                      int row_offset, int d_total, int rank, int world, int group_size,
+                      void* stream);
 
 /* mli_gemv_rowshard and mli_rowshard_wait_argmax in one launch: the CTAs
- * store their rows into every rank's logits as above, but the launch's last
- * CTA raises peer_rows[p][rank] once for all of this rank's rows (one
- * system-scope fence per launch instead of one per CTA), then waits (bounded
- * by timeout_us) for every rank's rows of this step, reduces every rank's CTA
- * partials to the argmax, writes it to *out and advances the step -- one
- * kernel per step instead of two.  own_block
- * is this rank's peer block (its header holds the counters, the step and the
- * launch's finished-CTA count); shard_rows is a HOST array of `world` row
- * counts (every rank's `rows`) summing to d_total.  On expiry *out = -1 and
- * the device error word is set. */
-int mli_gemv_rowshard_argmax(int form, float* const* peer_logits,
-                             unsigned long long* const* peer_rows, void* own_block,
+ * store their tagged rows and partial words into every rank's block as
+ * above; the launch's last CTA then polls (bounded by timeout_us) every
+ * rank's partial words of this step, reduces them to the argmax, writes it to
+ * *out and advances the step -- one kernel per step.  own_block is this
+ * rank's peer block (its header holds the step and the launch's finished-CTA
+ * count); shard_rows is a HOST array of `world` row counts (every rank's
+ * `rows`) summing to d_total.  On expiry *out = -1 and the device error word
+ * is set. */
+int mli_gemv_rowshard_argmax(int form, unsigned long long* const* peer_logits, void* own_block,
                              const float* x, const int8_t* w_q, const float* w_s, int n,
                              int rows, int row_offset, int d_total, int rank, int world,
                              int group_size, const int* shard_rows, long long* out,
                              int timeout_us, void* stream);
 
 /* Bytes of one rank's peer block for a d_total-row layer:
- *   [0, 64)    uint64 row counters, one per source rank
  *   [128, 132) uint32 step counter
  *   [192, 196) uint32 finished-CTA count of a fused step (zero between steps)
- *   [196, 200) uint32 rows produced by a fused step's CTAs (zero between steps)
- *   [256, ...) fp32 logits [2][d_total], then (at the next 16-byte boundary)
- *              the CTAs' (max, first index) partials int2 [2][8][512].
- * mli_gemv_rowshard's peer_logits[p] and mli_rowshard_wait_argmax's logits
- * point at offset 256 of a block, peer_rows[p] / rows_ctr at offset 0. */
+ *   [256, ...) logits words uint64 [2][d_total] (low 32 bits the fp32 value,
+ *              high 32 bits the step's tag), then (16-byte aligned) the CTAs'
+ *              partial words uint64 [2][8][512] (low 32 bits the maximum,
+ *              high 32 bits (first index << 12) | tag).
+ * The tag of step s is (s mod 4095) + 1; a zeroed block matches no step. */
 size_t mli_rowshard_block_bytes(int d_total);
 
-/* Completes a row-sharded step on this rank: waits until rank r's counter
- * rows_ctr[r] reaches (*step + 1) * shard_rows[r] for every r (bounded by
- * timeout_us; on expiry *out = -1 and the device error word is set), then
- * reduces every rank's CTA partials of this step to the first maximum of the
- * full logits (the reference's host argmax rule), writes its index to *out and
- * increments *step.  form and n are the GEMV's (they fix each rank's CTA
- * count); shard_rows is a HOST array of `world` row counts summing to
- * d_total. */
-int mli_rowshard_wait_argmax(int form, int n, const float* logits,
-                             const unsigned long long* rows_ctr, unsigned* step,
-                             const int* shard_rows, int world, int d_total,
-                             long long* out, int timeout_us, void* stream);
+/* Completes a row-sharded step on this rank: polls (bounded by timeout_us;
+ * on expiry *out = -1 and the device error word is set) every rank's partial
+ * words of step *step in this rank's block until their tags arrive, reduces
+ * them to the first maximum of the full logits (the reference's host argmax
+ * rule), writes its index to *out and increments *step.  form and n are the
+ * GEMV's (they fix each rank's CTA count); logits points at offset 256 of
+ * this rank's block; shard_rows is a HOST array of `world` row counts summing
+ * to d_total. */
+int mli_rowshard_wait_argmax(int form, int n, const unsigned long long* logits, unsigned* step,
+                             const int* shard_rows, int world, int d_total, long long* out,
+                             int timeout_us, void* stream);
 
 /* Index of the first maximum of x[0..n), on the device (replaces the
  * reference's logits copy to the host and host argmax, src/main_cuda.cpp:96-98,

@@ -67,11 +67,10 @@ SIGNATURES = {
     "mli_peer_open": (_I, [ctypes.c_char_p, ctypes.POINTER(_P)]),
     "mli_peer_close": (_I, [_P]),
     "mli_peer_free": (_I, [_P]),
-    "mli_gemv_rowshard": (_I, [_I, ctypes.POINTER(_P), ctypes.POINTER(_P), _P, _P, _P, _P, _I, _I, _I,
-                               _I, _I, _I, _I, _P]),
-    "mli_rowshard_wait_argmax": (_I, [_I, _I, _P, _P, _P, ctypes.POINTER(_I), _I, _I, _P, _I, _P]),
-    "mli_gemv_rowshard_argmax": (_I, [_I, ctypes.POINTER(_P), ctypes.POINTER(_P), _P, _P, _P, _P, _I, _I, _I,
-                                      _I, _I, _I, _I, ctypes.POINTER(_I), _P, _I, _P]),
+    "mli_gemv_rowshard": (_I, [_I, ctypes.POINTER(_P), _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P]),
+    "mli_rowshard_wait_argmax": (_I, [_I, _I, _P, _P, ctypes.POINTER(_I), _I, _I, _P, _I, _P]),
+    "mli_gemv_rowshard_argmax": (_I, [_I, ctypes.POINTER(_P), _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I,
+                                      ctypes.POINTER(_I), _P, _I, _P]),
     "mli_rowshard_block_bytes": (ctypes.c_size_t, [_I]),
     "mli_argmax": (_I, [_P, _I, _P, _P]),
     "mli_gemv_f32": (_I, [_P, _P, _P, _I, _I, _P]),

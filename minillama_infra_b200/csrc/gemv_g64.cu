@@ -89,24 +89,21 @@ struct StreamArgs {
   uint32_t stage_bytes;  // R * n + R * G * 4
   uint32_t x_off, ring_off, part_off;
   // Row-sharded output (world > 0): row r of this launch is global row
-  // row_offset + r; its value is stored into every rank's logits buffer
-  // peer_y[p] ([2][d_total], the half chosen by *step & 1), and every CTA
-  // then adds the number of rows it produced to peer_rows[p][rank].
+  // row_offset + r; its value is stored, tagged with the step, into every
+  // rank's logits words peer_y[p] ([2][d_total], the half chosen by
+  // *step & 1), and every CTA stores its rows' (max, first index) as one
+  // tagged partial word into every rank's block (no counters, no fences).
   int world, rank, row_offset, d_total;
   uint32_t out_off;  // shared-memory staging of this CTA's output rows
   const unsigned* step;
-  float* peer_y[kMaxPeers];
-  unsigned long long* peer_rows[kMaxPeers];
+  unsigned long long* peer_y[kMaxPeers];
   // Fused argmax (row-sharded, out != nullptr): the last CTA of the launch
-  // waits for every rank's rows of this step, reduces the CTA partials to the
+  // polls every rank's partial words of this step, reduces them to the
   // argmax, writes it and advances the step.
   long long* out;
   unsigned* step_rw;                   // this rank's step counter
   unsigned* ctas_done;                 // this rank's finished-CTA count (zero between launches)
-  unsigned* rows_done;                 // rows this launch's CTAs produced (zero between launches)
-  const unsigned long long* my_rows;   // this rank's per-source row counters
   unsigned long long timeout_ns;
-  int shard_rows[kMaxPeers];
   int shard_ctas[kMaxPeers];
 };
 
@@ -125,10 +122,6 @@ __device__ __forceinline__ void store_row(const StreamArgs& a, int row, float v,
   } else {
     staged[row - cta_row0] = v;
   }
-}
-
-__device__ __forceinline__ void fence_acq_rel_sys() {
-  asm volatile("fence.acq_rel.sys;" ::: "memory");
 }
 
 // (max, first index) over v[0..n) by the CTA's 256 threads, scanning each
@@ -323,13 +316,13 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_stream_kernel(const StreamAr
     }
   }
   if constexpr (kPeer) {
-    // Publish the CTA's rows to every rank as one coalesced burst, with the
-    // rows' (max, first index) in this CTA's partial slot, then raise every
-    // rank's counter for this rank by the rows produced.  A CTA that gave up
-    // on a stage publishes nothing (the counters are never raised for rows
-    // that were not produced).
+    // Publish the CTA's rows to every rank as one coalesced burst of tagged
+    // words, then the rows' (max, first index) as one tagged partial word per
+    // rank.  A reader knows a word has arrived by its tag, so nothing here
+    // waits for a fence.  A CTA that gave up on a stage publishes nothing.
     __syncthreads();
     const bool broken = *sm.broken != 0;
+    const unsigned tag = rowshard_tag(*a.step);
     if (!broken) {
       const int cta_rows = max(0, min((begin + cnt) * a.R, a.d) - cta_row0);
       __shared__ float s_best_v;
@@ -338,103 +331,34 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_stream_kernel(const StreamAr
       __syncthreads();
       const size_t off = static_cast<size_t>(parity) * a.d_total + a.row_offset + cta_row0;
       for (int p = 0; p < a.world; ++p) {
-        float* dst = a.peer_y[p] + off;
-        for (int i = threadIdx.x; i < cta_rows; i += kConsumerThreads) dst[i] = staged[i];
-        if (threadIdx.x == 0) {
-          int2* slot = rowshard_partials(a.peer_y[p], a.d_total) +
-                       (static_cast<size_t>(parity) * kMaxPeers + a.rank) * kMaxRankCtas + blockIdx.x;
-          *slot = make_int2(__float_as_int(s_best_v), s_best_i);
-        }
-      }
-      // The barrier orders every thread's stores before thread 0's fence,
-      // which (being cumulative) publishes them before the count.
-      __syncthreads();
-      if (threadIdx.x == 0 && cta_rows > 0) {
-        if (a.out == nullptr) {
-          // two-launch step: every CTA raises the ranks' counters itself
-          fence_acq_rel_sys();
-          for (int p = 0; p < a.world; ++p)
-            atomicAdd_system(a.peer_rows[p] + a.rank, static_cast<unsigned long long>(cta_rows));
-        } else {
-          // fused step: the launch's last CTA raises them once for all rows
-          atomicAdd(a.rows_done, static_cast<unsigned>(cta_rows));
+        unsigned long long* dst = a.peer_y[p] + off;
+        for (int i = threadIdx.x; i < cta_rows; i += kConsumerThreads)
+          st_relaxed_sys_b64(dst + i, tag_word(__float_as_uint(staged[i]), tag));
+        if (threadIdx.x == 0 && cta_rows > 0) {
+          unsigned long long* slot = rowshard_partials(a.peer_y[p], a.d_total) +
+                                     (static_cast<size_t>(parity) * kMaxPeers + a.rank) * kMaxRankCtas + blockIdx.x;
+          st_relaxed_sys_b64(slot, tag_word(__float_as_uint(s_best_v),
+                                            (static_cast<unsigned>(s_best_i) << 12) | tag));
         }
       }
     }
     if (a.out == nullptr) return;
-    // Fused argmax: the last CTA to finish takes over.
+    // Fused argmax: the last CTA to finish takes over (every other CTA of
+    // the launch has stored its words by then).
     __shared__ int s_last;
-    if (threadIdx.x == 0) {
-      __threadfence();
-      s_last = atomicAdd(a.ctas_done, 1u) == gridDim.x - 1;
-    }
+    if (threadIdx.x == 0) s_last = atomicAdd(a.ctas_done, 1u) == gridDim.x - 1;
     __syncthreads();
     if (!s_last) return;
-    __shared__ int s_fail;
-    if (threadIdx.x == 0) {
-      // Every other CTA's stores and row count precede its finished-count
-      // increment (release at GPU scope), which this CTA has acquired; one
-      // system-scope fence then publishes all of them before the ranks'
-      // counters rise (a release chain: one fence per launch instead of one
-      // per CTA).  Rows a CTA did not produce are never counted.
-      __threadfence();
-      *a.ctas_done = 0;  // every other CTA of this launch is done with it
-      const unsigned produced = atomicExch(a.rows_done, 0u);
-      fence_acq_rel_sys();
-      if (produced > 0)
-        for (int p = 0; p < a.world; ++p)
-          atomicAdd_system(a.peer_rows[p] + a.rank, static_cast<unsigned long long>(produced));
-      s_fail = 0;
-    }
-    __syncthreads();
+    if (threadIdx.x == 0) *a.ctas_done = 0;  // every other CTA of this launch is done with it
+    __shared__ int s_int;
     const unsigned s = *a.step;
-    if (threadIdx.x < a.world) {
-      const unsigned long long target =
-          static_cast<unsigned long long>(s + 1) * static_cast<unsigned long long>(a.shard_rows[threadIdx.x]);
-      const uint64_t t0 = global_timer_ns();
-      while (ld_acquire_sys(a.my_rows + threadIdx.x) < target) {
-        if (global_timer_ns() - t0 > a.timeout_ns) {
-          atomicExch(&s_fail, 1);
-          break;
-        }
-      }
-    }
-    __syncthreads();
-    if (s_fail) {
-      if (threadIdx.x == 0) {
-        record_device_error(kDevPeerTimeout);
-        *a.out = -1;
-      }
-      return;
-    }
-    // Every rank's CTAs left their rows' (max, first index) in this step's
-    // half of this rank's partials: reduce those, not the whole logits.
-    const float* own = a.peer_y[a.rank];
-    const int2* parts = rowshard_partials(own, a.d_total) + static_cast<size_t>(parity) * kMaxPeers * kMaxRankCtas;
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
-    for (int r = 0; r < a.world; ++r)
-      for (int c = threadIdx.x; c < a.shard_ctas[r]; c += kConsumerThreads) {
-        const int2 pr = __ldcg(parts + r * kMaxRankCtas + c);
-        argmax_combine(bv, bi, __int_as_float(pr.x), pr.y);
-      }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      argmax_combine(bv, bi, ov, oi);
-    }
-    if ((threadIdx.x & 31) == 0) {
-      sm.red[threadIdx.x >> 5] = bv;
-      sm.red_i[threadIdx.x >> 5] = bi;
-    }
-    __syncthreads();
+    const long long best =
+        rowshard_poll_argmax<kConsumerThreads>(a.peer_y[a.rank], a.d_total, s & 1u, rowshard_tag(s), a.world,
+                                               a.shard_ctas, a.timeout_ns, sm.red, sm.red_i, &s_int);
     if (threadIdx.x == 0) {
-      for (int w = 1; w < kConsumerWarps; ++w) argmax_combine(bv, bi, sm.red[w], sm.red_i[w]);
-      const float x0 = __ldcg(own + static_cast<size_t>(parity) * a.d_total);
-      if (bi == 0x7fffffff || x0 != x0) bi = 0;  // the reference's scan starts from x[0]
-      *a.out = bi;
-      *a.step_rw = s + 1;
+      if (best < 0) record_device_error(kDevPeerTimeout);
+      *a.out = best;
+      if (best >= 0) *a.step_rw = s + 1;
     }
   }
 }
@@ -684,16 +608,16 @@ int mli_gemv_w8a8_fused(float* y, int8_t* xq_out, float* xs_out, const float* x,
   return mli_gemv_w8a8(y, xq_out, xs_out, w_q, w_s, n, d, group_size, stream);
 }
 
-int mli_gemv_rowshard(int form, float* const* peer_logits, unsigned long long* const* peer_rows,
-                      const unsigned* step, const float* x, const int8_t* w_q, const float* w_s,
-                      int n, int rows, int row_offset, int d_total, int rank, int world,
-                      int group_size, void* stream) {
-  if (!peer_logits || !peer_rows || !step || !x || world <= 0 || world > kMaxPeers || rank < 0 ||
-      rank >= world || rows < 0 || row_offset < 0 || row_offset + rows > d_total || n <= 0 ||
-      group_size <= 0 || (form != 0 && form != 2))
+int mli_gemv_rowshard(int form, unsigned long long* const* peer_logits, const unsigned* step,
+                      const float* x, const int8_t* w_q, const float* w_s, int n, int rows, int row_offset,
+                      int d_total, int rank, int world, int group_size, void* stream) {
+  if (!peer_logits || !step || !x || world <= 0 || world > kMaxPeers || rank < 0 || rank >= world ||
+      rows < 0 || row_offset < 0 || row_offset + rows > d_total || n <= 0 || group_size <= 0 ||
+      (form != 0 && form != 2))
     return set_status(MLI_ERR_INVALID_ARG);
   for (int p = 0; p < world; ++p)
-    if (!peer_logits[p] || !peer_rows[p]) return set_status(MLI_ERR_INVALID_ARG);
+    if (!peer_logits[p]) return set_status(MLI_ERR_INVALID_ARG);
+  if (d_total >= kMaxRowshardRows) return set_status(MLI_ERR_UNSUPPORTED);
   if (rows == 0) return set_status(MLI_OK);
   if (!w_q || !w_s) return set_status(MLI_ERR_INVALID_ARG);
   if (!fast_path_ok(n, group_size) || !aligned(x, 16) || !aligned(w_q, 16) || !aligned(w_s, 16))
@@ -701,27 +625,24 @@ int mli_gemv_rowshard(int form, float* const* peer_logits, unsigned long long* c
   StreamArgs a = {};
   a.x = x; a.w = w_q; a.s = w_s;
   a.world = world; a.rank = rank; a.row_offset = row_offset; a.d_total = d_total; a.step = step;
-  for (int p = 0; p < world; ++p) {
-    a.peer_y[p] = peer_logits[p];
-    a.peer_rows[p] = peer_rows[p];
-  }
+  for (int p = 0; p < world; ++p) a.peer_y[p] = peer_logits[p];
   return launch_stream(form == 0 ? Form::kW8A32 : Form::kW8A8Fused, a, n, rows,
                        static_cast<cudaStream_t>(stream));
 }
 
-int mli_gemv_rowshard_argmax(int form, float* const* peer_logits,
-                             unsigned long long* const* peer_rows, void* own_block,
+int mli_gemv_rowshard_argmax(int form, unsigned long long* const* peer_logits, void* own_block,
                              const float* x, const int8_t* w_q, const float* w_s, int n,
                              int rows, int row_offset, int d_total, int rank, int world,
                              int group_size, const int* shard_rows, long long* out,
                              int timeout_us, void* stream) {
-  if (!peer_logits || !peer_rows || !own_block || !x || !shard_rows || !out || world <= 0 ||
+  if (!peer_logits || !own_block || !x || !shard_rows || !out || world <= 0 ||
       world > kMaxPeers || rank < 0 || rank >= world || rows <= 0 || row_offset < 0 ||
       row_offset + rows > d_total || n <= 0 || group_size <= 0 || timeout_us <= 0 ||
       (form != 0 && form != 2) || !w_q || !w_s)
     return set_status(MLI_ERR_INVALID_ARG);
   for (int p = 0; p < world; ++p)
-    if (!peer_logits[p] || !peer_rows[p]) return set_status(MLI_ERR_INVALID_ARG);
+    if (!peer_logits[p]) return set_status(MLI_ERR_INVALID_ARG);
+  if (d_total >= kMaxRowshardRows) return set_status(MLI_ERR_UNSUPPORTED);
   if (!fast_path_ok(n, group_size) || !aligned(x, 16) || !aligned(w_q, 16) || !aligned(w_s, 16))
     return set_status(MLI_ERR_UNSUPPORTED);
   StreamArgs a = {};
@@ -731,17 +652,13 @@ int mli_gemv_rowshard_argmax(int form, float* const* peer_logits,
   a.step = reinterpret_cast<const unsigned*>(blk + 128);
   a.step_rw = reinterpret_cast<unsigned*>(blk + 128);
   a.ctas_done = reinterpret_cast<unsigned*>(blk + 192);
-  a.rows_done = reinterpret_cast<unsigned*>(blk + 196);
-  a.my_rows = reinterpret_cast<const unsigned long long*>(blk);
   a.out = out;
   a.timeout_ns = static_cast<unsigned long long>(timeout_us) * 1000ull;
   long long total = 0;
   const Form f = form == 0 ? Form::kW8A32 : Form::kW8A8Fused;
   for (int p = 0; p < world; ++p) {
     a.peer_y[p] = peer_logits[p];
-    a.peer_rows[p] = peer_rows[p];
     if (shard_rows[p] <= 0) return set_status(MLI_ERR_INVALID_ARG);
-    a.shard_rows[p] = shard_rows[p];
     a.shard_ctas[p] = rowshard_grid(form, n, shard_rows[p]);
     if (a.shard_ctas[p] <= 0 || a.shard_ctas[p] > kMaxRankCtas) return set_status(MLI_ERR_UNSUPPORTED);
     total += shard_rows[p];

@@ -26,22 +26,48 @@ extern __device__ unsigned int g_device_error;
 #endif
 
 // Row-sharded layers (gemv_g64.cu, rowshard.cu): at most this many ranks and
-// CTAs per rank.  Each rank's logits buffer ([2][d_total] fp32) is followed,
-// at the next 16-byte boundary, by the (max, first index) partials of every
-// CTA of every rank, int2 [2][kMaxPeers][kMaxRankCtas].
+// CTAs per rank.  A rank's peer block holds its logits as 8-byte words
+// [2][d_total] (the half is the step's parity), then, at the next 16-byte
+// boundary, one 8-byte partial word per CTA of every rank,
+// [2][kMaxPeers][kMaxRankCtas].  Every word carries the tag of the step that
+// wrote it, so a reader knows a word has arrived by the word alone:
+//   logits word:  low 32 bits the fp32 value, high 32 bits the tag;
+//   partial word: low 32 bits the CTA's maximum (fp32), high 32 bits
+//                 (first index << 12) | tag  (indices below 2^20).
+// Tags cycle 1 .. kRowTagPeriod; zeroed memory (tag 0) never matches.
 constexpr int kMaxPeers = 8;
 constexpr int kMaxRankCtas = 512;
+constexpr unsigned kRowTagPeriod = 4095;
+constexpr int kMaxRowshardRows = 1 << 20;
 
-__host__ __device__ __forceinline__ int2* rowshard_partials(float* logits, int d_total) {
-  const size_t bytes = (static_cast<size_t>(d_total) * 8u + 15u) & ~static_cast<size_t>(15);
-  return reinterpret_cast<int2*>(reinterpret_cast<char*>(logits) + bytes);
+__host__ __device__ __forceinline__ unsigned rowshard_tag(unsigned step) {
+  return step % kRowTagPeriod + 1;
 }
-__host__ __device__ __forceinline__ const int2* rowshard_partials(const float* logits, int d_total) {
-  return rowshard_partials(const_cast<float*>(logits), d_total);
+__host__ __device__ __forceinline__ unsigned long long* rowshard_partials(unsigned long long* logits,
+                                                                         int d_total) {
+  return logits + ((static_cast<size_t>(d_total) * 2u + 1u) & ~static_cast<size_t>(1));
+}
+__host__ __device__ __forceinline__ const unsigned long long* rowshard_partials(const unsigned long long* logits,
+                                                                               int d_total) {
+  return rowshard_partials(const_cast<unsigned long long*>(logits), d_total);
 }
 __host__ __device__ constexpr size_t rowshard_block_bytes(int d_total) {
-  return 256 + ((static_cast<size_t>(d_total) * 8u + 15u) & ~static_cast<size_t>(15)) +
-         sizeof(int2) * 2 * kMaxPeers * kMaxRankCtas;
+  return 256 + ((static_cast<size_t>(d_total) * 2u + 1u) & ~static_cast<size_t>(1)) * 8u +
+         8u * 2 * kMaxPeers * kMaxRankCtas;
+}
+
+// System-scope relaxed 8-byte accesses of tagged words (single-copy atomic:
+// a reader sees a value together with its tag).
+__device__ __forceinline__ void st_relaxed_sys_b64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_b64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned long long tag_word(uint32_t lo, uint32_t hi) {
+  return (static_cast<unsigned long long>(hi) << 32) | lo;
 }
 
 #ifndef MLI_SEPARATE_DEVICE_MODULE
@@ -253,6 +279,108 @@ __device__ __forceinline__ void argmax_combine(float& bv, int& bi, float v, int 
     bv = v;
     bi = i;
   }
+}
+
+// Completes a row-sharded step on kT threads of one CTA: polls every rank's
+// CTA partial words of this step (tag `tag`, half `parity` of this rank's
+// block), reduces them to the first maximum of the full logits (the
+// reference's host argmax, src/main_cuda.cpp:96-98), and returns it on every
+// thread -- or -1 if a word did not arrive within timeout_ns.  Each thread
+// loads all of its words at once and reloads only the missing ones, so a step
+// costs one round trip per retry, not one per word.  `red_v` / `red_i` hold
+// kT / 32 entries; `s_int` is one shared int.
+template <int kT>
+__device__ __forceinline__ long long rowshard_poll_argmax(const unsigned long long* logits, int d_total,
+                                                          unsigned parity, unsigned tag, int world,
+                                                          const int* shard_ctas, unsigned long long timeout_ns,
+                                                          float* red_v, int* red_i, int* s_int) {
+  constexpr int kPer = (kMaxPeers * kMaxRankCtas + kT - 1) / kT;
+  const unsigned long long* parts = rowshard_partials(logits, d_total) +
+                                    static_cast<size_t>(parity) * kMaxPeers * kMaxRankCtas;
+  int start[kMaxPeers + 1];
+  start[0] = 0;
+#pragma unroll
+  for (int r = 0; r < kMaxPeers; ++r) start[r + 1] = start[r] + (r < world ? shard_ctas[r] : 0);
+  const int total = start[kMaxPeers];
+  // this thread's words: flat indices threadIdx.x + k kT, k < kPer
+  unsigned pending = 0;
+  int slot[kPer];
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const int f = static_cast<int>(threadIdx.x) + k * kT;
+    slot[k] = 0;
+    if (f < total) {
+      int r = 0;
+#pragma unroll
+      for (int q = 1; q < kMaxPeers; ++q) r += f >= start[q] ? 1 : 0;
+      slot[k] = r * kMaxRankCtas + (f - start[r]);
+      pending |= 1u << k;
+    }
+  }
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  bool fail = false;
+  const uint64_t t0 = global_timer_ns();
+  unsigned ns = 32;
+  while (pending != 0) {
+    unsigned long long w[kPer];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k)
+      if ((pending >> k) & 1u) w[k] = ld_relaxed_sys_b64(parts + slot[k]);
+#pragma unroll
+    for (int k = 0; k < kPer; ++k)
+      if (((pending >> k) & 1u) && (static_cast<unsigned>(w[k] >> 32) & 0xfffu) == tag) {
+        argmax_combine(bv, bi, __uint_as_float(static_cast<unsigned>(w[k])), static_cast<int>(w[k] >> 44));
+        pending &= ~(1u << k);
+      }
+    if (pending == 0) break;
+    if (global_timer_ns() - t0 > timeout_ns) {
+      fail = true;
+      break;
+    }
+    __nanosleep(ns);
+    ns = ns < 256 ? 2 * ns : 256;
+  }
+  // the reference's scan starts from x[0]: its value decides a NaN start
+  float x0 = 0.f;
+  if (threadIdx.x == 0 && !fail) {
+    const unsigned long long* w0 = logits + static_cast<size_t>(parity) * d_total;
+    unsigned long long w = ld_relaxed_sys_b64(w0);
+    while (static_cast<unsigned>(w >> 32) != tag) {
+      if (global_timer_ns() - t0 > timeout_ns) {
+        fail = true;
+        break;
+      }
+      __nanosleep(64);
+      w = ld_relaxed_sys_b64(w0);
+    }
+    x0 = __uint_as_float(static_cast<unsigned>(w));
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+    argmax_combine(bv, bi, ov, oi);
+  }
+  if (threadIdx.x == 0) *s_int = 0;
+  __syncthreads();
+  if (fail) atomicExch(s_int, 1);
+  if ((threadIdx.x & 31) == 0) {
+    red_v[threadIdx.x >> 5] = bv;
+    red_i[threadIdx.x >> 5] = bi;
+  }
+  __syncthreads();
+  const bool failed = *s_int != 0;
+  bv = red_v[0];
+  bi = red_i[0];
+#pragma unroll
+  for (int w = 1; w < kT / 32; ++w) argmax_combine(bv, bi, red_v[w], red_i[w]);
+  __syncthreads();
+  if (threadIdx.x == 0) *s_int = (bi == 0x7fffffff || x0 != x0) ? 0 : bi;
+  __syncthreads();
+  const long long res = failed ? -1 : *s_int;
+  __syncthreads();
+  return res;
 }
 
 __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {

@@ -1,15 +1,18 @@
 // rowshard.cu -- row-sharded classifier support: peer buffers over CUDA IPC,
 // device argmax, and the bounded wait that completes a sharded GEMV step.
 //
-// A row-sharded step on every rank is two launches on that rank's stream:
+// A row-sharded step on every rank is two launches on that rank's stream
+// (or one, mli_gemv_rowshard_argmax, which does both):
 //   1. mli_gemv_rowshard: the streaming GEMV over this rank's rows, storing
-//      each output row straight into every rank's logits buffer over NVLink
-//      and adding its row count to every rank's per-source counters;
-//   2. mli_rowshard_wait_argmax: waits (bounded) until every rank's rows of
-//      this step have arrived, then reduces the full logits to their argmax
-//      and advances the step counter (which also flips the logits half the
-//      next step writes, so a slow rank still reading this step's half is
-//      never overwritten).
+//      each output row, tagged with the step, straight into every rank's
+//      logits words over NVLink, and each CTA's (max, first index) as one
+//      tagged partial word into every rank's block;
+//   2. mli_rowshard_wait_argmax: polls (bounded) every rank's partial words
+//      of this step until their tags arrive, reduces them to the argmax and
+//      advances the step counter (which also flips the half the next step
+//      writes, so a slow rank still reading this step's half is never
+//      overwritten).  No fence and no counter is needed: each word says by
+//      itself whether it belongs to this step.
 // The argmax replaces the reference's device-to-host copy of the logits and
 // host argmax (src/main_cuda.cpp:96-98, src/model_cuda_v2_shared.cu:571-575)
 // with the same first-maximum rule.
@@ -94,82 +97,29 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* x, 
 }
 
 struct WaitArgs {
-  const float* logits;              // this rank's [2][d_total] (partials follow)
-  const unsigned long long* rows;   // this rank's counters [world], raised by every rank
-  unsigned* step;                   // this rank's step counter
+  const unsigned long long* logits;  // this rank's logits words [2][d_total] (partials follow)
+  unsigned* step;                    // this rank's step counter
   long long* out;
   int world, d_total;
   unsigned long long timeout_ns;
-  int shard_rows[kMaxPeers];        // rows each rank contributes per step
-  int shard_ctas[kMaxPeers];        // CTAs (partial slots) each rank writes per step
+  int shard_ctas[kMaxPeers];         // CTAs (partial words) each rank writes per step
 };
 
-
 __global__ void __launch_bounds__(kWaitThreads) rowshard_wait_argmax_kernel(const WaitArgs a) {
-  __shared__ unsigned s_step;
-  __shared__ int s_fail;
   __shared__ float red_v[kWaitThreads / 32];
   __shared__ int red_i[kWaitThreads / 32];
+  __shared__ int s_int;
   griddep_wait();
   // Let the next kernel launch and stream its weights during the wait; it
   // reads *step only after this kernel completes (its own griddepcontrol.wait).
   griddep_launch_dependents();
+  const unsigned s = *a.step;
+  const long long best = rowshard_poll_argmax<kWaitThreads>(a.logits, a.d_total, s & 1u, rowshard_tag(s), a.world,
+                                                            a.shard_ctas, a.timeout_ns, red_v, red_i, &s_int);
   if (threadIdx.x == 0) {
-    s_step = *a.step;
-    s_fail = 0;
-  }
-  __syncthreads();
-  const unsigned s = s_step;
-  if (threadIdx.x < a.world) {
-    const unsigned long long target =
-        static_cast<unsigned long long>(s + 1) * static_cast<unsigned long long>(a.shard_rows[threadIdx.x]);
-    const uint64_t t0 = global_timer_ns();
-    while (ld_acquire_sys(a.rows + threadIdx.x) < target) {
-      if (global_timer_ns() - t0 > a.timeout_ns) {
-        atomicExch(&s_fail, 1);
-        break;
-      }
-      __nanosleep(32);
-    }
-  }
-  __syncthreads();
-  if (s_fail) {
-    if (threadIdx.x == 0) {
-      record_device_error(kDevPeerTimeout);
-      *a.out = -1;
-    }
-    return;
-  }
-  // Every rank's CTAs left their rows' (max, first index) in this step's
-  // half of the partials: reduce those instead of the whole logits vector.
-  const unsigned parity = s & 1u;
-  const int2* parts = rowshard_partials(a.logits, a.d_total) +
-                      static_cast<size_t>(parity) * kMaxPeers * kMaxRankCtas;
-  float bv = -INFINITY;
-  int bi = 0x7fffffff;
-  for (int r = 0; r < a.world; ++r) {
-    for (int c = threadIdx.x; c < a.shard_ctas[r]; c += kWaitThreads) {
-      const int2 pr = __ldcg(parts + r * kMaxRankCtas + c);
-      argmax_combine(bv, bi, __int_as_float(pr.x), pr.y);
-    }
-  }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-    const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-    argmax_combine(bv, bi, ov, oi);
-  }
-  if ((threadIdx.x & 31) == 0) {
-    red_v[threadIdx.x >> 5] = bv;
-    red_i[threadIdx.x >> 5] = bi;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    for (int w = 1; w < kWaitThreads / 32; ++w) argmax_combine(bv, bi, red_v[w], red_i[w]);
-    const float x0 = __ldcg(a.logits + static_cast<size_t>(parity) * a.d_total);
-    if (bi == 0x7fffffff || x0 != x0) bi = 0;  // the reference's scan starts from x[0]
-    *a.out = bi;
-    *a.step = s + 1;
+    if (best < 0) record_device_error(kDevPeerTimeout);
+    *a.out = best;
+    if (best >= 0) *a.step = s + 1;
   }
 }
 
@@ -218,16 +168,15 @@ int mli_argmax(const float* x, int n, long long* out, void* stream) {
                            static_cast<cudaStream_t>(stream), true, x, n, out));
 }
 
-int mli_rowshard_wait_argmax(int form, int n, const float* logits,
-                             const unsigned long long* rows_ctr, unsigned* step,
+int mli_rowshard_wait_argmax(int form, int n, const unsigned long long* logits, unsigned* step,
                              const int* shard_rows, int world, int d_total, long long* out,
                              int timeout_us, void* stream) {
-  if (!logits || !rows_ctr || !step || !shard_rows || !out || world <= 0 || world > kMaxPeers ||
+  if (!logits || !step || !shard_rows || !out || world <= 0 || world > kMaxPeers ||
       d_total <= 0 || timeout_us <= 0 || n <= 0 || (form != 0 && form != 2))
     return set_status(MLI_ERR_INVALID_ARG);
+  if (d_total >= kMaxRowshardRows) return set_status(MLI_ERR_UNSUPPORTED);
   WaitArgs a = {};
   a.logits = logits;
-  a.rows = rows_ctr;
   a.step = step;
   a.out = out;
   a.world = world;
@@ -236,7 +185,6 @@ int mli_rowshard_wait_argmax(int form, int n, const float* logits,
   long long total = 0;
   for (int r = 0; r < world; ++r) {
     if (shard_rows[r] < 0) return set_status(MLI_ERR_INVALID_ARG);
-    a.shard_rows[r] = shard_rows[r];
     a.shard_ctas[r] = rowshard_grid(form, n, shard_rows[r]);
     if (a.shard_ctas[r] < 0 || a.shard_ctas[r] > kMaxRankCtas) return set_status(MLI_ERR_UNSUPPORTED);
     total += shard_rows[r];

@@ -94,25 +94,49 @@ class ShardedLinear:
         return self.full[: self.d]
 
 
+def rowshard_tag(step: int) -> int:
+    """Tag of the words a row-sharded step writes (mli_rowshard_block_bytes)."""
+    return step % 4095 + 1
+
+
+def read_tagged_logits(ptr: int, d: int, half: int, step: int):
+    """The fp32 logits of step `step` from a peer block's logits words at
+    device address `ptr` (offset 256 of the block), checking that every word
+    carries that step's tag.  Call it once every rank has finished the step."""
+    import numpy as np
+    import torch
+
+    from . import ops
+
+    raw = torch.empty(d, dtype=torch.int64, device=torch.cuda.current_device())
+    torch.cuda.synchronize()
+    ops.copy_from_ptr(raw, ptr + half * d * 8, d * 8)
+    words = raw.cpu().numpy().view(np.uint32).reshape(d, 2)
+    if not np.all(words[:, 1] == rowshard_tag(step)):
+        bad = int(np.count_nonzero(words[:, 1] != rowshard_tag(step)))
+        raise RuntimeError(f"{bad} of {d} logits words do not carry step {step}'s tag")
+    return words[:, 0].copy().view(np.float32)
+
+
 class PeerShardedLinear:
     """Row-sharded layer whose all-gather is fused into the GEMV.
 
     Every rank allocates one peer block (CUDA IPC, no multicast; layout in
     include/mli_gemv.h, mli_rowshard_block_bytes):
-        [0, 64)    uint64 row counters, one per source rank (raised over NVLink)
         [128, 132) uint32 step counter (local)
         [192, 196) uint32 finished-CTA count of a fused step (local)
-        [196, 200) uint32 rows produced by a fused step's CTAs (local)
-        [256, ...) fp32 logits [2][d] (the half is the step's parity), then the
-                   CTAs' (max, first index) partials
+        [256, ...) logits words uint64 [2][d] ({fp32 value, step tag}; the half
+                   is the step's parity), then the CTAs' tagged (max, first
+                   index) partial words
     and opens every other rank's block.  A step is one launch on the current
-    stream, mli_gemv_rowshard_argmax: this rank's rows stored into every rank's
-    logits with the CTAs' partials; the launch's last CTA raises every rank's
-    counter for this rank once (one system-scope fence per launch), waits
-    (bounded) for all ranks' rows, takes the argmax from the partials and
-    advances the step.  (forward(fused=False) runs the same as two launches,
-    mli_gemv_rowshard + mli_rowshard_wait_argmax.)  The handles travel through torch.distributed (any
-    backend); no collective runs on the data path.  world == 1 needs no
+    stream, mli_gemv_rowshard_argmax: this rank's rows, tagged with the step,
+    stored into every rank's logits, each CTA's partial word into every rank's
+    block; the launch's last CTA polls (bounded) all ranks' partial words of
+    this step, takes the argmax and advances the step.  Nothing waits for a
+    fence: each word tells by its tag whether it belongs to this step.
+    (forward(fused=False) runs the same as two launches, mli_gemv_rowshard +
+    mli_rowshard_wait_argmax.)  The handles travel through torch.distributed
+    (any backend); no collective runs on the data path.  world == 1 needs no
     process group (the single GPU then gets the fused GEMV + argmax).
     """
 
@@ -156,7 +180,6 @@ class PeerShardedLinear:
             bases.append(ptr.value)
         P = ctypes.c_void_p
         self._peer_logits = (P * world)(*[b + self.HEADER for b in bases])
-        self._peer_rows = (P * world)(*bases)
         self._shard_rows = (ctypes.c_int * world)(*[row_shard(d, world, r).rows for r in range(world)])
         self.base = self._own.value
         self.out = torch.zeros((), dtype=torch.int64, device=w_q.device)
@@ -166,8 +189,13 @@ class PeerShardedLinear:
             dist.barrier(group=group)  # every rank has opened every block before any step
 
     def logits(self, half: int):
-        """fp32 view of this rank's logits half (0 or 1) -- a device pointer wrapper."""
-        return self.base + self.HEADER + half * self.d * 4
+        """Device address of this rank's logits words of one half (0 or 1)."""
+        return self.base + self.HEADER + half * self.d * 8
+
+    def read_logits(self, step: int):
+        """fp32 logits of step `step` (0-based) from this rank's block; every
+        rank must have finished that step."""
+        return read_tagged_logits(self.base + self.HEADER, self.d, step & 1, step)
 
     def forward(self, x, stream=None, fused: bool = True):
         """One step: this rank's rows to every rank, then the argmax into
@@ -179,16 +207,15 @@ class PeerShardedLinear:
         st = torch.cuda.current_stream().cuda_stream if stream is None else stream
         if fused:
             check(self.lib.mli_gemv_rowshard_argmax(
-                self.form_code, self._peer_logits, self._peer_rows, self.base, x.data_ptr(),
-                self.w_q.data_ptr(), self.w_s.data_ptr(), self.n, self.shard.rows, self.shard.r0, self.d,
-                self.rank, self.world, 64, self._shard_rows, self.out.data_ptr(), self.timeout_us, st),
-                "mli_gemv_rowshard_argmax")
+                self.form_code, self._peer_logits, self.base, x.data_ptr(), self.w_q.data_ptr(),
+                self.w_s.data_ptr(), self.n, self.shard.rows, self.shard.r0, self.d, self.rank, self.world, 64,
+                self._shard_rows, self.out.data_ptr(), self.timeout_us, st), "mli_gemv_rowshard_argmax")
         else:
-            check(self.lib.mli_gemv_rowshard(self.form_code, self._peer_logits, self._peer_rows,
-                                             self.base + 128, x.data_ptr(), self.w_q.data_ptr(),
-                                             self.w_s.data_ptr(), self.n, self.shard.rows, self.shard.r0,
-                                             self.d, self.rank, self.world, 64, st), "mli_gemv_rowshard")
-            check(self.lib.mli_rowshard_wait_argmax(self.form_code, self.n, self.base + self.HEADER, self.base,
+            check(self.lib.mli_gemv_rowshard(self.form_code, self._peer_logits, self.base + 128, x.data_ptr(),
+                                             self.w_q.data_ptr(), self.w_s.data_ptr(), self.n, self.shard.rows,
+                                             self.shard.r0, self.d, self.rank, self.world, 64, st),
+                  "mli_gemv_rowshard")
+            check(self.lib.mli_rowshard_wait_argmax(self.form_code, self.n, self.base + self.HEADER,
                                                     self.base + 128, self._shard_rows, self.world, self.d,
                                                     self.out.data_ptr(), self.timeout_us, st),
                   "mli_rowshard_wait_argmax")

@@ -79,8 +79,9 @@ def test_launch_flags_roundtrip():
     lambda l: l.mli_quantize_activation_rows(8, 8, 8, 0, 64, None),
     lambda l: l.mli_gemm_w8a8(8, 8, 8, 8, 8, 0, 64, 8, 64, None, 0, None),
     lambda l: l.mli_gemm_w8a8_cuda_core(8, 8, 8, 8, 8, 4, 100, 8, 64, None),
-    lambda l: l.mli_rowshard_wait_argmax(0, 2048, 8, 8, 8, None, 1, 64, 8, 100, None),
-    lambda l: l.mli_gemv_rowshard_argmax(0, None, None, 8, 8, 8, 8, 2048, 64, 0, 64, 0, 1, 64, None, 8, 100, None),
+    lambda l: l.mli_rowshard_wait_argmax(0, 2048, 8, 8, None, 1, 64, 8, 100, None),
+    lambda l: l.mli_gemv_rowshard_argmax(0, None, 8, 8, 8, 8, 2048, 64, 0, 64, 0, 1, 64, None, 8, 100, None),
+    lambda l: l.mli_gemv_rowshard(0, None, 8, 8, 8, 8, 2048, 64, 0, 64, 0, 1, 64, None),
     lambda l: l.mli_argmax(None, 8, 8, None),
     lambda l: l.mli_gemv_f32(None, 8, 8, 64, 8, None),
     lambda l: l.mli_gemv_f32(8, 8, 8, 0, 8, None),

@@ -10,6 +10,7 @@ import pytest
 from oracle import oracle as orc
 from minillama_infra_b200 import ops, synth
 from minillama_infra_b200._lib import check, lib
+from minillama_infra_b200.shard import read_tagged_logits
 
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
@@ -70,14 +71,13 @@ class Block:
         self.base = self.ptr.value
         self.d = d
 
-    def logits(self, half):
-        return self.base + HEADER + half * self.d * 4
+    def logits(self, half=0):
+        """Device address of the logits words (8 bytes per row) of one half."""
+        return self.base + HEADER + half * self.d * 8
 
-    def read_logits(self, half):
-        torch.cuda.synchronize()
-        t = torch.empty(self.d, dtype=torch.float32, device=dev())
-        ops.copy_from_ptr(t, self.logits(half), self.d * 4)
-        return t.cpu().numpy()
+    def read_logits(self, step):
+        """fp32 logits of step `step`, every word checked for the step's tag."""
+        return read_tagged_logits(self.logits(0), self.d, step & 1, step)
 
     def free(self):
         lib().mli_peer_free(self.base)
@@ -96,19 +96,18 @@ def test_rowshard_single_rank_loopback(form):
     b = Block(d)
     P = ctypes.c_void_p
     logits_arr = (P * 1)(b.logits(0))
-    rows_arr = (P * 1)(b.base)
     shard_rows = (ctypes.c_int * 1)(d)
     out = torch.zeros((), dtype=torch.int64, device=dev())
     code = 0 if form == "w8a32" else 2
     try:
         for step in range(3):  # both halves, then the first again
-            check(lib().mli_gemv_rowshard(code, logits_arr, rows_arr, b.base + 128, x.data_ptr(),
+            check(lib().mli_gemv_rowshard(code, logits_arr, b.base + 128, x.data_ptr(),
                                           w_q.data_ptr(), w_s.data_ptr(), n, d, 0, d, 0, 1, 64, None),
                   "rowshard")
-            check(lib().mli_rowshard_wait_argmax(code, n, b.logits(0), b.base, b.base + 128, shard_rows, 1, d,
+            check(lib().mli_rowshard_wait_argmax(code, n, b.logits(0), b.base + 128, shard_rows, 1, d,
                                                  out.data_ptr(), 1_000_000, None), "wait")
             torch.cuda.synchronize()
-            got = b.read_logits(step & 1)
+            got = b.read_logits(step)
             assert np.array_equal(got.view(np.uint32), ref.cpu().numpy().view(np.uint32))
             assert int(out.item()) == int(torch.argmax(ref).item())
         assert ops.device_error() == 0
@@ -132,9 +131,9 @@ def test_rowshard_argmax_first_max_across_ctas():
     out = torch.zeros((), dtype=torch.int64, device=dev())
     try:
         for step in range(2):
-            check(lib().mli_gemv_rowshard(0, (P * 1)(b.logits(0)), (P * 1)(b.base), b.base + 128, tx.data_ptr(),
+            check(lib().mli_gemv_rowshard(0, (P * 1)(b.logits(0)), b.base + 128, tx.data_ptr(),
                                           tw.data_ptr(), ts.data_ptr(), n, d, 0, d, 0, 1, 64, None), "rowshard")
-            check(lib().mli_rowshard_wait_argmax(0, n, b.logits(0), b.base, b.base + 128, (ctypes.c_int * 1)(d), 1,
+            check(lib().mli_rowshard_wait_argmax(0, n, b.logits(0), b.base + 128, (ctypes.c_int * 1)(d), 1,
                                                  d, out.data_ptr(), 1_000_000, None), "wait")
             torch.cuda.synchronize()
             assert int(out.item()) == 100
@@ -148,7 +147,7 @@ def test_rowshard_wait_gives_up_when_rows_never_arrive():
     out = torch.zeros((), dtype=torch.int64, device=dev())
     shard_rows = (ctypes.c_int * 2)(512, 512)
     try:
-        check(lib().mli_rowshard_wait_argmax(0, 2048, b.logits(0), b.base, b.base + 128, shard_rows, 2, d,
+        check(lib().mli_rowshard_wait_argmax(0, 2048, b.logits(0), b.base + 128, shard_rows, 2, d,
                                              out.data_ptr(), 100_000, None), "wait")
         torch.cuda.synchronize()
         assert int(out.item()) == -1
@@ -178,11 +177,11 @@ def test_rowshard_fused_argmax_single_rank(form):
     code = 0 if form == "w8a32" else 2
     try:
         for step in range(3):
-            check(lib().mli_gemv_rowshard_argmax(code, (P * 1)(b.logits(0)), (P * 1)(b.base), b.base, x.data_ptr(),
+            check(lib().mli_gemv_rowshard_argmax(code, (P * 1)(b.logits(0)), b.base, x.data_ptr(),
                                                  w_q.data_ptr(), w_s.data_ptr(), n, d, 0, d, 0, 1, 64,
                                                  (ctypes.c_int * 1)(d), out.data_ptr(), 1_000_000, None), "fused")
             torch.cuda.synchronize()
-            got = b.read_logits(step & 1)
+            got = b.read_logits(step)
             assert np.array_equal(got.view(np.uint32), ref.cpu().numpy().view(np.uint32))
             assert int(out.item()) == int(torch.argmax(ref).item())
         assert ops.device_error() == 0
@@ -200,7 +199,7 @@ def test_rowshard_fused_gives_up_when_a_rank_never_arrives():
     P = ctypes.c_void_p
     out = torch.zeros((), dtype=torch.int64, device=dev())
     try:
-        check(lib().mli_gemv_rowshard_argmax(0, (P * 2)(b0.logits(0), b1.logits(0)), (P * 2)(b0.base, b1.base),
+        check(lib().mli_gemv_rowshard_argmax(0, (P * 2)(b0.logits(0), b1.logits(0)),
                                              b0.base, x.data_ptr(), w_q.data_ptr(), w_s.data_ptr(), n, 512, 0, d,
                                              0, 2, 64, (ctypes.c_int * 2)(512, 512), out.data_ptr(), 100_000,
                                              None), "fused")

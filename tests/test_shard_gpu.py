@@ -51,13 +51,15 @@ def _worker(rank, world, port, d, n, form, q, fused=False):
             lin = PeerShardedLinear(w_q[sh.r0:sh.r1].clone(), w_s[sh.r0:sh.r1].clone(), d, n, rank, world,
                                     form=form)
             same, arg = True, True
+            full_bits = full.cpu().numpy().view("uint32")
             for step in range(5):  # both logits halves, several times
                 out = lin.forward(x)
                 torch.cuda.synchronize()
-                got = torch.empty(d, dtype=torch.float32, device=dev)
-                ops.copy_from_ptr(got, lin.logits(step & 1), d * 4)
-                same = same and bool(torch.equal(got.view(torch.int32), full.view(torch.int32)))
+                dist.barrier()  # every rank's words of this step have landed
+                got = lin.read_logits(step)  # also checks every word's step tag
+                same = same and bool((got.view("uint32") == full_bits).all())
                 arg = arg and int(out.item()) == want
+                dist.barrier()
             lin.close()
         q.put((rank, same, arg, ops.device_error()))
         dist.barrier()
