@@ -507,7 +507,29 @@ def time_graph(g, steps, warmup, stream, world, device, sampler=None):
 # ---------------------------------------------------------------------------
 # batched W8A8 on the Llama-3.2-3B projections (tensor cores)
 # ---------------------------------------------------------------------------
-def gemm3b_measure(args, device, rank, world, m, modes=("group", "per_call", "cuda_core"), sampler=None):
+def int8_peak_measure(device, iters=4096):
+    """This GPU's int8 tensor-core roof: one CTA per SM issuing back-to-back
+    kind::i8 MMAs (M = 128, N = 256, K = 32) on resident operands, no loads,
+    no epilogue (mli_debug_int8_mma_peak), timed with CUDA events."""
+    from minillama_infra_b200._lib import check, lib
+
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    stream = torch.cuda.current_stream()
+    for _ in range(3):
+        check(lib().mli_debug_int8_mma_peak(256, iters, sms, stream.cuda_stream), "int8 peak")
+    torch.cuda.synchronize()
+    ms = timed(lambda: check(lib().mli_debug_int8_mma_peak(256, iters, sms, stream.cuda_stream), "int8 peak"),
+               5, stream)
+    ops_ = sms * iters * 4 * 2 * 128 * 256 * 32
+    if ops.device_error() != 0:
+        raise RuntimeError("the int8 peak kernel gave up on its wait")
+    return {"TOPS": round(ops_ / (ms * 1e-3) / 1e12, 1), "ms": round(ms, 4), "ctas": sms,
+            "mma": "tcgen05.mma.cta_group::1.kind::i8 M=128 N=256 K=32, operands in shared memory, one "
+                   "issuing thread per SM, no loads, no epilogue"}
+
+
+def gemm3b_measure(args, device, rank, world, m, modes=("group", "per_call", "cuda_core"), sampler=None,
+                   int8_peak=None):
     """The seven Llama-3.2-3B projections at m tokens, 4 layers with fresh
     seeds rotated so that no step finds its weights in L2.  Each rank runs its
     own batch (data parallel).  Returns ms per layer per mode and the check of
@@ -565,6 +587,8 @@ def gemm3b_measure(args, device, rank, world, m, modes=("group", "per_call", "cu
         "GB/s": round(world * bytes_layer / (ms * 1e-3) / 1e9, 1),
         "frac_of_hbm_peak_per_gpu": round(bytes_layer / (ms * 1e-3) / 1e9 / peak, 4),
         "frac_of_int8_dense_datasheet_4500_TOPS": round(ops_layer / (ms * 1e-3) / 1e12 / 4500, 4),
+        "frac_of_int8_measured_peak": (round(ops_layer / (ms * 1e-3) / 1e12 / int8_peak, 4)
+                                       if int8_peak else None),
         "bytes_per_layer": bytes_layer, "ops_per_layer": ops_layer,
         "check": {"max_abs_rel_vs_oracle_layer0_every_token": worst, "tolerance": 1e-6},
     }
@@ -1136,8 +1160,11 @@ def main():
         if "ffn" in extras:
             line["ffn_rowshard"] = {f: ffn_measure(args, device, rank, world, f) for f in ("w8a32", "w8a8")}
         if "gemm3b" in extras:
-            line["gemm3b"] = {f"m{m}": gemm3b_measure(args, device, rank, world, m, modes=("group", "per_call"))
+            peak = int8_peak_measure(device)
+            line["gemm3b"] = {f"m{m}": gemm3b_measure(args, device, rank, world, m, modes=("group", "per_call"),
+                                                      int8_peak=peak["TOPS"])
                               for m in (16, 64, 256)}
+            line["gemm3b"]["int8_tensor_peak_measured"] = peak
         if "decode" in extras and world == 1:
             line["decode_e2e"] = decode_e2e_measure(device)
         if world == 1 and not args.no_cpu_baseline:
@@ -1183,7 +1210,9 @@ def run_single_workload(args, device, rank, world, sampler):
         scaling = "strong"
         extra = {"ffn": r, "gpu_launches": args.ffn_steps * 16 * 2}
     else:
-        r = gemm3b_measure(args, device, rank, world, args.m, sampler=sampler)
+        peak = int8_peak_measure(device)
+        r = gemm3b_measure(args, device, rank, world, args.m, sampler=sampler, int8_peak=peak["TOPS"])
+        r["int8_tensor_peak_measured"] = peak
         ms = r["ms_per_layer"]
         config = {"workload": f"llama-3.2-3b per-layer projections (7 GEMMs) at M={args.m} tokens, W8A8, tcgen05 "
                               "kind::i8 path, one grouped launch per layer", "m": args.m,

@@ -257,6 +257,14 @@ int mli_gemm_w8a8_group(const mli_gemm_op* ops, int count, int m, int group_size
  * MLI_ERR_UNSUPPORTED for shapes outside the tensor-core path. */
 int mli_debug_plan_gemm(int m, int n, int d, size_t workspace_bytes, int* out);
 
+/* Diagnostic: `ctas` CTAs each issue `iters` x 4 back-to-back tcgen05
+ * kind::i8 MMAs (M = 128, N = n in {64, 128, 256}, K = 32; 2 * 128 * n * 32
+ * integer ops each) on operands resident in shared memory, from one thread,
+ * with no loads and no epilogue: timed by the caller, it gives this GPU's
+ * int8 tensor-core roof for the batched path's utilisation.  No reference
+ * counterpart. */
+int mli_debug_int8_mma_peak(int n, int iters, int ctas, void* stream);
+
 /* ---- row-sharded linear layer across GPUs (one process per GPU) --------- */
 
 /* Peer buffers: device memory this process allocates and exports through a

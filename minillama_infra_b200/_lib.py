@@ -79,6 +79,7 @@ SIGNATURES = {
     "mli_chain_destroy": (_I, [_P]),
     "mli_debug_plan_chain": (_I, [_OPS, _I, _I, _I, ctypes.POINTER(_I)]),
     "mli_debug_plan_gemm": (_I, [_I, _I, _I, ctypes.c_size_t, ctypes.POINTER(_I)]),
+    "mli_debug_int8_mma_peak": (_I, [_I, _I, _I, _P]),
     "mli_gemm_w8a8_group": (_I, [ctypes.POINTER(GemmOp), _I, _I, _I, _P]),
 }
 

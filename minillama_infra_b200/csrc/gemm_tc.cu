@@ -204,6 +204,16 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[kCols
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+// The same wait, tied to the 16 registers of the load it completes: their
+// uses cannot be scheduled before it.
+__device__ __forceinline__ void tmem_wait_ld16(uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
+                 "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]),
+                 "+r"(r[14]), "+r"(r[15])
+               :
+               : "memory");
+}
 
 // Accumulator bias: int32 accumulation onto the bits of 1.5 * 2^23 leaves the
 // bits of the float 1.5 * 2^23 + I for any |I| < 2^22 (a group dot is at most
@@ -580,21 +590,36 @@ __device__ __forceinline__ void gemm_tile(const CUtensorMap* map_w, const CUtens
         if (ok && !mbar_wait_bounded(&sm.acc_full[pb], (c / kPairs) & 1, kWaitLimitNs)) ok = false;
         if (!ok) continue;
         tmem_fence_after();
-#pragma unroll 1
-        for (int h = 0; h < 2; ++h) {
-          const uint32_t taddr = tl + static_cast<uint32_t>((buf + h) * kBN);
-          const float w = wrow[h];
-          const uint64_t w2 = f2_pack(__float_as_uint(w), __float_as_uint(w));
+        // The pair's two groups as one software pipeline of kLd-column
+        // loads: load q + 1 is issued as soon as load q has landed, so its
+        // latency overlaps q's arithmetic (one exposed load per pair instead
+        // of one per kLd columns).
+        {
+          static_assert(kLd == 16, "pipelined loads of 16 columns");
+          constexpr int kL = kCols / kLd;  // loads per group
+          const uint32_t base = tl + static_cast<uint32_t>(buf * kBN);
+          const uint64_t w2a = f2_pack(__float_as_uint(wrow[0]), __float_as_uint(wrow[0]));
+          const uint64_t w2b = f2_pack(__float_as_uint(wrow[1]), __float_as_uint(wrow[1]));
+          uint32_t ra[kLd], rb[kLd];
+          tmem_ld16(base, ra);
 #pragma unroll
-          for (int q = 0; q < kCols / kLd; ++q) {
-            uint32_t r[kLd];
-            tmem_ld16(taddr + kLd * q, r);
-            tmem_wait_ld();
+          for (int q = 0; q < 2 * kL; ++q) {
+            uint32_t(&cur)[kLd] = (q & 1) ? rb : ra;
+            uint32_t(&nxt)[kLd] = (q & 1) ? ra : rb;
+            tmem_wait_ld16(cur);
+            if (q + 1 < 2 * kL) {
+              const int q1 = q + 1;
+              tmem_ld16(base + static_cast<uint32_t>((q1 / kL) * kBN + kLd * (q1 % kL)), nxt);
+            }
+            const uint64_t w2 = q < kL ? w2a : w2b;
+            const int col = (q % kL) * (kLd / 2);
 #pragma unroll
             for (int j = 0; j < kLd / 2; ++j)
-              acc[q * (kLd / 2) + j] = f2_unbias_fma(f2_pack(r[2 * j], r[2 * j + 1]), bias2, w2, acc[q * (kLd / 2) + j]);
+              acc[col + j] = f2_unbias_fma(f2_pack(cur[2 * j], cur[2 * j + 1]), bias2, w2, acc[col + j]);
           }
-          tmem_fill_bias<kCols>(taddr);  // ready for the buffer's next use
+          // both buffers ready for their next use
+          tmem_fill_bias<kCols>(base);
+          tmem_fill_bias<kCols>(base + kBN);
         }
         // both buffers go back to the MMA warp once their refill has completed
         tmem_wait_st();
@@ -947,6 +972,59 @@ cudaError_t launch_group_bn(const GroupArgs& g, int grid, int cluster, cudaStrea
                           stream, true, static_cast<unsigned>(cluster), g);
 }
 
+// ---------------------------------------------------------------------------
+// The int8 tensor-core roof of this GPU (mli_debug_int8_mma_peak): every CTA
+// issues back-to-back kind::i8 MMAs (M = 128, N = kN, K = 32) from one thread
+// on operands resident in shared memory (zeros: the values do not change the
+// rate), alternating between two accumulators, with no loads and no
+// epilogue -- the denominator the batched path's tensor utilisation is
+// measured against.
+// ---------------------------------------------------------------------------
+template <int kN>
+__global__ void __launch_bounds__(128, 1) mma_peak_kernel(int iters, unsigned int* err) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~static_cast<uintptr_t>(1023u));
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tmem_base;
+  constexpr uint32_t kBytes = kStageA + kN * kChunk;
+  for (uint32_t i = threadIdx.x * 16u; i < kBytes; i += 128u * 16u)
+    *reinterpret_cast<uint4*>(base + i) = make_uint4(0, 0, 0, 0);
+  fence_proxy_async_smem();  // the zeros are visible to the tensor cores
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  constexpr uint32_t kCols = 2 * kN;
+  if ((threadIdx.x >> 5) == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
+                 "r"(kCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tmem_fence_before();
+  __syncthreads();
+  tmem_fence_after();
+  const uint32_t tmem = tmem_base;
+  if (threadIdx.x == 0) {
+    const uint32_t idesc = i8_idesc(kN);
+    const uint64_t a_desc = sw128_desc(smem_u32(base));
+    const uint64_t b_desc = sw128_desc(smem_u32(base + kStageA));
+    for (int it = 0; it < iters; ++it) {
+      const uint32_t d = tmem + static_cast<uint32_t>((it & 1) * kN);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) mma_i8(d, a_desc + 2 * kk, b_desc + 2 * kk, idesc, true);
+    }
+    mma_commit(&bar);
+    if (!mbar_wait_bounded(&bar, 0, kWaitLimitNs) && err) atomicCAS(err, 0u, static_cast<unsigned>(kDevMmaTimeout));
+  }
+  tmem_fence_before();
+  __syncthreads();
+  tmem_fence_after();
+  if ((threadIdx.x >> 5) == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
+}
+
 }  // namespace tc
 
 size_t gemm_tc_workspace_bytes(int m, int n, int d, int sm_count) {
@@ -1088,6 +1166,28 @@ extern "C" int mli_gemm_w8a8_group(const mli_gemm_op* ops, int count, int m, int
     if (ops[i].n % tc::kChunk != 0 || !aligned(ops[i].xq, 16) || !aligned(ops[i].w_q, 16))
       return set_status(MLI_ERR_UNSUPPORTED);
   return gemm_w8a8_tc_group(ops, count, m, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int mli_debug_int8_mma_peak(int n, int iters, int ctas, void* stream) {
+  using namespace mli;
+  if ((n != 64 && n != 128 && n != 256) || iters <= 0 || ctas <= 0) return set_status(MLI_ERR_INVALID_ARG);
+  // more than half of an SM's shared memory: one CTA per SM, so no CTA waits
+  // for another's tensor memory
+  const size_t need = 1024u + tc::kStageA + static_cast<size_t>(n) * tc::kChunk;
+  const size_t smem = need > 120u * 1024u ? need : 120u * 1024u;
+  const void* fn = n == 256 ? reinterpret_cast<const void*>(tc::mma_peak_kernel<256>)
+                   : n == 128 ? reinterpret_cast<const void*>(tc::mma_peak_kernel<128>)
+                              : reinterpret_cast<const void*>(tc::mma_peak_kernel<64>);
+  cudaError_t e = ensure_dynamic_smem(fn, smem);
+  if (e != cudaSuccess) return check_cuda(e);
+  unsigned int* err = device_error_word();
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (n) {
+    case 256: e = launch(tc::mma_peak_kernel<256>, dim3(ctas), dim3(128), smem, st, false, iters, err); break;
+    case 128: e = launch(tc::mma_peak_kernel<128>, dim3(ctas), dim3(128), smem, st, false, iters, err); break;
+    default: e = launch(tc::mma_peak_kernel<64>, dim3(ctas), dim3(128), smem, st, false, iters, err); break;
+  }
+  return check_cuda(e);
 }
 
 extern "C" int mli_debug_plan_gemm(int m, int n, int d, size_t workspace_bytes, int* out) {
