@@ -55,6 +55,12 @@ enum mli_status_code {
  * sums in the workspace and a second kernel), and one without a workspace does
  * not split K. */
 #define MLI_LAUNCH_NO_CLUSTER 4u
+/* Batched W8A8 with more than 64 tokens: by default a problem of enough
+ * 128 x 128 output tiles to keep the SMs evenly busy (at least one per SM,
+ * the busiest SM at most 1.3 x the ideal share) runs as a persistent kernel,
+ * one CTA per SM walking whole tiles (no K split); with this bit it takes the
+ * split-K kernels. */
+#define MLI_LAUNCH_NO_PERSISTENT 8u
 
 /* ---- library state ------------------------------------------------------ */
 const char* mli_status_string(int status);
@@ -67,7 +73,9 @@ void mli_set_launch_flags(unsigned flags);
  * kernel gave up on a bounded wait since the last call; otherwise the first
  * code recorded: 1 a weight stage never landed in shared memory, 2 the
  * tensor-core pipeline stalled, 3 a rank's rows of a row-sharded layer never
- * arrived, 4 a chained GEMV's inputs were never completed. */
+ * arrived, 4 a chained GEMV's inputs were never completed, 5 the batched
+ * tensor-core GEMM met a finite group scale of 2^38 or more (its outputs are
+ * not written). */
 int mli_device_error(unsigned* code_out);
 
 /* ---- batch-1 linear ops (the reference's matmul launchers) ------------- */
@@ -256,6 +264,12 @@ int mli_gemm_w8a8_group(const mli_gemm_op* ops, int count, int m, int group_size
  * (1: none), 1 when the splits sum through the workspace.  Returns
  * MLI_ERR_UNSUPPORTED for shapes outside the tensor-core path. */
 int mli_debug_plan_gemm(int m, int n, int d, size_t workspace_bytes, int* out);
+/* Persistent plan of mli_gemm_w8a8_group (and, with count 1, of
+ * mli_gemm_w8a8) on the current device (no launch).  out[5] = 1 when the
+ * persistent kernel runs the call, CTAs, output tiles, the busiest CTA's
+ * cost and the total cost (a tile costs its K chunks of 128 plus one).  The
+ * pointers of `ops` are looked at, not dereferenced. */
+int mli_debug_plan_gemm_group(const mli_gemm_op* ops, int count, int m, int* out);
 
 /* Diagnostic: `ctas` CTAs each issue `iters` x 4 back-to-back tcgen05
  * kind::i8 MMAs (M = 128, N = n in {64, 128, 256}, K = 32; 2 * 128 * n * 32

@@ -22,6 +22,7 @@ MLI_ERR_CUDA = 3
 MLI_ERR_DEVICE = 4
 MLI_LAUNCH_PDL = 1
 MLI_LAUNCH_NO_CLUSTER = 4
+MLI_LAUNCH_NO_PERSISTENT = 8
 
 # Every symbol include/mli_gemv.h declares with C linkage, with its ctypes
 # signature (device pointers and streams travel as void*).
@@ -79,6 +80,7 @@ SIGNATURES = {
     "mli_chain_destroy": (_I, [_P]),
     "mli_debug_plan_chain": (_I, [_OPS, _I, _I, _I, ctypes.POINTER(_I)]),
     "mli_debug_plan_gemm": (_I, [_I, _I, _I, ctypes.c_size_t, ctypes.POINTER(_I)]),
+    "mli_debug_plan_gemm_group": (_I, [ctypes.POINTER(GemmOp), _I, _I, ctypes.POINTER(_I)]),
     "mli_debug_int8_mma_peak": (_I, [_I, _I, _I, _P]),
     "mli_gemm_w8a8_group": (_I, [ctypes.POINTER(GemmOp), _I, _I, _I, _P]),
 }

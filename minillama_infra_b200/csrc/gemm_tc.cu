@@ -73,6 +73,15 @@ struct Shape {
   // wide tiles keep 128 fp32 sums per epilogue thread: registers move from
   // the producer warpgroup to the epilogue warpgroups
   static constexpr bool kSplitRegs = kBN >= 64;
+  // 128-token tiles: the accumulator offset is written by one extra MMA per
+  // group (a constant unsigned tile, see kMmaBias* below) instead of
+  // tensor-memory stores from the epilogue, and every 64-column group is a
+  // unit of its own, so that each epilogue warpgroup has two buffers (the
+  // MMAs fill one while it reads the other).  Narrower tiles refill by
+  // stores (one store of 16 columns per group) and hand over a chunk's two
+  // groups as one unit.
+  static constexpr bool kMmaBias = kBN >= 128;
+  static constexpr int kUnitGroups = kMmaBias ? 1 : 2;
 };
 // Registers per thread after the setmaxnreg split: the producer warpgroup
 // gives up what its loops do not need, the epilogue warpgroups take it (the
@@ -83,7 +92,7 @@ constexpr int kRegsProducer = 88;
 constexpr int kRegsEpilogue = 208;
 constexpr int kRegsBlock = 128 * (kRegsProducer + 2 * kRegsEpilogue);
 constexpr int kMaxAccBufs = 8;
-constexpr int kMaxAccPairs = kMaxAccBufs / 2;  // a chunk's two groups fill one pair of buffers
+constexpr int kMaxUnits = 4;  // 4 single-group units at 128 tokens, 4 chunk pairs of 8 buffers below
 
 // Accumulator buffers per tile width: as many as tensor memory holds (512
 // columns), at most 8, so the MMAs run up to that many groups ahead of the
@@ -136,6 +145,21 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
 __device__ __forceinline__ uint32_t i8_idesc(int bn) {
   return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(bn >> 3) << 17) |
          (static_cast<uint32_t>(kBM >> 4) << 24);
+}
+// The same with unsigned int8 A and B (the accumulator-offset MMA).
+__device__ __forceinline__ uint32_t u8_idesc(int bn) {
+  return (2u << 4) | (static_cast<uint32_t>(bn >> 3) << 17) | (static_cast<uint32_t>(kBM >> 4) << 24);
+}
+// K-major operand of one 32-byte K step in the 32-byte-swizzle layout: rows of
+// 32 bytes, 8-row atoms of 256 bytes; 128 rows span 4 KB.
+__device__ __forceinline__ uint64_t sw32_desc(uint32_t saddr) {
+  uint64_t desc = 0;
+  desc |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);       // start address
+  desc |= static_cast<uint64_t>(1u) << 16;                      // leading offset (unused)
+  desc |= static_cast<uint64_t>((256u >> 4) & 0x3FFFu) << 32;   // stride offset: 8 rows
+  desc |= static_cast<uint64_t>(1u) << 46;                      // descriptor version
+  desc |= static_cast<uint64_t>(6u) << 61;                      // 32-byte swizzle
+  return desc;
 }
 
 __device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t a_desc, uint64_t b_desc,
@@ -221,6 +245,24 @@ __device__ __forceinline__ void tmem_wait_ld16(uint32_t (&r)[16]) {
 // exactly -- no int->float conversion instruction in the epilogue.
 constexpr uint32_t kAccBias = 0x4B400000u;
 constexpr float kAccBiasF = 12582912.0f;  // 1.5 * 2^23
+
+// Offset written by an MMA (128-token tiles).  One K = 32 step of unsigned
+// int8 A = B = a constant tile whose every 16-byte chunk holds kMmaBiasChunk
+// (bytes 255 x 8, 63, 10, 3, 3, 1, 0, 0, 0: squares summing to 2^19) leaves
+// V0 = 2 * 2^19 = 2^20 in every accumulator, whatever the swizzle does to the
+// chunks.  The group dot then leaves bits V0 + I, 0 < V0 + I < 2^23 for any
+// int8 operands (|I| <= 2^20, I > -2^20), which read as a float are the
+// subnormal (V0 + I) * 2^-149: one exact subtraction of 2^-129 gives
+// I * 2^-149.  The group scale enters as ws * 2^90 (exact), so the fused
+// multiply-add adds I * ws * 2^-59 with the rounding of I * ws, and the tile
+// is scaled by 2^59 (exact) before it leaves the registers.  Exact for group
+// scales in [2^-67, 2^38); a finite scale of 2^38 or more is refused through
+// the error word.
+constexpr uint32_t kMmaBiasBits = 1u << 20;        // the float 2^-129
+constexpr uint32_t kMmaScaleIn = 0x6C800000u;      // 2^90
+constexpr uint32_t kMmaScaleOut = 0x5D000000u;     // 2^59
+constexpr uint32_t kBiasTileBytes = 4096;          // 128 rows x 32 bytes
+__device__ __forceinline__ uint4 mma_bias_chunk() { return make_uint4(0xFFFFFFFFu, 0xFFFFFFFFu, 0x03030A3Fu, 0x1u); }
 
 // Fills this warp's 32 lanes x kCols columns at taddr with the bias: a store's
 // source is as many consecutive registers as it has columns, so 16 columns
@@ -321,8 +363,9 @@ struct Smem {
   uint32_t stage;
   uint64_t* full;
   uint64_t* empty;
-  uint64_t* acc_full;    // per pair of accumulator buffers
+  uint64_t* acc_full;    // per unit of accumulator buffers
   uint64_t* acc_empty;
+  unsigned char* bias;   // the offset MMA's constant operand (128-token tiles)
   uint32_t* tmem_base;
   int* flag;
   float* ws;             // [kBM][kWsStride] group scales of the current window
@@ -341,12 +384,15 @@ constexpr uint32_t kBarBytes = 512u;
 
 __host__ __device__ constexpr uint32_t rings_bytes(int bn) { return stages(bn) * stage_bytes(bn); }
 __host__ __device__ constexpr uint32_t smem_bytes(int bn) {
-  return 1024u /* alignment slack */ + rings_bytes(bn) + kBarBytes + kWsBytes + 512u /* xs */;
+  return 1024u /* alignment slack */ + rings_bytes(bn) + kBiasTileBytes + kBarBytes + kWsBytes + 512u /* xs */;
 }
 static_assert(smem_bytes(128) <= 232448 && smem_bytes(64) <= 232448 && smem_bytes(32) <= 232448 &&
                   smem_bytes(16) <= 232448,
               "shared memory per block");
-static_assert((2 * kMaxStages + 2 * kMaxAccPairs) * 8 + 8 <= kBarBytes, "barrier area");
+static_assert((2 * kMaxStages + 2 * kMaxUnits) * 8 + 8 <= kBarBytes, "barrier area");
+static_assert(stage_bytes(128) % 1024 == 0 && stage_bytes(64) % 1024 == 0 && stage_bytes(32) % 1024 == 0 &&
+                  stage_bytes(16) % 1024 == 0,
+              "the offset tile after the ring stays 1024-byte aligned");
 // the finished tile ([bn][kBM] fp32) is staged in the ring
 static_assert(128 * kBM * 4 <= rings_bytes(128) && 64 * kBM * 4 <= rings_bytes(64) &&
                   32 * kBM * 4 <= rings_bytes(32) && 16 * kBM * 4 <= rings_bytes(16),
@@ -358,14 +404,15 @@ __device__ __forceinline__ Smem carve(unsigned char* raw, int bn) {
       (reinterpret_cast<uintptr_t>(raw) + 1023u) & ~static_cast<uintptr_t>(1023u));
   s.ring = base;
   s.stage = stage_bytes(bn);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(base + rings_bytes(bn));
+  s.bias = base + rings_bytes(bn);  // 1024-byte aligned: every stage is a multiple of 1 KB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s.bias + kBiasTileBytes);
   s.full = bars;
   s.empty = bars + kMaxStages;
   s.acc_full = bars + 2 * kMaxStages;
-  s.acc_empty = bars + 2 * kMaxStages + kMaxAccPairs;
-  s.tmem_base = reinterpret_cast<uint32_t*>(bars + 2 * kMaxStages + 2 * kMaxAccPairs);
+  s.acc_empty = bars + 2 * kMaxStages + kMaxUnits;
+  s.tmem_base = reinterpret_cast<uint32_t*>(bars + 2 * kMaxStages + 2 * kMaxUnits);
   s.flag = reinterpret_cast<int*>(s.tmem_base + 1);
-  s.ws = reinterpret_cast<float*>(base + rings_bytes(bn) + kBarBytes);
+  s.ws = reinterpret_cast<float*>(s.bias + kBiasTileBytes + kBarBytes);
   s.xs = s.ws + kBM * kWsStride;
   return s;
 }
@@ -426,18 +473,29 @@ __device__ __forceinline__ void gemm_tile(const CUtensorMap* map_w, const CUtens
   constexpr int kAccBufs = acc_bufs(kBN);
   constexpr int kEpiWarps = Shape<kBN>::kEpiWarps;
   constexpr int kS = stages(kBN);
-  constexpr int kPairs = kAccBufs / 2;
+  constexpr bool kMmaBias = Shape<kBN>::kMmaBias;
+  constexpr int kUG = Shape<kBN>::kUnitGroups;    // groups per unit (buffers handed over together)
+  constexpr int kUnits = kAccBufs / kUG;          // 4: even, so a unit always has the same owner
+  constexpr int kUnitsPerChunk = 2 / kUG;
   constexpr bool kTwoIssuers = kBN <= 32;
   constexpr uint32_t kTmemCols = kAccBufs * kBN;  // 128, 256 or 512: a power of two
+  static_assert(kUnits <= kMaxUnits && kUnits % 2 == 0, "units alternate between the two warpgroups");
 
+  if constexpr (kMmaBias) {
+    // the offset MMA's operand: every 16-byte chunk the same (generic-proxy
+    // writes, made visible to the tensor cores before the block barrier)
+    for (uint32_t i = threadIdx.x; i < kBiasTileBytes / 16; i += Shape<kBN>::kThreads)
+      reinterpret_cast<uint4*>(sm.bias)[i] = mma_bias_chunk();
+    fence_proxy_async_smem();
+  }
   if (threadIdx.x == 0) {
     for (int i = 0; i < kS; ++i) {
       mbar_init(&sm.full[i], 1);
       mbar_init(&sm.empty[i], 1);
     }
-    for (int i = 0; i < kPairs; ++i) {
+    for (int i = 0; i < kUnits; ++i) {
       mbar_init(&sm.acc_full[i], 1);
-      mbar_init(&sm.acc_empty[i], 4);  // the four warps of the pair's epilogue warpgroup
+      mbar_init(&sm.acc_empty[i], 4);  // the four warps of the unit's epilogue warpgroup
     }
     *sm.flag = 0;
     fence_barrier_init();
@@ -485,43 +543,54 @@ __device__ __forceinline__ void gemm_tile(const CUtensorMap* map_w, const CUtens
   } else if (warp == 1 || (kTwoIssuers && warp == 2)) {
     // ---------------- MMA issuer(s) ----------------
     // Narrow tiles (kTwoIssuers) have two issuing threads, warp 1 the even
-    // chunks and warp 2 the odd ones: one thread's instruction issue (about
-    // 90 cycles per tcgen05.mma) bounds them.  The chunks of the two use
-    // disjoint accumulator pairs (kPairs is even); a stage passes between
-    // them through its full and empty barriers, and a commit tracks only its
-    // own thread's MMAs.  Wide tiles are bound by the epilogue, where a
-    // second issuer only takes issue slots.  Per chunk: one wait for its
-    // stage, one for its pair of accumulator buffers, four MMAs (two K=32
-    // steps per group), one commit for the pair and one for the stage.
+    // chunks and warp 2 the odd ones: one thread's instruction issue bounds
+    // them.  The chunks of the two use disjoint units (kUnits is even); a
+    // stage passes between them through its full and empty barriers, and a
+    // commit tracks only its own thread's MMAs.  Wide tiles are bound by the
+    // epilogue, where a second issuer only takes issue slots.  Per chunk: one
+    // wait for its stage; per unit one wait for its buffers, per group the
+    // offset MMA (128-token tiles) and two K = 32 steps, one commit; one
+    // commit for the stage.
     if (lane == 0) {
       const uint32_t idesc = i8_idesc(kBN);
+      const uint32_t bias_idesc = u8_idesc(kBN);
+      const uint64_t bias_desc = sw32_desc(smem_u32(sm.bias));
       bool ok = true;
       constexpr int kIssuers = kTwoIssuers ? 2 : 1;
-      for (int c = warp - 1; c < nchunks; c += kIssuers) {
-        const int st = c % kS, pb = c % kPairs;
-        // use u of a pair waits for phase u: the epilogue's bias fill
-        // (phase 0) or its read of use u - 1
-        if (!mbar_wait_bounded(&sm.full[st], (c / kS) & 1, kWaitLimitNs) ||
-            !mbar_wait_bounded(&sm.acc_empty[pb], (c / kPairs) & 1, kWaitLimitNs)) {
+      for (int c = warp - 1; c < nchunks && ok; c += kIssuers) {
+        const int st = c % kS;
+        if (!mbar_wait_bounded(&sm.full[st], (c / kS) & 1, kWaitLimitNs)) {
           ok = false;
           break;
         }
-        tmem_fence_after();
         // descriptor start addresses count 16-byte units: a K step of 32
         // bytes adds 2 (stage bases stay below 2^18 bytes, so no carry)
         const uint64_t a_desc = sw128_desc(smem_u32(stage_a(sm, st)));
         const uint64_t b_desc = sw128_desc(smem_u32(stage_b(sm, st)));
 #pragma unroll
-        for (int g = 0; g < 2; ++g) {
-          const uint32_t d = tmem + static_cast<uint32_t>((2 * pb + g) * kBN);
-#pragma unroll
-          for (int kk = 0; kk < 2; ++kk) {
-            const uint64_t koff = static_cast<uint64_t>(2 * (2 * g + kk));
-            mma_i8(d, a_desc + koff, b_desc + koff, idesc, true);
+        for (int j = 0; j < kUnitsPerChunk; ++j) {
+          const int u = c * kUnitsPerChunk + j, ub = u % kUnits;
+          // use k of a unit waits for phase k: the epilogue's first arrival
+          // (phase 0) or its read of use k - 1
+          if (!mbar_wait_bounded(&sm.acc_empty[ub], (u / kUnits) & 1, kWaitLimitNs)) {
+            ok = false;
+            break;
           }
+          tmem_fence_after();
+#pragma unroll
+          for (int gg = 0; gg < kUG; ++gg) {
+            const int g = j * kUG + gg;  // group of the chunk
+            const uint32_t d = tmem + static_cast<uint32_t>((ub * kUG + gg) * kBN);
+            if constexpr (kMmaBias) mma_i8(d, bias_desc, bias_desc, bias_idesc, false);
+#pragma unroll
+            for (int kk = 0; kk < 2; ++kk) {
+              const uint64_t koff = static_cast<uint64_t>(2 * (2 * g + kk));
+              mma_i8(d, a_desc + koff, b_desc + koff, idesc, true);
+            }
+          }
+          mma_commit(&sm.acc_full[ub]);
         }
-        mma_commit(&sm.acc_full[pb]);
-        mma_commit(&sm.empty[st]);  // the stage is free once its MMAs have read it
+        if (ok) mma_commit(&sm.empty[st]);  // the stage is free once its MMAs have read it
       }
       if (!ok) {
         record_device_error(a, kDevMmaTimeout);
@@ -541,26 +610,30 @@ __device__ __forceinline__ void gemm_tile(const CUtensorMap* map_w, const CUtens
     if constexpr (Shape<kBN>::kSplitRegs) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsEpilogue));
     // ---------------- epilogue (two warpgroups) ----------------
     const int quad = warp & 3;                                     // TMEM lanes 32*quad .. +31
-    const int role = (warp - Shape<kBN>::kFirstEpiWarp) >> 2;      // chunks c with c % 2 == role
+    const int role = (warp - Shape<kBN>::kFirstEpiWarp) >> 2;      // units u with u % 2 == role
     constexpr int kCols = Shape<kBN>::kCols;
     constexpr int kLd = Shape<kBN>::kLdCols;
     uint64_t acc[kCols / 2];  // fp32 pairs: columns 2j, 2j + 1
 #pragma unroll
     for (int j = 0; j < kCols / 2; ++j) acc[j] = 0;
-    const uint64_t bias2 = f2_pack(__float_as_uint(kAccBiasF), __float_as_uint(kAccBiasF));
+    const uint32_t off_bits = kMmaBias ? kMmaBiasBits : __float_as_uint(kAccBiasF);
+    const uint64_t bias2 = f2_pack(off_bits, off_bits);
     const int et = static_cast<int>(threadIdx.x) - Shape<kBN>::kFirstEpiWarp * 32;  // epilogue thread
     const uint32_t tl = tmem + (static_cast<uint32_t>(32 * quad) << 16);
-    // Chunk c fills buffer pair c % kPairs; pair pb always belongs to
-    // warpgroup pb % 2 (chunks alternate and kPairs is even).  Every buffer
-    // starts at the bias.
+    // Unit u (groups u * kUG ..) fills buffers kUG * (u % kUnits) ..; unit
+    // ub always belongs to warpgroup ub % 2 (units alternate and kUnits is
+    // even).  Without the offset MMA every buffer starts at the bias.
+    if constexpr (!kMmaBias) {
 #pragma unroll 1
-    for (int b = 0; b < kAccBufs; ++b)
-      if (((b >> 1) & 1) == role) tmem_fill_bias<kCols>(tl + static_cast<uint32_t>(b * kBN));
-    tmem_wait_st();
-    tmem_fence_before();
+      for (int b = 0; b < kAccBufs; ++b)
+        if ((b / kUG) % 2 == role) tmem_fill_bias<kCols>(tl + static_cast<uint32_t>(b * kBN));
+      tmem_wait_st();
+      tmem_fence_before();
+    }
     __syncwarp();
     if (lane == 0)
-      for (int pb = role; pb < kPairs; pb += 2) mbar_arrive(&sm.acc_empty[pb]);
+      for (int ub = role; ub < kUnits; ub += 2) mbar_arrive(&sm.acc_empty[ub]);
+    bool range_ok = true;  // every group scale within the offset MMA's exact range
     auto stage_scales = [&](int g0) {
       stage_group_scales<kEpiWarps * 32>(sm.ws, a.ws, a.G, a.d, row0, 2 * c_begin + g0, ngroups - g0, et);
     };
@@ -572,7 +645,7 @@ __device__ __forceinline__ void gemm_tile(const CUtensorMap* map_w, const CUtens
     cp_async_wait_all();
     epi_sync<kEpiWarps>();
     bool ok = true;
-    for (int w0 = 0; w0 < ngroups; w0 += kWsWin) {  // windows of group scales (kWsWin % 4 == 0)
+    for (int w0 = 0; w0 < ngroups; w0 += kWsWin) {  // windows of group scales (whole unit pairs)
       if (w0 > 0) {
         epi_sync<kEpiWarps>();  // both warpgroups are done with the previous window
         stage_scales(w0);
@@ -580,57 +653,72 @@ __device__ __forceinline__ void gemm_tile(const CUtensorMap* map_w, const CUtens
         epi_sync<kEpiWarps>();
       }
       const int wend = ngroups - w0 < kWsWin ? ngroups : w0 + kWsWin;
-      // this warpgroup's chunks of the window (chunk c = gi / 2: groups gi,
-      // gi + 1 in buffers 2 pb, 2 pb + 1); after a timeout the warp keeps
+      // this warpgroup's units of the window (unit u: groups u * kUG ..
+      // in buffers kUG * (u % kUnits) ..); after a timeout the warp keeps
       // walking the windows without waiting, so that both warpgroups meet
       // the same barriers
-      for (int gi = w0 + 2 * role; gi < wend; gi += 4) {
-        const int c = gi >> 1, pb = c % kPairs, buf = 2 * pb;
-        const float* wrow = sm.ws + (32 * quad + lane) * kWsStride + (gi - w0);
-        if (ok && !mbar_wait_bounded(&sm.acc_full[pb], (c / kPairs) & 1, kWaitLimitNs)) ok = false;
+      for (int u = w0 / kUG + role; u * kUG < wend; u += 2) {
+        const int ub = u % kUnits;
+        const float* wrow = sm.ws + (32 * quad + lane) * kWsStride + (u * kUG - w0);
+        if (ok && !mbar_wait_bounded(&sm.acc_full[ub], (u / kUnits) & 1, kWaitLimitNs)) ok = false;
         if (!ok) continue;
         tmem_fence_after();
-        // The pair's two groups as one software pipeline of kLd-column
-        // loads: load q + 1 is issued as soon as load q has landed, so its
-        // latency overlaps q's arithmetic (one exposed load per pair instead
-        // of one per kLd columns).
+        // The unit's groups as one software pipeline of kLd-column loads:
+        // load q + 1 is issued as soon as load q has landed, so its latency
+        // overlaps q's arithmetic (one exposed load per unit).
         {
           static_assert(kLd == 16, "pipelined loads of 16 columns");
           constexpr int kL = kCols / kLd;  // loads per group
-          const uint32_t base = tl + static_cast<uint32_t>(buf * kBN);
-          const uint64_t w2a = f2_pack(__float_as_uint(wrow[0]), __float_as_uint(wrow[0]));
-          const uint64_t w2b = f2_pack(__float_as_uint(wrow[1]), __float_as_uint(wrow[1]));
+          const uint32_t base = tl + static_cast<uint32_t>(ub * kUG * kBN);
+          uint64_t w2[kUG];
+#pragma unroll
+          for (int gg = 0; gg < kUG; ++gg) {
+            float w = wrow[gg];
+            if constexpr (kMmaBias) {
+              const float ws = w * __uint_as_float(kMmaScaleIn);  // exact below 2^38
+              range_ok &= !(isinf(ws) && isfinite(w));
+              w = ws;
+            }
+            w2[gg] = f2_pack(__float_as_uint(w), __float_as_uint(w));
+          }
           uint32_t ra[kLd], rb[kLd];
           tmem_ld16(base, ra);
 #pragma unroll
-          for (int q = 0; q < 2 * kL; ++q) {
+          for (int q = 0; q < kUG * kL; ++q) {
             uint32_t(&cur)[kLd] = (q & 1) ? rb : ra;
             uint32_t(&nxt)[kLd] = (q & 1) ? ra : rb;
             tmem_wait_ld16(cur);
-            if (q + 1 < 2 * kL) {
+            if (q + 1 < kUG * kL) {
               const int q1 = q + 1;
               tmem_ld16(base + static_cast<uint32_t>((q1 / kL) * kBN + kLd * (q1 % kL)), nxt);
             }
-            const uint64_t w2 = q < kL ? w2a : w2b;
             const int col = (q % kL) * (kLd / 2);
 #pragma unroll
             for (int j = 0; j < kLd / 2; ++j)
-              acc[col + j] = f2_unbias_fma(f2_pack(cur[2 * j], cur[2 * j + 1]), bias2, w2, acc[col + j]);
+              acc[col + j] = f2_unbias_fma(f2_pack(cur[2 * j], cur[2 * j + 1]), bias2, w2[q / kL], acc[col + j]);
           }
-          // both buffers ready for their next use
-          tmem_fill_bias<kCols>(base);
-          tmem_fill_bias<kCols>(base + kBN);
+          if constexpr (!kMmaBias) {
+            // the unit's buffers ready for their next use
+#pragma unroll
+            for (int gg = 0; gg < kUG; ++gg) tmem_fill_bias<kCols>(base + static_cast<uint32_t>(gg * kBN));
+            tmem_wait_st();
+          }
         }
-        // both buffers go back to the MMA warp once their refill has completed
-        tmem_wait_st();
+        // the buffers go back to the MMA warp once read (and refilled)
         tmem_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.acc_empty[pb]);
+        if (lane == 0) mbar_arrive(&sm.acc_empty[ub]);
       }
     }
     if (!ok) {
       record_device_error(a, kDevMmaTimeout);
       *sm.flag = 1;
+    }
+    if constexpr (kMmaBias) {
+      if (!range_ok) {
+        record_device_error(a, kDevScaleRange);
+        *sm.flag = 1;
+      }
     }
     epi_sync<kEpiWarps>();
     // Every load has landed and every MMA that read the ring has
@@ -641,11 +729,15 @@ __device__ __forceinline__ void gemm_tile(const CUtensorMap* map_w, const CUtens
     const bool good = *sm.flag == 0;
     float* tile = reinterpret_cast<float*>(sm.ring);
     const int r_local = 32 * quad + lane;
+    // sums of the offset-MMA path are kept scaled by 2^-59 (exact)
+    const float out_scale = kMmaBias ? __uint_as_float(kMmaScaleOut) : 1.f;
     if (good && role == 0) {
 #pragma unroll
       for (int j = 0; j < kCols / 2; ++j) {
         float v0, v1;
         f2_unpack(acc[j], v0, v1);
+        v0 *= out_scale;
+        v1 *= out_scale;
         tile[(2 * j) * kBM + r_local] = v0;
         tile[(2 * j + 1) * kBM + r_local] = v1;
       }
@@ -657,6 +749,8 @@ __device__ __forceinline__ void gemm_tile(const CUtensorMap* map_w, const CUtens
       for (int j = 0; j < kCols / 2; ++j) {
         float v0, v1;
         f2_unpack(acc[j], v0, v1);
+        v0 *= out_scale;
+        v1 *= out_scale;
         float* t0 = tile + (2 * j) * kBM + r_local;
         float* t1 = tile + (2 * j + 1) * kBM + r_local;
         const float s0 = *t0 + v0, s1 = *t1 + v1;
@@ -679,20 +773,39 @@ __device__ __forceinline__ void gemm_tile(const CUtensorMap* map_w, const CUtens
       bool all_good = true;
       for (int p = 0; p < s; ++p) all_good &= ld_cluster_s32(cluster_peer(smem_u32(sm.flag), p)) == 0;
       if (all_good) {
+        // This thread's float4s of the share, q = q0 + et + k * kEpiThreads:
+        // per partial tile, every load is issued before the first is used (one
+        // remote round trip per split instead of one per float4), summed in
+        // split order.
+        constexpr int kMaxIt = (kQuads + kEpiThreads - 1) / kEpiThreads;
         const int q0 = split * kQuads / s, q1 = (split + 1) * kQuads / s;
-        for (int q = q0 + et; q < q1; q += kEpiThreads) {
-          const int j = q >> 5, t = tok0 + j;
-          if (t >= a.m) continue;
-          float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-          for (int p = 0; p < s; ++p) {
-            const float4 u = ld_cluster_f4(cluster_peer(tile_s + 16u * q, p));
-            v.x += u.x;
-            v.y += u.y;
-            v.z += u.z;
-            v.w += u.w;
+        float4 v[kMaxIt];
+#pragma unroll
+        for (int k = 0; k < kMaxIt; ++k) v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int p = 0; p < s; ++p) {
+          const uint32_t peer_tile = cluster_peer(tile_s, p);
+          float4 u[kMaxIt];
+#pragma unroll
+          for (int k = 0; k < kMaxIt; ++k) {
+            const int q = q0 + et + k * kEpiThreads;
+            u[k] = q < q1 ? ld_cluster_f4(peer_tile + 16u * q) : make_float4(0.f, 0.f, 0.f, 0.f);
           }
+#pragma unroll
+          for (int k = 0; k < kMaxIt; ++k) {
+            v[k].x += u[k].x;
+            v[k].y += u[k].y;
+            v[k].z += u[k].z;
+            v[k].w += u[k].w;
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < kMaxIt; ++k) {
+          const int q = q0 + et + k * kEpiThreads;
+          const int j = q >> 5, t = tok0 + j;
+          if (q >= q1 || t >= a.m) continue;
           const float x = sm.xs[j];
-          store_out4(a.y, a, t, row0 + 4 * (q & 31), make_float4(v.x * x, v.y * x, v.z * x, v.w * x));
+          store_out4(a.y, a, t, row0 + 4 * (q & 31),
+                     make_float4(v[k].x * x, v[k].y * x, v[k].z * x, v[k].w * x));
         }
       }
     } else if (*sm.flag == 0) {
@@ -744,6 +857,302 @@ __global__ void __launch_bounds__(Shape<kBN>::kThreads, 1)
   int o = 0;
   while (o + 1 < g.count && static_cast<int>(blockIdx.x) >= g.base[o + 1]) ++o;
   gemm_tile<kBN>(&g.mw[o], &g.mx[o], g.op[o], static_cast<int>(blockIdx.x) - g.base[o]);
+}
+
+// ---------------------------------------------------------------------------
+// Persistent whole tiles (128 tokens per tile).  One CTA per SM walks a list
+// of output tiles made on the host (whole K per tile, no split; largest
+// first onto the least-loaded CTA), and its TMA, MMA and epilogue counters
+// run on across tile boundaries: the next tile's loads and MMAs proceed
+// while the epilogue finishes the current one, and the block's set-up
+// (barriers, tensor memory, the offset tile) happens once per launch.
+//   * warp 0 streams 32 KB stages (128 weight rows x 128 B and 128 tokens x
+//     128 B) into a ring of kPStages;
+//   * warps 1 and 2 issue the MMAs of alternate chunks (one thread's
+//     instruction issue would bound the loop): per 64-column group the
+//     offset MMA and two K = 32 steps into one of kPBufs single-group
+//     buffers of 128 columns (a chunk's two groups fill buffers 0-1 or 2-3,
+//     so the two issuers never share one);
+//   * the epilogue warpgroups split the tile by token columns (warpgroup w
+//     the 64 tokens 64 w ..), so every epilogue thread ends a tile holding
+//     the complete sums of its weight row for its 64 tokens, and stores them
+//     straight to Y (a warp writes 32 consecutive rows of one token: 128
+//     contiguous bytes).  Group scales come from global memory, a few chunks
+//     ahead of their use.
+// ---------------------------------------------------------------------------
+constexpr int kPStages = 6;
+constexpr uint32_t kPStage = kStageA + 128u * kChunk;   // 32 KB
+constexpr int kPBufs = 4;                               // 4 x 128 = 512 tensor-memory columns
+constexpr int kPCols = 64;                              // token columns per epilogue warpgroup
+constexpr int kPWsAhead = 4;                            // chunks of group scales in flight
+constexpr int kPMaxUnits = 4096;                        // tiles in one launch
+constexpr int kPMaxCtas = 256;                          // at least the SM count
+constexpr int kPThreads = 384;
+constexpr int kPStreams = 1;  // tile lists per CTA
+constexpr uint32_t kPSmemBytes = 1024u + kPStages * kPStage + kBiasTileBytes + 256u;
+
+struct POp {
+  float* y;
+  const float* xs;
+  const float* ws;
+  int m, n, d, G, tiles_n, chunks;
+};
+struct PArgs {
+  CUtensorMap mw[kMaxGroupOps];
+  CUtensorMap mx[kMaxGroupOps];
+  POp op[kMaxGroupOps];
+  unsigned int* err;
+  unsigned short first[kPStreams * kPMaxCtas + 1];  // CTA c runs unit[first[c] .. first[c + 1])
+  unsigned short unit[kPMaxUnits];      // (op << 12) | tile, tile = tile_m * tiles_n + tile_n
+};
+
+static_assert(kPSmemBytes <= 232448, "shared memory per block");
+static_assert(sizeof(PArgs) <= 32764, "kernel parameter space");
+static_assert(kPStages % 2 == 0 && kPBufs % 4 == 0, "alternate chunks keep to their own stages and buffers");
+
+struct PTile {
+  int o, row0, tok0, chunks;
+};
+__device__ __forceinline__ PTile p_tile(const PArgs& p, int i) {
+  const unsigned u = p.unit[i];
+  PTile t;
+  t.o = static_cast<int>(u >> 12);
+  const int tile = static_cast<int>(u & 0xFFFu);
+  const int tn = p.op[t.o].tiles_n;
+  t.row0 = (tile / tn) * kBM;
+  t.tok0 = (tile % tn) * 128;
+  t.chunks = p.op[t.o].chunks;
+  return t;
+}
+
+__device__ __forceinline__ void p_record_error(const PArgs& p, unsigned int code) {
+  if (p.err) atomicCAS(p.err, 0u, code);
+}
+
+// The group scales of chunk c (groups 2c, 2c + 1) of one weight row.
+__device__ __forceinline__ float2 p_ws(const float2* row, bool in, int c, int chunks) {
+  return in && c < chunks ? __ldg(row + c) : make_float2(0.f, 0.f);
+}
+
+__global__ void __launch_bounds__(kPThreads, 1) gemm_w8a8_persistent_kernel(const __grid_constant__ PArgs p) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* ring = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~static_cast<uintptr_t>(1023u));
+  unsigned char* bias = ring + kPStages * kPStage;
+  uint64_t* full = reinterpret_cast<uint64_t*>(bias + kBiasTileBytes);
+  uint64_t* empty = full + kPStages;
+  uint64_t* acc_full = empty + kPStages;
+  uint64_t* acc_empty = acc_full + kPBufs;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + kPBufs);
+  volatile int* broken = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int u_begin = p.first[blockIdx.x], u_end = p.first[blockIdx.x + 1];
+
+  for (uint32_t i = threadIdx.x; i < kBiasTileBytes / 16; i += kPThreads)
+    reinterpret_cast<uint4*>(bias)[i] = mma_bias_chunk();
+  fence_proxy_async_smem();
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kPStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < kPBufs; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 8);  // every epilogue warp reads every buffer
+    }
+    *broken = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kPBufs * 128u)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tmem_fence_before();
+  __syncthreads();
+  tmem_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  griddep_launch_dependents();
+
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsProducer));
+    if (warp == 0 && lane == 0) {
+      // ---------------- TMA producer ----------------
+      bool ok = true;
+      // The first tile's weight chunks that fit the ring go out before the
+      // wait for the previous kernel (weights never depend on it).
+      int pre = 0;
+      if (u_begin < u_end) {
+        const PTile f = p_tile(p, u_begin);
+        pre = f.chunks < kPStages ? f.chunks : kPStages;
+        for (int c = 0; c < pre; ++c) {
+          mbar_arrive_expect_tx(&full[c], kPStage);
+          tma_load_2d(ring + c * kPStage, &p.mw[f.o], c * kChunk, f.row0, &full[c]);
+        }
+      }
+      griddep_wait();
+      int gc = 0;  // chunk counter over the whole tile list
+      for (int i = u_begin; i < u_end && ok; ++i) {
+        const PTile t = p_tile(p, i);
+        for (int c = 0; c < t.chunks; ++c, ++gc) {
+          const int st = gc % kPStages;
+          unsigned char* sa = ring + st * kPStage;
+          if (gc < pre) {
+            tma_load_2d(sa + kStageA, &p.mx[t.o], c * kChunk, t.tok0, &full[st]);
+            continue;
+          }
+          if (gc >= kPStages && !mbar_wait_bounded(&empty[st], ((gc / kPStages) - 1) & 1, kWaitLimitNs)) {
+            ok = false;
+            break;
+          }
+          if (*broken) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[st], kPStage);
+          tma_load_2d(sa, &p.mw[t.o], c * kChunk, t.row0, &full[st]);
+          tma_load_2d(sa + kStageA, &p.mx[t.o], c * kChunk, t.tok0, &full[st]);
+        }
+      }
+      if (!ok) {
+        p_record_error(p, kDevMmaTimeout);
+        *broken = 1;
+      }
+    } else if ((warp == 1 || warp == 2) && lane == 0) {
+      // ---------------- MMA issuers: warp 1 the even chunks, warp 2 the odd ----------------
+      const uint32_t idesc = i8_idesc(128);
+      const uint32_t bias_idesc = u8_idesc(128);
+      const uint64_t bias_desc = sw32_desc(smem_u32(bias));
+      bool ok = true;
+      int gc = 0, gu = 0;  // chunk and group counters over the whole tile list
+      for (int i = u_begin; i < u_end && ok; ++i) {
+        const PTile t = p_tile(p, i);
+        for (int c = 0; c < t.chunks && ok; ++c, ++gc) {
+          if ((gc & 1) != warp - 1) {
+            gu += 2;
+            continue;
+          }
+          const int st = gc % kPStages;
+          if (!mbar_wait_bounded(&full[st], (gc / kPStages) & 1, kWaitLimitNs) || *broken) {
+            ok = false;
+            break;
+          }
+          const uint64_t a_desc = sw128_desc(smem_u32(ring + st * kPStage));
+          const uint64_t b_desc = sw128_desc(smem_u32(ring + st * kPStage + kStageA));
+#pragma unroll
+          for (int g = 0; g < 2; ++g, ++gu) {
+            const int ub = gu % kPBufs;
+            if (!mbar_wait_bounded(&acc_empty[ub], (gu / kPBufs) & 1, kWaitLimitNs)) {
+              ok = false;
+              break;
+            }
+            tmem_fence_after();
+            const uint32_t d = tmem + static_cast<uint32_t>(ub * 128);
+            mma_i8(d, bias_desc, bias_desc, bias_idesc, false);
+#pragma unroll
+            for (int kk = 0; kk < 2; ++kk) {
+              const uint64_t koff = static_cast<uint64_t>(2 * (2 * g + kk));
+              mma_i8(d, a_desc + koff, b_desc + koff, idesc, true);
+            }
+            mma_commit(&acc_full[ub]);
+          }
+          if (ok) mma_commit(&empty[st]);
+        }
+      }
+      if (!ok) {
+        p_record_error(p, kDevMmaTimeout);
+        *broken = 1;
+      }
+    }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsEpilogue));
+    // ---------------- epilogue: 8 warps, token columns by warpgroup ----------------
+    const int quad = warp & 3;
+    const int role = (warp - 4) >> 2;
+    const int r_local = 32 * quad + lane;
+    const uint32_t tl = tmem + (static_cast<uint32_t>(32 * quad) << 16) + static_cast<uint32_t>(role * kPCols);
+    const uint64_t off2 = f2_pack(kMmaBiasBits, kMmaBiasBits);
+    const float scale_in = __uint_as_float(kMmaScaleIn);
+    const float scale_out = __uint_as_float(kMmaScaleOut);
+    __syncwarp();
+    if (lane == 0)
+      for (int ub = 0; ub < kPBufs; ++ub) mbar_arrive(&acc_empty[ub]);  // every buffer starts free
+    griddep_wait();  // xs and the outputs belong to the stream order
+    bool ok = true, range_ok = true;
+    int gu = 0;
+    for (int i = u_begin; i < u_end; ++i) {
+      const PTile t = p_tile(p, i);
+      const POp& op = p.op[t.o];
+      const int row = t.row0 + r_local;
+      const bool row_in = row < op.d;  // rows past d read zeros (TMA fill) and are not stored
+      const float2* wsrow = reinterpret_cast<const float2*>(op.ws + static_cast<size_t>(row_in ? row : 0) * op.G);
+      static_assert(kPWsAhead == 4, "four chunks of scales in flight");
+      float2 w0 = p_ws(wsrow, row_in, 0, t.chunks), w1 = p_ws(wsrow, row_in, 1, t.chunks);
+      float2 w2 = p_ws(wsrow, row_in, 2, t.chunks), w3 = p_ws(wsrow, row_in, 3, t.chunks);
+      uint64_t acc[kPCols / 2];
+#pragma unroll
+      for (int j = 0; j < kPCols / 2; ++j) acc[j] = 0;
+#pragma unroll 1
+      for (int c = 0; c < t.chunks; ++c) {
+        const float2 wc = w0;
+        w0 = w1;
+        w1 = w2;
+        w2 = w3;
+        w3 = p_ws(wsrow, row_in, c + kPWsAhead, t.chunks);
+#pragma unroll
+        for (int g = 0; g < 2; ++g, ++gu) {
+          const int ub = gu % kPBufs;
+          if (ok && (!mbar_wait_bounded(&acc_full[ub], (gu / kPBufs) & 1, kWaitLimitNs) || *broken)) ok = false;
+          if (!ok) continue;
+          tmem_fence_after();
+          uint32_t ra[32], rb[32];
+          tmem_ld32(tl + static_cast<uint32_t>(ub * 128), ra);
+          tmem_ld32(tl + static_cast<uint32_t>(ub * 128 + 32), rb);
+          tmem_wait_ld16(*reinterpret_cast<uint32_t(*)[16]>(ra));
+          tmem_wait_ld16(*reinterpret_cast<uint32_t(*)[16]>(ra + 16));
+          tmem_wait_ld16(*reinterpret_cast<uint32_t(*)[16]>(rb));
+          tmem_wait_ld16(*reinterpret_cast<uint32_t(*)[16]>(rb + 16));
+          // the buffer is back with the MMA warp as soon as it is in registers
+          tmem_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[ub]);
+          const float w = g ? wc.y : wc.x;
+          const float wsc = w * scale_in;  // exact below 2^38
+          range_ok &= !(isinf(wsc) && isfinite(w));
+          const uint64_t w2p = f2_pack(__float_as_uint(wsc), __float_as_uint(wsc));
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc[j] = f2_unbias_fma(f2_pack(ra[2 * j], ra[2 * j + 1]), off2, w2p, acc[j]);
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            acc[16 + j] = f2_unbias_fma(f2_pack(rb[2 * j], rb[2 * j + 1]), off2, w2p, acc[16 + j]);
+        }
+      }
+      if (ok && range_ok && row_in) {
+        // Y[t][row] for this warpgroup's 64 tokens: (sum * 2^59) * xs[t]
+        const int tb = t.tok0 + role * kPCols;
+#pragma unroll
+        for (int j = 0; j < kPCols / 2; ++j) {
+          float v0, v1;
+          f2_unpack(acc[j], v0, v1);
+          const int t0 = tb + 2 * j;
+          if (t0 < op.m) op.y[static_cast<size_t>(t0) * op.d + row] = (v0 * scale_out) * __ldg(op.xs + t0);
+          if (t0 + 1 < op.m) op.y[static_cast<size_t>(t0 + 1) * op.d + row] = (v1 * scale_out) * __ldg(op.xs + t0 + 1);
+        }
+      }
+    }
+    if (!ok) {
+      p_record_error(p, kDevMmaTimeout);
+      *broken = 1;
+    }
+    if (!range_ok) p_record_error(p, kDevScaleRange);
+  }
+
+  tmem_fence_before();
+  __syncthreads();
+  tmem_fence_after();
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kPBufs * 128u) : "memory");
 }
 
 // Split-K: y[t][r] = xs[t] * sum_s partial[s][t][r], the splits summed in split
@@ -973,6 +1382,137 @@ cudaError_t launch_group_bn(const GroupArgs& g, int grid, int cluster, cudaStrea
 }
 
 // ---------------------------------------------------------------------------
+// Persistent plan: whole tiles, each costing its K chunks plus one chunk of
+// set-up and output, largest first onto the least-loaded CTA (ties to the
+// lowest CTA).  Taken when every SM gets a tile and the busiest CTA carries
+// at most kPMaxImbalance times the ideal share of all the SMs; otherwise the
+// split-K kernels fill the GPU better.
+// ---------------------------------------------------------------------------
+constexpr double kPMaxImbalance = 1.3;
+constexpr int kPTileOverhead = 1;
+
+struct PChoice {
+  bool use = false;
+  int ctas = 0, units = 0;
+  long long makespan = 0, total = 0;
+};
+
+PChoice persistent_plan(const mli_gemm_op* ops, int count, int m, const DeviceInfo& dev, PArgs* pa) {
+  PChoice r;
+  if (m <= 64 || count < 1 || count > kMaxGroupOps || (launch_flags() & MLI_LAUNCH_NO_PERSISTENT)) return r;
+  const int tiles_n = (m + 127) / 128;
+  int order[kMaxGroupOps];
+  for (int i = 0; i < count; ++i) {
+    if (ops[i].n % kChunk != 0 || !aligned(ops[i].w_s, 8)) return r;
+    const long long tiles = static_cast<long long>((ops[i].d + kBM - 1) / kBM) * tiles_n;
+    if (tiles > 4096 || r.units + tiles > kPMaxUnits) return r;
+    r.units += static_cast<int>(tiles);
+    r.total += tiles * (ops[i].n / kChunk + kPTileOverhead);
+    order[i] = i;
+  }
+  for (int i = 1; i < count; ++i)  // ops by tile cost, largest first (stable)
+    for (int j = i; j > 0 && ops[order[j]].n > ops[order[j - 1]].n; --j) {
+      const int t = order[j];
+      order[j] = order[j - 1];
+      order[j - 1] = t;
+    }
+  r.ctas = r.units < dev.sm_count ? r.units : dev.sm_count;
+  if (r.ctas > kPMaxCtas) r.ctas = kPMaxCtas;
+  if (r.ctas < 1) return r;
+  // min-heap of (load, cta)
+  static thread_local long long load[kPMaxCtas];
+  static thread_local long long sload[kPStreams * kPMaxCtas];
+  static thread_local int heap[kPMaxCtas];
+  static thread_local unsigned short assign[kPMaxUnits];
+  static thread_local unsigned short code[kPMaxUnits];
+  const int H = r.ctas;
+  auto less = [&](int a, int b) { return load[a] < load[b] || (load[a] == load[b] && a < b); };
+  for (int c = 0; c < H; ++c) {
+    load[c] = 0;
+    for (int k = 0; k < kPStreams; ++k) sload[kPStreams * c + k] = 0;
+    heap[c] = c;  // all loads zero: index order is a valid heap
+  }
+  int u = 0;
+  for (int k = 0; k < count; ++k) {
+    const int o = order[k];
+    const long long cost = ops[o].n / kChunk + kPTileOverhead;
+    const int tiles = ((ops[o].d + kBM - 1) / kBM) * tiles_n;
+    for (int tile = 0; tile < tiles; ++tile, ++u) {
+      const int c = heap[0];
+      const int v = kPStreams == 1 ? c : kPStreams * c + (sload[kPStreams * c + 1] < sload[kPStreams * c] ? 1 : 0);
+      assign[u] = static_cast<unsigned short>(v);
+      code[u] = static_cast<unsigned short>((k << 12) | tile);  // op slot k of the launch
+      sload[v] += cost;
+      load[c] += cost;
+      // sift down
+      int i = 0;
+      for (;;) {
+        const int l = 2 * i + 1, rr = l + 1;
+        int m = i;
+        if (l < H && less(heap[l], heap[m])) m = l;
+        if (rr < H && less(heap[rr], heap[m])) m = rr;
+        if (m == i) break;
+        const int t = heap[i];
+        heap[i] = heap[m];
+        heap[m] = t;
+        i = m;
+      }
+    }
+  }
+  for (int c = 0; c < H; ++c) r.makespan = load[c] > r.makespan ? load[c] : r.makespan;
+  r.use = r.units >= dev.sm_count &&
+          static_cast<double>(r.makespan) <= kPMaxImbalance * static_cast<double>(r.total) / dev.sm_count;
+  if (!r.use || !pa) return r;
+  // units grouped by CTA, each CTA's in the order assigned
+  const int V = kPStreams * H;
+  int cnt[kPStreams * kPMaxCtas + 1] = {};
+  for (int i = 0; i < r.units; ++i) ++cnt[assign[i] + 1];
+  for (int v = 0; v < V; ++v) cnt[v + 1] += cnt[v];
+  for (int v = 0; v <= V; ++v) pa->first[v] = static_cast<unsigned short>(cnt[v]);
+  for (int i = 0; i < r.units; ++i) pa->unit[cnt[assign[i]]++] = code[i];
+  // op slots in the launch follow the cost order
+  for (int k = 0; k < count; ++k) {
+    const mli_gemm_op& op = ops[order[k]];
+    if (!make_map(&pa->mw[k], op.w_q, op.d, op.n, kBM) || !make_map(&pa->mx[k], op.xq, m, op.n, 128)) {
+      r.use = false;
+      return r;
+    }
+    POp& po = pa->op[k];
+    po.y = op.y;
+    po.xs = op.xs;
+    po.ws = op.w_s;
+    po.m = m;
+    po.n = op.n;
+    po.d = op.d;
+    po.G = op.n / 64;
+    po.tiles_n = tiles_n;
+    po.chunks = op.n / kChunk;
+  }
+  pa->err = device_error_word();
+  return r;
+}
+
+// Plans and launches the persistent kernel: returns -1 (nothing launched)
+// when the split-K kernels are the better plan, else the status.
+int launch_persistent(const mli_gemm_op* ops, int count, int m, const DeviceInfo& dev, cudaStream_t stream) {
+  static thread_local PArgs pa;
+  const PChoice ch = persistent_plan(ops, count, m, dev, &pa);
+  if (!ch.use) return -1;
+  static const bool fits = []() {
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, gemm_w8a8_persistent_kernel) != cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    return fa.numRegs * kPThreads >= kRegsBlock;
+  }();
+  if (!fits) return check_cuda(cudaErrorInvalidConfiguration);
+  cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(gemm_w8a8_persistent_kernel), kPSmemBytes);
+  if (e != cudaSuccess) return check_cuda(e);
+  return check_cuda(launch(gemm_w8a8_persistent_kernel, dim3(ch.ctas), dim3(kPThreads), kPSmemBytes, stream, true, pa));
+}
+
+// ---------------------------------------------------------------------------
 // The int8 tensor-core roof of this GPU (mli_debug_int8_mma_peak): every CTA
 // issues back-to-back kind::i8 MMAs (M = 128, N = kN, K = 32) from one thread
 // on operands resident in shared memory (zeros: the values do not change the
@@ -1042,6 +1582,11 @@ int gemm_w8a8_tc(float* y, const int8_t* xq, const float* xs, const int8_t* w_q,
   cudaError_t err = cudaSuccess;
   const DeviceInfo& dev = current_device(&err);
   if (err != cudaSuccess) return set_status(MLI_ERR_CUDA, err);
+  {
+    const mli_gemm_op op = {y, xq, xs, w_q, w_s, n, d};
+    const int pr = tc::launch_persistent(&op, 1, m, dev, stream);
+    if (pr != -1) return pr;
+  }
   const bool have_ws = workspace != nullptr &&
                        workspace_bytes >= gemm_tc_workspace_bytes(m, n, d, dev.sm_count);
   const tc::Plan p = tc::choose(m, n, d, dev, have_ws);
@@ -1089,6 +1634,10 @@ int gemm_w8a8_tc_group(const mli_gemm_op* ops, int count, int m, cudaStream_t st
   cudaError_t err = cudaSuccess;
   const DeviceInfo& dev = current_device(&err);
   if (err != cudaSuccess) return set_status(MLI_ERR_CUDA, err);
+  {
+    const int pr = tc::launch_persistent(ops, count, m, dev, stream);
+    if (pr != -1) return pr;
+  }
   int order[tc::kMaxGroupOps];
   for (int i = 0; i < count; ++i) order[i] = i;
   for (int i = 1; i < count; ++i)  // insertion sort, largest n first (stable)
@@ -1188,6 +1737,23 @@ extern "C" int mli_debug_int8_mma_peak(int n, int iters, int ctas, void* stream)
     default: e = launch(tc::mma_peak_kernel<64>, dim3(ctas), dim3(128), smem, st, false, iters, err); break;
   }
   return check_cuda(e);
+}
+
+extern "C" int mli_debug_plan_gemm_group(const mli_gemm_op* ops, int count, int m, int* out) {
+  using namespace mli;
+  if (!ops || !out || count < 1 || count > MLI_GEMM_GROUP_MAX || m <= 0) return set_status(MLI_ERR_INVALID_ARG);
+  for (int i = 0; i < count; ++i)
+    if (ops[i].n <= 0 || ops[i].d <= 0) return set_status(MLI_ERR_INVALID_ARG);
+  cudaError_t err = cudaSuccess;
+  const DeviceInfo& dev = current_device(&err);
+  if (err != cudaSuccess) return set_status(MLI_ERR_CUDA, err);
+  const tc::PChoice ch = tc::persistent_plan(ops, count, m, dev, nullptr);
+  out[0] = ch.use ? 1 : 0;
+  out[1] = ch.ctas;
+  out[2] = ch.units;
+  out[3] = static_cast<int>(ch.makespan);
+  out[4] = static_cast<int>(ch.total);
+  return set_status(MLI_OK);
 }
 
 extern "C" int mli_debug_plan_gemm(int m, int n, int d, size_t workspace_bytes, int* out) {

@@ -20,6 +20,7 @@ enum DeviceError : unsigned int {
   kDevMmaTimeout = 2,    // tensor-core pipeline barrier never completed
   kDevPeerTimeout = 3,   // rows of a row-sharded step never arrived from a rank
   kDevChainTimeout = 4,  // a chained GEMV's inputs were never completed
+  kDevScaleRange = 5,    // a group scale outside the batched tensor-core path's exact range
 };
 #ifndef MLI_SEPARATE_DEVICE_MODULE
 extern __device__ unsigned int g_device_error;

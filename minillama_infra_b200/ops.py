@@ -107,6 +107,28 @@ def gemm_w8a8_group(items, m: int, group_size: int = 64, stream=None):
     check(lib().mli_gemm_w8a8_group(arr, len(items), m, group_size, _stream(stream)), "gemm_w8a8_group")
 
 
+def gemm_group_plan(items, m: int) -> dict:
+    """The persistent plan mli_gemm_w8a8_group would take for these items
+    (same tuples as gemm_w8a8_group; nothing is launched)."""
+    from ._lib import GemmOp
+
+    arr = (GemmOp * len(items))()
+    for i, (y, xq, xs, w_q, w_s, n, d) in enumerate(items):
+        arr[i] = GemmOp(_ptr(y), _ptr(xq), _ptr(xs), _ptr(w_q), _ptr(w_s), n, d)
+    out = (ctypes.c_int * 5)()
+    check(lib().mli_debug_plan_gemm_group(arr, len(items), m, out), "debug_plan_gemm_group")
+    return {"persistent": bool(out[0]), "ctas": out[1], "tiles": out[2], "busiest": out[3], "total": out[4]}
+
+
+def set_gemm_persistent(enabled: bool) -> None:
+    """Batched W8A8 above 64 tokens: let well-balanced problems run on the
+    persistent whole-tile kernel (default), or always take the split-K ones."""
+    from ._lib import MLI_LAUNCH_NO_PERSISTENT
+    flags = lib().mli_get_launch_flags()
+    flags = (flags & ~MLI_LAUNCH_NO_PERSISTENT) if enabled else (flags | MLI_LAUNCH_NO_PERSISTENT)
+    lib().mli_set_launch_flags(flags)
+
+
 def gemm_w8a8_cuda_core(y, xq, xs, w_q, w_s, m: int, n: int, d: int, group_size: int = 64, stream=None):
     check(lib().mli_gemm_w8a8_cuda_core(_ptr(y), _ptr(xq), _ptr(xs), _ptr(w_q), _ptr(w_s), m, n, d,
                                         group_size, _stream(stream)), "gemm_w8a8_cuda_core")

@@ -254,6 +254,70 @@ def test_gemm_split_k_cluster_and_workspace_paths(m, n, d):
     assert ops.device_error() == 0
 
 
+@pytest.mark.parametrize("m", [16, 64, 128, 256])
+@pytest.mark.parametrize("pattern", ["max", "min", "mixed"])
+def test_gemm_extreme_int8_operands(m, pattern):
+    """Group dots at the ends of the int8 range: all -128 x -128 (I = 2^20),
+    -128 x 127 (I = -1,040,384) and random bytes over the full range, with
+    unit scales (every output an exact integer) and with random scales; the
+    offset-MMA path (128-token tiles) and the refill path agree with the
+    oracle exactly on the integer case."""
+    n, d = 1024, 256
+    rng = np.random.default_rng(5 + m)
+    if pattern == "max":
+        xq_h = np.full((m, n), -128, np.int8)
+        wq_h = np.full((d, n), -128, np.int8)
+    elif pattern == "min":
+        xq_h = np.full((m, n), -128, np.int8)
+        wq_h = np.full((d, n), 127, np.int8)
+    else:
+        xq_h = rng.integers(-128, 128, (m, n), dtype=np.int16).astype(np.int8)
+        wq_h = rng.integers(-128, 128, (d, n), dtype=np.int16).astype(np.int8)
+    for scales in ("unit", "random"):
+        if scales == "unit":
+            xs_h = np.ones(m, np.float32)
+            ws_h = np.ones((d, n // 64), np.float32)
+        else:
+            xs_h = rng.uniform(1e-4, 1e-1, m).astype(np.float32)
+            ws_h = rng.uniform(1e-5, 1e-2, (d, n // 64)).astype(np.float32)
+        y = Guarded(m * d)
+        ops.gemm_w8a8(y.t, up(xq_h), up(xs_h), up(wq_h), up(ws_h), m, n, d, 64)
+        torch.cuda.synchronize()
+        got = y.check().reshape(m, d)
+        for t in sorted({0, m // 2, m - 1}):
+            ref = orc.gemv_w8a8_f64(xq_h[t], xs_h[t:t + 1], wq_h, ws_h)
+            if scales == "unit":  # sums of 16 integers of magnitude <= 2^20: exact in fp32
+                assert np.array_equal(got[t].astype(np.float64), ref), (t, scales)
+            else:
+                assert orc.max_abs_rel(got[t], ref) <= TOL_W8A8, (t, scales)
+    assert ops.device_error() == 0
+
+
+def test_gemm_group_scale_range():
+    """128-token tiles take the group scale as ws * 2^90: exact up to 2^38
+    (checked at 2^37), refused through the device error word (code 5) at
+    2^40."""
+    m, n, d = 128, 1024, 128
+    rng = np.random.default_rng(11)
+    xq_h = rng.integers(-127, 128, (m, n), dtype=np.int16).astype(np.int8)
+    wq_h = rng.integers(-127, 128, (d, n), dtype=np.int16).astype(np.int8)
+    xs_h = rng.uniform(1e-3, 1e-2, m).astype(np.float32)
+    ws_h = rng.uniform(1e-4, 1e-3, (d, n // 64)).astype(np.float32)
+    ws_h[3, 5] = 2.0 ** 37
+    y = torch.empty(m * d, dtype=torch.float32, device=dev())
+    ops.gemm_w8a8(y, up(xq_h), up(xs_h), up(wq_h), up(ws_h), m, n, d, 64)
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    got = y.cpu().numpy().reshape(m, d)
+    for t in (0, 77, 127):
+        ref = orc.gemv_w8a8_f64(xq_h[t], xs_h[t:t + 1], wq_h, ws_h)
+        assert orc.max_abs_rel(got[t], ref) <= TOL_W8A8, t
+    ws_h[3, 5] = 2.0 ** 40
+    ops.gemm_w8a8(y, up(xq_h), up(xs_h), up(wq_h), up(ws_h), m, n, d, 64)
+    torch.cuda.synchronize()
+    assert ops.device_error() == 5
+
+
 @pytest.mark.parametrize("m,n,d", [(16, 3072, 1024), (256, 3072, 1024), (256, 8192, 3072), (64, 2048, 8192)])
 def test_gemm_plan_is_consistent(m, n, d):
     """mli_gemm_w8a8's plan on this GPU: K splits within [1, K chunks / 2],
@@ -316,6 +380,84 @@ def test_gemm_w8a8_group_parity(m, shapes):
     torch.cuda.synchronize()
     for o, f, (_, _, _, _, _, n, d) in zip(outs, firsts, items):
         assert np.array_equal(o.cpu().numpy().reshape(m, d).view(np.uint32), f.view(np.uint32))
+    assert ops.device_error() == 0
+
+
+def _layer_items(shapes, m, seed):
+    items = []
+    for i, (d, n) in enumerate(shapes):
+        q, s = synth.weights_torch(d, n, seed=seed + i, device=dev())
+        x = synth.activation_gpu(n, seed + 50 + i, dev(), m=m, outliers=True)
+        xq = torch.empty((m, n), dtype=torch.int8, device=dev())
+        xs = torch.empty(m, dtype=torch.float32, device=dev())
+        ops.quantize_activation_rows(xq, xs, x, m, n)
+        items.append((Guarded(m * d), xq, xs, q, s, n, d))
+    return items
+
+
+def _check_items(items, m, got):
+    for (y, xq, xs, q, s, n, d), yn in zip(items, got):
+        xq_h, xs_h, q_h, s_h = xq.cpu().numpy(), xs.cpu().numpy(), q.cpu().numpy(), s.cpu().numpy()
+        for t in sorted({0, 1, m // 2, m - 1}):
+            ref = orc.gemv_w8a8_f64(xq_h[t], xs_h[t:t + 1], q_h, s_h)
+            assert orc.max_abs_rel(yn[t], ref) <= TOL_W8A8, (d, n, t)
+
+
+# (d, n) sets with enough 128 x 128 output tiles for the persistent kernel:
+# the Llama-3.2-3B projections of one layer, and ragged rows and tokens
+# (partial last row tile and token tile, K of 8 to 24 chunks).
+PERSISTENT_CASES = [
+    (256, [(d, n) for (_, d, n) in synth.LLAMA_3B]),
+    (300, [(d, n) for (_, d, n) in synth.LLAMA_3B]),
+    (500, [(3000, 3072), (8100, 3072), (1000, 1024)]),
+]
+
+
+@pytest.mark.parametrize("m,shapes", PERSISTENT_CASES)
+def test_gemm_persistent_group_parity(m, shapes):
+    """mli_gemm_w8a8_group takes the persistent whole-tile kernel for these
+    problems; sampled tokens of every matrix match the oracle, a second launch
+    gives the same bits, and the split-K kernels agree within the tolerance."""
+    items = _layer_items(shapes, m, 700)
+    args = [(y.t, xq, xs, q, s, n, d) for (y, xq, xs, q, s, n, d) in items]
+    plan = ops.gemm_group_plan(args, m)
+    assert plan["persistent"], plan
+    assert plan["ctas"] == min(plan["tiles"], torch.cuda.get_device_properties(0).multi_processor_count)
+    ops.gemm_w8a8_group(args, m)
+    torch.cuda.synchronize()
+    got = [y.check().reshape(m, d) for (y, _, _, _, _, n, d) in items]
+    _check_items(items, m, got)
+    again = [torch.empty(m * d, dtype=torch.float32, device=dev()) for (_, _, _, _, _, n, d) in items]
+    ops.gemm_w8a8_group([(o,) + a[1:] for o, a in zip(again, args)], m)
+    torch.cuda.synchronize()
+    for o, g in zip(again, got):
+        assert np.array_equal(o.cpu().numpy().reshape(g.shape).view(np.uint32), g.view(np.uint32))
+    try:
+        ops.set_gemm_persistent(False)
+        assert not ops.gemm_group_plan(args, m)["persistent"]
+        ops.gemm_w8a8_group([(o,) + a[1:] for o, a in zip(again, args)], m)
+        torch.cuda.synchronize()
+    finally:
+        ops.set_gemm_persistent(True)
+    for o, g in zip(again, got):
+        sk = o.cpu().numpy().reshape(g.shape)
+        for t in (0, m - 1):
+            assert orc.max_abs_rel(sk[t], g[t]) <= TOL_W8A8
+    assert ops.device_error() == 0
+
+
+def test_gemm_persistent_single_matrix():
+    """mli_gemm_w8a8 on one matrix with enough tiles (8192 x 3072 at 512
+    tokens: 256 tiles) runs on the persistent kernel too; at 256 tokens (128
+    tiles, fewer than the SMs) it takes the split-K kernels."""
+    m = 512
+    items = _layer_items([(8192, 3072)], m, 900)
+    y, xq, xs, q, s, n, d = items[0]
+    assert ops.gemm_group_plan([(y.t, xq, xs, q, s, n, d)], m)["persistent"]
+    assert not ops.gemm_group_plan([(y.t, xq[:256], xs[:256], q, s, n, d)], 256)["persistent"]
+    ops.gemm_w8a8(y.t, xq, xs, q, s, m, n, d, 64)
+    torch.cuda.synchronize()
+    _check_items(items, m, [y.check().reshape(m, d)])
     assert ops.device_error() == 0
 
 
