@@ -740,6 +740,72 @@ def classifier_measure(args, device, rank, world, form, allgather="p2p", sampler
 # ---------------------------------------------------------------------------
 # the Llama-3.2-1B FFN blocks, row-sharded over the ranks
 # ---------------------------------------------------------------------------
+def ffn_chain_measure(args, device, rank, world, form, layers=16):
+    """The 16 FFN blocks of a Llama-3.2-1B decode step as a stack (layer l+1
+    reads layer l's output), row-sharded over the ranks in ONE chained launch
+    per step on every rank: each rank's gate/up (SwiGLU, 8192/G rows) and down
+    (2048/G rows) store their rows, tagged with the launch, into every rank's
+    copy of hb / x' over NVLink inside the kernel (mli_chain_create_sharded);
+    no NCCL call.  Total work is fixed (strong scaling).  Every layer's hb and
+    the last x' are checked bit for bit against the same stack on one GPU."""
+    import numpy as np
+
+    from minillama_infra_b200.shard import ChainShardedFFN, row_shard
+
+    dim, hidden = 2048, 8192
+    hs, ds = row_shard(hidden, world, rank), row_shard(dim, world, rank)
+    full, mine = [], []
+    for l in range(layers):
+        g = synth.weights_torch(hidden, dim, seed=2000 * l + 4, device=device)
+        u = synth.weights_torch(hidden, dim, seed=2000 * l + 5, device=device)
+        d = synth.weights_torch(dim, hidden, seed=2000 * l + 6, device=device)
+        full.append((g[0], g[1], u[0], u[1], d[0], d[1]))
+        mine.append((g[0][hs.r0:hs.r1].clone(), g[1][hs.r0:hs.r1].clone(), u[0][hs.r0:hs.r1].clone(),
+                     u[1][hs.r0:hs.r1].clone(), d[0][ds.r0:ds.r1].clone(), d[1][ds.r0:ds.r1].clone()))
+    x0 = synth.activation_gpu(dim, 990, device, outliers=(form == "w8a8"))
+    one = ChainShardedFFN(full, x0, dim, hidden, 0, 1, form=form)
+    one.run()
+    torch.cuda.synchronize()
+    want = [one.hidden_rows(l)[0].view(np.uint32) for l in range(layers)] + [one.output_rows()[0].view(np.uint32)]
+    one.close()
+    del one, full
+    torch.cuda.empty_cache()
+
+    def exchange(h):
+        out = [None] * world
+        dist.all_gather_object(out, h)
+        return out
+
+    sh = ChainShardedFFN(mine, x0, dim, hidden, rank, world, form=form, exchange=exchange if world > 1 else None)
+    barrier(world)
+    stream = torch.cuda.Stream(device)
+    g = graph_of(lambda: sh.run(stream), stream)
+    ms = time_graph(g, args.ffn_steps, args.warmup, stream, world, device)
+    del g
+    torch.cuda.synchronize()
+    barrier(world)  # every rank's last run has landed everywhere
+    got = [sh.hidden_rows(l) for l in range(layers)] + [sh.output_rows()]
+    ok = all(t and np.array_equal(v.view(np.uint32), w) for (v, t), w in zip(got, want))
+    barrier(world)
+    sh.close()
+    okt = torch.tensor([1 if ok else 0], device=device)
+    if world > 1:
+        dist.all_reduce(okt, op=dist.ReduceOp.MIN)
+    bytes_step = layers * (2 * synth.gemv_bytes(hidden, dim) + synth.gemv_bytes(dim, hidden))
+    peak, _ = measured_peaks()
+    return {
+        "form": form, "gpus": world, "layers": layers,
+        "ms_per_step": round(ms, 5), "us_per_layer": round(ms * 1e3 / layers, 2),
+        "GB/s": round(bytes_step / (ms * 1e-3) / 1e9, 1),
+        "per_gpu_frac_of_hbm_peak": round(bytes_step / world / (ms * 1e-3) / 1e9 / peak, 4),
+        "exchange": "tagged peer stores of hb and x' rows inside one chained launch per step (no NCCL)"
+                    if world > 1 else "none (one GPU)",
+        "dependencies": "layer l+1 reads layer l's x'; down reads every rank's hb rows",
+        "bytes_per_step": bytes_step, "launches_per_step": 1,
+        "check": {"every_hb_and_last_x_bit_exact_vs_1gpu_stack": bool(okt.item())},
+    }
+
+
 def ffn_measure(args, device, rank, world, form, layers=16, sampler=None):
     """The 16 FFN blocks of a Llama-3.2-1B decode step row-sharded over the
     ranks (gate/up: 8192/G rows with SwiGLU, NCCL all-gather of hb; down:
@@ -1159,6 +1225,8 @@ def main():
                                            for f in ("w8a32", "w8a8")}
         if "ffn" in extras:
             line["ffn_rowshard"] = {f: ffn_measure(args, device, rank, world, f) for f in ("w8a32", "w8a8")}
+            line["ffn_chain_rowshard"] = {f: ffn_chain_measure(args, device, rank, world, f)
+                                          for f in ("w8a32", "w8a8")}
         if "gemm3b" in extras:
             peak = int8_peak_measure(device)
             line["gemm3b"] = {f"m{m}": gemm3b_measure(args, device, rank, world, m, modes=("group", "per_call"),

@@ -172,16 +172,46 @@ typedef struct mli_chain mli_chain; /* opaque */
 
 /* Plans a chain of `count` GEMVs of one form for the current device: checks
  * every op (MLI_ERR_INVALID_ARG / MLI_ERR_UNSUPPORTED as the single calls
- * would; n % 256 == 0, 16-byte aligned x/xq, w_q, w_s), allocates a small
- * device block (the op table and one counter per op) and copies the table
- * with synchronous runtime calls: make it before any stream capture.  The
- * op's pointers are baked in; the buffers they name must outlive the chain. */
+ * would; n % 256 == 0, 16-byte aligned x/xq, w_q, w_s), allocates two small
+ * device blocks (the op table, and the mirrors: the rows of every op a later
+ * op reads, as 8-byte {value, tag} words) and copies the table with
+ * synchronous runtime calls: make it before any stream capture.  The op's
+ * pointers are baked in; the buffers they name must outlive the chain. */
 int mli_chain_create(const mli_gemv_op* ops, int count, mli_chain** chain);
+
+/* A chain whose GEMVs are row-sharded over `world` ranks (one process per
+ * GPU, 1 <= world <= 8; every rank creates the same op list with its own
+ * rows): op i computes rows [row_offset[i], row_offset[i] + d) of a GEMV of
+ * d_total[i] rows, its y pointing at the first of them.  An op whose x is
+ * the whole vector (the buffer at y - row_offset of an earlier op, with
+ * n == d_total) reads every rank's rows of it: each rank stores the rows it
+ * computes, tagged with the launch, into every rank's mirror over NVLink
+ * (plain peer stores), and readers check the tags -- no collective, no fence.
+ * Mirrors are kept twice, alternating by launch, so a rank may run one launch
+ * ahead of another; every launch must read rows of every rank (an FFN block:
+ * down reads all of hb), else a rank two launches ahead would overwrite rows
+ * still being read (the reader then times out with device error 4).  Ranks
+ * must run their chains the same number of times.  Before the first run:
+ * mli_chain_export on every rank, mli_peer_open of the other ranks' handles,
+ * mli_chain_set_peers. */
+int mli_chain_create_sharded(const mli_gemv_op* ops, const int* row_offset, const int* d_total,
+                             int count, int world, mli_chain** chain);
+/* The CUDA IPC handle (64 bytes) of the chain's mirror block. */
+int mli_chain_export(mli_chain* chain, unsigned char* ipc_handle);
+/* Every rank's mirror block in this process (peer_mirrors[r] from
+ * mli_peer_open of rank r's handle; the own entry, index `rank`, is ignored). */
+int mli_chain_set_peers(mli_chain* chain, void* const* peer_mirrors, int rank);
+/* Synchronous: the whole rows (d_total floats) of op `op` from the chain's
+ * last run, read from this rank's mirror (every rank's rows of a sharded op);
+ * *complete = 1 when every row carries that run's tag.  For ops some later op
+ * reads (others have no mirror: MLI_ERR_INVALID_ARG). */
+int mli_chain_rows(mli_chain* chain, int op, float* out, int* complete);
 
 /* Runs the whole chain as one cooperative launch (one CTA per SM) on
  * `stream`: every op's y is bit-identical to its single call.  A chain's runs
- * must not overlap on the GPU (they share the counters); run it in one stream
- * order.  Must be called with the chain's device current. */
+ * must not overlap on the GPU (they share the mirrors); run it in one stream
+ * order.  Must be called with the chain's device current (and, for a sharded
+ * chain, after mli_chain_set_peers). */
 int mli_chain_run(mli_chain* chain, void* stream);
 
 /* Frees the chain's device block (synchronising like cudaFree). */

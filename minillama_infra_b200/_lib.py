@@ -76,6 +76,10 @@ SIGNATURES = {
     "mli_argmax": (_I, [_P, _I, _P, _P]),
     "mli_gemv_f32": (_I, [_P, _P, _P, _I, _I, _P]),
     "mli_chain_create": (_I, [_OPS, _I, ctypes.POINTER(_P)]),
+    "mli_chain_create_sharded": (_I, [_OPS, ctypes.POINTER(_I), ctypes.POINTER(_I), _I, _I, ctypes.POINTER(_P)]),
+    "mli_chain_export": (_I, [_P, ctypes.c_char_p]),
+    "mli_chain_set_peers": (_I, [_P, ctypes.POINTER(_P), _I]),
+    "mli_chain_rows": (_I, [_P, _I, _P, ctypes.POINTER(_I)]),
     "mli_chain_run": (_I, [_P, _P]),
     "mli_chain_destroy": (_I, [_P]),
     "mli_debug_plan_chain": (_I, [_OPS, _I, _I, _I, ctypes.POINTER(_I)]),

@@ -53,6 +53,7 @@
 //    finish advances the launch sequence, so the next launch (or graph
 //    replay) needs no host-side reset and never takes an old row for a new
 //    one.
+#include <algorithm>
 #include <cstdlib>
 #include <cstring>
 #include <vector>
@@ -72,7 +73,10 @@ constexpr int kMaxRing = 6;
 constexpr int kHeader = 256;
 constexpr int kMaxSlices = 8;
 constexpr int kMaxOps = 1 << 16;
-constexpr unsigned kSeqPeriod = 65535;  // the launch sequence runs 1 .. 65535
+// The launch sequence runs 1 .. 65534: an even period, so consecutive launches
+// always alternate between the two halves of a sharded chain's mirrors.
+constexpr unsigned kSeqPeriod = 65534;
+constexpr int kMaxPeers = 8;  // ranks of a sharded chain
 
 // Row epilogues: store y = v; add into y (the residual adds after the
 // reference's o and down projections, src/model_cuda_v2_shared.cu:99-118,
@@ -81,7 +85,7 @@ constexpr unsigned kSeqPeriod = 65535;  // the launch sequence runs 1 .. 65535
 // op of a SwiGLU pair (no units of its own).
 constexpr int kEpiStore = 0, kEpiAdd = 1, kEpiSwiglu = 2, kEpiCompanion = 3;
 
-// Device-side descriptor of one GEMV of the chain, 96 bytes (geometry
+// Device-side descriptor of one GEMV of the chain, 112 bytes (geometry
 // precomputed on the host, as plan_stream does for the single-GEMV kernel).
 // Kernels copy the table into shared memory when it fits.
 struct Op {
@@ -103,14 +107,16 @@ struct Op {
   uint8_t S;             // slices per row
   uint8_t epi;           // kEpi*: how a finished row is stored
   uint16_t R;            // rows per stage (a SwiGLU stage: R/2 gate rows, then the R/2 up rows)
-  uint32_t pad;
+  int row_off;           // row of the whole (row-sharded) GEMV this op's row 0 is
+  int d_total;           // rows of the whole GEMV: the length of this op's mirror
+  int pad[3];
   __host__ __device__ const float* x() const { return static_cast<const float*>(act); }
   // output rows per work unit
   __host__ __device__ int Ru() const { return epi == kEpiSwiglu ? R / 2 : R; }
   __host__ __device__ const int8_t* xq() const { return static_cast<const int8_t*>(act); }
   __host__ __device__ int G() const { return n / kGroup; }
 };
-static_assert(sizeof(Op) == 96, "chain op descriptor is 96 bytes");
+static_assert(sizeof(Op) == 112 && sizeof(Op) % 16 == 0, "chain op descriptor: 112 bytes, copied as uint4s");
 
 struct Args {
   const Op* ops;        // global copy of the table
@@ -121,7 +127,10 @@ struct Args {
   int count;
   int n_polls;
   int units;            // stages of all ops
-  uint64_t* mirror;     // every op's rows as {value, tag} words
+  uint64_t* mirror;     // every op's rows as {value, tag} words (this rank's block)
+  uint64_t* const* peers;  // sharded chains: every rank's mirror block (the own one included)
+  int world;            // ranks of a sharded chain (1: rows stay on this GPU)
+  uint32_t mirror_half; // words from a mirror to its copy for odd launches (0: one copy)
   unsigned* seq;        // launch sequence, 1 .. kSeqPeriod (advanced by the last CTA)
   unsigned* finished;   // CTAs finished in this launch
   int ring;
@@ -165,12 +174,20 @@ __host__ __device__ __forceinline__ uint32_t row_tag(unsigned seq, int op) {
   return (seq << 16) | static_cast<uint32_t>(op & 0xffff);
 }
 
-__device__ __forceinline__ void ld_relaxed_v2(const uint64_t* p, uint64_t& a, uint64_t& b) {
-  asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+// Mirror words are read with GPU-scope relaxed loads, or system-scope ones
+// when other GPUs write them (a sharded chain).
+__device__ __forceinline__ void ld_relaxed_v2(const uint64_t* p, uint64_t& a, uint64_t& b, bool sys) {
+  if (sys)
+    asm volatile("ld.relaxed.sys.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+  else
+    asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
-__device__ __forceinline__ uint64_t ld_relaxed_b64(const uint64_t* p) {
+__device__ __forceinline__ uint64_t ld_relaxed_b64(const uint64_t* p, bool sys) {
   uint64_t v;
-  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  if (sys)
+    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  else
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 __device__ __forceinline__ void st_relaxed_b64(uint64_t* p, uint64_t v) {
@@ -270,6 +287,11 @@ __device__ __forceinline__ void issue_unit(const Args& a, const Op* ops, unsigne
   }
 }
 
+// Offset of this launch's copy of the mirrors (sharded chains keep two,
+// alternating by launch, so that a rank already in the next launch never
+// overwrites words another rank is still reading).
+__device__ __forceinline__ uint32_t mirror_half(const Args& a, unsigned seq) { return (seq & 1u) ? a.mirror_half : 0u; }
+
 // Consumer threads check, by their mirrors' tags, that every row of the ops
 // polls[first, first + count) was written in this launch.  False if a row did
 // not arrive in time.
@@ -281,18 +303,19 @@ __device__ __forceinline__ bool poll_ops(const Args& a, const Op* ops, const int
     const int j = polls[p];
     const Op& q = ops[j];
     const uint32_t tag = row_tag(seq, j);
-    const uint64_t* m = a.mirror + q.mirror;
-    for (int r0 = threadIdx.x; r0 < q.d; r0 += 8 * kT) {
+    const uint64_t* m = a.mirror + mirror_half(a, seq) + q.mirror;
+    const bool sys = a.world > 1;
+    for (int r0 = threadIdx.x; r0 < q.d_total; r0 += 8 * kT) {
       unsigned pending = 0;
 #pragma unroll
       for (int k = 0; k < 8; ++k)
-        if (r0 + k * kT < q.d) pending |= 1u << k;
+        if (r0 + k * kT < q.d_total) pending |= 1u << k;
       unsigned ns = 32;
       while (true) {
         uint64_t w[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k)
-          if ((pending >> k) & 1u) w[k] = ld_relaxed_b64(m + r0 + k * kT);
+          if ((pending >> k) & 1u) w[k] = ld_relaxed_b64(m + r0 + k * kT, sys);
 #pragma unroll
         for (int k = 0; k < 8; ++k)
           if (((pending >> k) & 1u) && has_tag(w[k], tag)) pending &= ~(1u << k);
@@ -315,7 +338,8 @@ constexpr int kPre = 8;  // float4 of activation held per consumer thread
 // Shared preparation: consumer thread t holds columns 4t + 4 kT j, j < kPre
 // (the whole activation for n <= 4 kT kPre).  False on a timeout.
 template <int kT>
-__device__ __forceinline__ bool cta_x_load(const Op& op, const uint64_t* m, uint32_t tag, float4 (&v)[kPre]) {
+__device__ __forceinline__ bool cta_x_load(const Op& op, const uint64_t* m, uint32_t tag, bool sys,
+                                           float4 (&v)[kPre]) {
   const int t = static_cast<int>(threadIdx.x);
   const int n = op.n;
   if (m == nullptr) {
@@ -338,11 +362,11 @@ __device__ __forceinline__ bool cta_x_load(const Op& op, const uint64_t* m, uint
     unsigned ns = 32;
     while (true) {
       uint64_t a0, a1, a2, a3, b0 = 0, b1 = 0, b2 = 0, b3 = 0;
-      ld_relaxed_v2(m + c0, a0, a1);
-      ld_relaxed_v2(m + c0 + 2, a2, a3);
+      ld_relaxed_v2(m + c0, a0, a1, sys);
+      ld_relaxed_v2(m + c0 + 2, a2, a3, sys);
       if (two) {
-        ld_relaxed_v2(m + c1, b0, b1);
-        ld_relaxed_v2(m + c1 + 2, b2, b3);
+        ld_relaxed_v2(m + c1, b0, b1, sys);
+        ld_relaxed_v2(m + c1 + 2, b2, b3, sys);
       }
       if (all_tagged4(a0, a1, a2, a3, tag) && (!two || all_tagged4(b0, b1, b2, b3, tag))) {
         v[j] = make_float4(word_value(a0), word_value(a1), word_value(a2), word_value(a3));
@@ -445,7 +469,7 @@ __device__ __forceinline__ float cta_quant(const float4 (&v)[kPre], const float*
 // Per-warp preparation (W8A32, when no two warps share a slice): the lane's
 // chunks k = 0, 1 of its slice, 16 columns each at col0 + 512k, as
 // v[4k + j] = columns col0 + 512k + 4j .. + 3.  False on a timeout.
-__device__ __forceinline__ bool warp_x_load(const Op& op, const uint64_t* m, uint32_t tag, int col0,
+__device__ __forceinline__ bool warp_x_load(const Op& op, const uint64_t* m, uint32_t tag, bool sys, int col0,
                                             unsigned vmask, float4 (&v)[kPre]) {
   if (m == nullptr) {
 #pragma unroll
@@ -469,10 +493,10 @@ __device__ __forceinline__ bool warp_x_load(const Op& op, const uint64_t* m, uin
     unsigned ns = 32;
     while (true) {
       uint64_t a0, a1, a2, a3, b0, b1, b2, b3;
-      ld_relaxed_v2(p0, a0, a1);
-      ld_relaxed_v2(p0 + 2, a2, a3);
-      ld_relaxed_v2(p1, b0, b1);
-      ld_relaxed_v2(p1 + 2, b2, b3);
+      ld_relaxed_v2(p0, a0, a1, sys);
+      ld_relaxed_v2(p0 + 2, a2, a3, sys);
+      ld_relaxed_v2(p1, b0, b1, sys);
+      ld_relaxed_v2(p1 + 2, b2, b3, sys);
       if (all_tagged4(a0, a1, a2, a3, tag) && all_tagged4(b0, b1, b2, b3, tag)) {
         v[q] = make_float4(word_value(a0), word_value(a1), word_value(a2), word_value(a3));
         v[q + 1] = make_float4(word_value(b0), word_value(b1), word_value(b2), word_value(b3));
@@ -542,10 +566,10 @@ __device__ __forceinline__ void warp_digits(const float4 (&v)[kPre], unsigned vm
 // or the fused W8A8 int8 copy (its scale into *xscale).  All consumer threads
 // call it.  False (on every thread) when an input row did not arrive in time.
 template <Form F, int kT>
-__device__ __forceinline__ bool prep_cta(const Op& op, const uint64_t* m, uint32_t tag, unsigned char* xregion,
-                                      float* red, float* red2, float* xscale) {
+__device__ __forceinline__ bool prep_cta(const Op& op, const uint64_t* m, uint32_t tag, bool sys,
+                                         unsigned char* xregion, float* red, float* red2, float* xscale) {
   float4 pre[kPre];
-  bool fail = !cta_x_load<kT>(op, m, tag, pre);
+  bool fail = !cta_x_load<kT>(op, m, tag, sys, pre);
   fail = named_sync_or<kT>(fail);  // also: every consumer is done reading the shared region
   if (fail) return false;
   const int n = op.n;
@@ -609,7 +633,8 @@ __global__ void __launch_bounds__((kW + 1) * 32, 1) gemv_chain_kernel(const Args
   if (a.table_off != 0) {
     const uint4* src = reinterpret_cast<const uint4*>(a.ops);
     uint4* dst = reinterpret_cast<uint4*>(smem + a.table_off);
-    for (int i = threadIdx.x; i < a.count * 6; i += blockDim.x) dst[i] = __ldg(src + i);
+    constexpr int kOpVecs = static_cast<int>(sizeof(Op) / sizeof(uint4));
+    for (int i = threadIdx.x; i < a.count * kOpVecs; i += blockDim.x) dst[i] = __ldg(src + i);
     int* pdst = reinterpret_cast<int*>(smem + a.table_off + sizeof(Op) * a.count);
     for (int i = threadIdx.x; i <= a.n_phases; i += blockDim.x) pdst[i] = __ldg(a.phases + i);
     for (int i = threadIdx.x; i < a.n_polls; i += blockDim.x) pdst[a.n_phases + 1 + i] = __ldg(a.polls + i);
@@ -684,7 +709,8 @@ __global__ void __launch_bounds__((kW + 1) * 32, 1) gemv_chain_kernel(const Args
           S = op.S; sl = role.sl; wj = role.wj; warp_on = role.on; vmask = role.vmask;
           const int col0 = role.col0;
           // (a broken CTA reads the activation as it stands, without waiting)
-          const uint64_t* src_m = op.src >= 0 && !broken ? a.mirror + ops[op.src].mirror : nullptr;
+          const uint64_t* src_m =
+              op.src >= 0 && !broken ? a.mirror + mirror_half(a, seq) + ops[op.src].mirror : nullptr;
           const uint32_t src_tag = row_tag(seq, op.src);
           if constexpr (F == Form::kW8A8) {
             xscale = __ldcg(op.xs);
@@ -696,11 +722,12 @@ __global__ void __launch_bounds__((kW + 1) * 32, 1) gemv_chain_kernel(const Args
           } else if (F == Form::kW8A32 && op.S == kW && op.norm_w == nullptr) {
             // every warp owns its slice: prepare it in registers, no barrier
             float4 pre[kPre];
-            if (!warp_x_load(op, src_m, src_tag, col0, vmask, pre)) fail = true;
+            if (!warp_x_load(op, src_m, src_tag, a.world > 1, col0, vmask, pre)) fail = true;
             if constexpr (F == Form::kW8A32) warp_digits(pre, vmask, xd, fac);
           } else {
             float t_scale = 0.f;
-            if (!prep_cta<F, kT>(op, src_m, src_tag, smem + a.x_off, sm.red, sm.red2, &t_scale)) fail = true;
+            if (!prep_cta<F, kT>(op, src_m, src_tag, a.world > 1, smem + a.x_off, sm.red, sm.red2, &t_scale))
+              fail = true;
             xscale = t_scale;
             if constexpr (F == Form::kW8A32) {
               const int8_t* planes = reinterpret_cast<const int8_t*>(smem + a.x_off);
@@ -776,9 +803,14 @@ __global__ void __launch_bounds__((kW + 1) * 32, 1) gemv_chain_kernel(const Args
           // the op's mirror and the ADD base, from the table (kept out of the
           // registers of the row loop)
           const Op& op = ops[o];
-          uint64_t* my_mirror = op.mirror >= 0 ? a.mirror + op.mirror : nullptr;
+          // rows r of the op are words row_off + r of its mirror (the whole GEMV's rows)
+          const uint32_t half = mirror_half(a, seq);
+          const size_t my_off = op.mirror >= 0 ? half + op.mirror + op.row_off : 0;
+          const bool share = a.world > 1;
+          uint64_t* my_mirror = op.mirror >= 0 ? a.mirror + my_off : nullptr;
           const uint32_t my_tag = row_tag(seq, o);
-          const uint64_t* base_mirror = op.base >= 0 ? a.mirror + ops[op.base].mirror : nullptr;
+          const uint64_t* base_mirror =
+              op.base >= 0 ? a.mirror + half + ops[op.base].mirror + op.row_off : nullptr;
           const uint32_t base_tag = row_tag(seq, op.base);
           bool late = false;
           const uint64_t t0 = global_timer_ns();
@@ -794,12 +826,12 @@ __global__ void __launch_bounds__((kW + 1) * 32, 1) gemv_chain_kernel(const Args
             } else if (kEpi && epi == kEpiAdd) {
               float b;
               if (base_mirror != nullptr && !*sm.broken) {
-                uint64_t w = ld_relaxed_b64(base_mirror + row0 + rr);
+                uint64_t w = ld_relaxed_b64(base_mirror + row0 + rr, share);
                 unsigned ns = 32;
                 while (!has_tag(w, base_tag) && !late) {
                   late = global_timer_ns() - t0 > kWaitLimitNs;
                   poll_backoff(ns);
-                  w = ld_relaxed_b64(base_mirror + row0 + rr);
+                  w = ld_relaxed_b64(base_mirror + row0 + rr, share);
                 }
                 b = word_value(w);
               } else {
@@ -808,7 +840,16 @@ __global__ void __launch_bounds__((kW + 1) * 32, 1) gemv_chain_kernel(const Args
               v = b + v;
             }
             y[row0 + rr] = v;
-            if (my_mirror != nullptr) st_relaxed_b64(my_mirror + row0 + rr, tagged(v, my_tag));
+            if (my_mirror != nullptr) {
+              const uint64_t w = tagged(v, my_tag);
+              if (share) {
+                // every rank's mirror, over NVLink (plain peer stores)
+                for (int pr = 0; pr < a.world; ++pr)
+                  st_relaxed_sys_b64(reinterpret_cast<unsigned long long*>(a.peers[pr] + my_off + row0 + rr), w);
+              } else {
+                st_relaxed_b64(my_mirror + row0 + rr, w);
+              }
+            }
           }
           if (late) {
             record_error(a, kDevChainTimeout);
@@ -885,8 +926,13 @@ constexpr int kMaxHeldCols = 4 * 8 * 32 * kPre;
 
 // Validates the op list and lays out the chain.  Returns MLI_OK,
 // MLI_ERR_INVALID_ARG or MLI_ERR_UNSUPPORTED (without touching the device).
+// row_offset / d_total (NULL: 0 / d): op i computes rows [row_offset[i],
+// row_offset[i] + d) of a GEMV of d_total[i] rows, its y pointing at the first
+// of them; an op reading the whole vector takes the full buffer
+// (y - row_offset) as its x, and its rows arrive through the producer's
+// mirror from every rank.
 int plan_chain(const mli_gemv_op* in, int count, int sm_count, int smem_per_sm, int smem_optin,
-               unsigned flags, Plan* p) {
+               unsigned flags, const int* row_offset, const int* d_total, Plan* p) {
   if (!in || count <= 0 || sm_count <= 0 || smem_optin <= 0 || smem_per_sm <= 0)
     return MLI_ERR_INVALID_ARG;
   if (count > kMaxOps) return MLI_ERR_UNSUPPORTED;
@@ -904,9 +950,13 @@ int plan_chain(const mli_gemv_op* in, int count, int sm_count, int smem_per_sm, 
   long long units = 0;
   size_t slot = 0, xbytes = 0, mirror = 0;
   int part_stride = 0, epoch = -1;
+  auto roff = [&](int i) { return row_offset ? row_offset[i] : 0; };
+  auto dtot = [&](int i) { return d_total ? d_total[i] : in[i].d; };
   for (int i = 0; i < count; ++i) {
     const mli_gemv_op& s = in[i];
     const bool companion = i > 0 && in[i - 1].epilogue == kEpiSwiglu && !is_comp[i - 1];
+    if (roff(i) < 0 || static_cast<long long>(roff(i)) + s.d > dtot(i)) return MLI_ERR_INVALID_ARG;
+    if (companion && (roff(i) != roff(i - 1) || dtot(i) != dtot(i - 1))) return MLI_ERR_INVALID_ARG;
     is_comp[i] = companion;
     if (s.form != form) return MLI_ERR_INVALID_ARG;
     if (s.epilogue < kEpiStore || s.epilogue > kEpiSwiglu) return MLI_ERR_INVALID_ARG;
@@ -939,6 +989,8 @@ int plan_chain(const mli_gemv_op* in, int count, int sm_count, int smem_per_sm, 
     op.norm_w = s.norm_w;
     op.n = s.n;
     op.d = s.d;
+    op.row_off = roff(i);
+    op.d_total = dtot(i);
     const int S = (s.n + slice_cols(f) - 1) / slice_cols(f);
     if (S > kMaxSlices) return MLI_ERR_UNSUPPORTED;
     // the whole vector is prepared in shared memory when some warps share a
@@ -967,11 +1019,11 @@ int plan_chain(const mli_gemv_op* in, int count, int sm_count, int smem_per_sm, 
     op.src = -1;
     if (f != Form::kW8A8) {
       for (int j = i - 1; j >= 0; --j)
-        if (!is_comp[j] && in[j].y == s.x) {
+        if (!is_comp[j] && in[j].y - roff(j) == s.x) {
           op.src = j;
           break;
         }
-      if (op.src >= 0 && (op.src >= s.wait || in[op.src].d != s.n)) return MLI_ERR_INVALID_ARG;
+      if (op.src >= 0 && (op.src >= s.wait || dtot(op.src) != s.n)) return MLI_ERR_INVALID_ARG;
       if (companion) op.src = p->ops[i - 1].src;
     }
     // More columns than the consumers hold: only an input ready at launch,
@@ -986,7 +1038,9 @@ int plan_chain(const mli_gemv_op* in, int count, int sm_count, int smem_per_sm, 
           op.base = j;
           break;
         }
-      if (op.base >= 0 && (op.base >= s.wait || in[op.base].d != s.d)) return MLI_ERR_INVALID_ARG;
+      if (op.base >= 0 && (op.base >= s.wait || in[op.base].d != s.d || roff(op.base) != roff(i) ||
+                           dtot(op.base) != dtot(i)))
+        return MLI_ERR_INVALID_ARG;
     }
     op.mirror = -1;  // assigned below to the ops some later op reads
     // Ops of the wait prefix [0, wait) that must be checked by tag: all but
@@ -1042,10 +1096,13 @@ int plan_chain(const mli_gemv_op* in, int count, int sm_count, int smem_per_sm, 
     if (p->ops[i].base >= 0) read[p->ops[i].base] = 1;
   }
   for (int j : p->polls) read[j] = 1;
+  // a row-sharded chain keeps every op's whole rows (its outputs are read back
+  // from the mirrors)
+  if (row_offset) std::fill(read.begin(), read.end(), 1);
   for (int i = 0; i < count; ++i)
     if (read[i] && p->ops[i].epi != kEpiCompanion) {
       p->ops[i].mirror = static_cast<int>(mirror);
-      mirror += align_up(static_cast<size_t>(p->ops[i].d), 2);  // 16-byte aligned runs
+      mirror += align_up(static_cast<size_t>(p->ops[i].d_total), 2);  // 16-byte aligned runs
       if (mirror > (1u << 30)) return MLI_ERR_UNSUPPORTED;
     }
   p->mirror_words = mirror;
@@ -1117,25 +1174,31 @@ struct mli_chain {
   size_t smem;
   int grid;
   int threads;
+  int world;         // ranks the chain's rows are shared with (1: none)
+  bool peers_ready;  // sharded chains: mli_chain_set_peers has run
   mli::chain::KernelFn kernel;
   mli::chain::Args args;
-  void* dev_mem;  // op table, phases, polls, mirrors, then the launch words
+  std::vector<mli::chain::Op> ops;  // host copy of the op table (mirror offsets, row ranges)
+  void* dev_mem;     // op table, phases, polls, peer pointers, then the launch words
+  void* mirror_mem;  // the mirrors (their own allocation, so that other ranks can map them)
+  size_t mirror_bytes;
 };
 
 using namespace mli;
 
-extern "C" {
+namespace {
 
-int mli_chain_create(const mli_gemv_op* ops, int count, mli_chain** chain_out) {
+int chain_create(const mli_gemv_op* ops, const int* row_offset, const int* d_total, int count, int world,
+                 mli_chain** chain_out) {
   if (!chain_out) return set_status(MLI_ERR_INVALID_ARG);
   *chain_out = nullptr;
-  if (!ops || count <= 0) return set_status(MLI_ERR_INVALID_ARG);
+  if (!ops || count <= 0 || world < 1 || world > chain::kMaxPeers) return set_status(MLI_ERR_INVALID_ARG);
   cudaError_t err = cudaSuccess;
   const DeviceInfo& dev = current_device(&err);
   if (err != cudaSuccess) return set_status(MLI_ERR_CUDA, err);
   chain::Plan p;
   const int rc = chain::plan_chain(ops, count, dev.sm_count, dev.smem_per_sm, dev.smem_optin_per_cta,
-                                   launch_flags(), &p);
+                                   launch_flags(), row_offset, d_total, &p);
   if (rc != MLI_OK) return set_status(rc);
   const chain::KernelFn kfn = chain::kernel_for(ops[0].form, p.v);
   const int threads = (p.v.warps + 1) * 32;
@@ -1145,15 +1208,23 @@ int mli_chain_create(const mli_gemv_op* ops, int count, mli_chain** chain_out) {
   err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, threads, p.smem);
   if (err != cudaSuccess) return check_cuda(err);
   if (per_sm < p.v.per_sm) return set_status(MLI_ERR_UNSUPPORTED);
-  // device block: op table | phases | polls | mirrors | launch sequence, finished count
+  // device block: op table | phases | polls | peer pointers | launch sequence, finished count
   const size_t table = chain::align_up(sizeof(chain::Op) * count, 256);
   const size_t phases = chain::align_up(sizeof(int) * p.phases.size(), 256);
   const size_t polls = chain::align_up(sizeof(int) * (p.polls.size() + 1), 256);
-  const size_t mirror = chain::align_up(sizeof(uint64_t) * p.mirror_words, 256);
+  const size_t peers = chain::align_up(sizeof(uint64_t*) * chain::kMaxPeers, 256);
   const size_t words = 256;
+  // mirrors: one copy, or two (alternating by launch) when rows are shared
+  const size_t half_words = chain::align_up(p.mirror_words, 32);
+  const size_t mirror_bytes = chain::align_up(sizeof(uint64_t) * half_words * (world > 1 ? 2 : 1), 256) + 256;
   void* mem = nullptr;
-  err = cudaMalloc(&mem, table + phases + polls + mirror + words);
-  if (err != cudaSuccess) return set_status(MLI_ERR_CUDA, err);
+  void* mir = nullptr;
+  err = cudaMalloc(&mem, table + phases + polls + peers + words);
+  if (err == cudaSuccess) err = cudaMalloc(&mir, mirror_bytes);
+  if (err != cudaSuccess) {
+    if (mem) cudaFree(mem);
+    return set_status(MLI_ERR_CUDA, err);
+  }
   char* base = static_cast<char*>(mem);
   err = cudaMemcpy(base, p.ops.data(), sizeof(chain::Op) * count, cudaMemcpyHostToDevice);
   if (err == cudaSuccess)
@@ -1162,12 +1233,14 @@ int mli_chain_create(const mli_gemv_op* ops, int count, mli_chain** chain_out) {
     err = cudaMemcpy(base + table + phases, p.polls.data(), sizeof(int) * p.polls.size(),
                      cudaMemcpyHostToDevice);
   // zeroed mirrors carry tag 0, which no launch uses; the sequence starts at 1
-  if (err == cudaSuccess) err = cudaMemset(base + table + phases + polls, 0, mirror + words);
+  if (err == cudaSuccess) err = cudaMemset(mir, 0, mirror_bytes);
+  if (err == cudaSuccess) err = cudaMemset(base + table + phases + polls, 0, peers + words);
   const unsigned first_seq = 1;
   if (err == cudaSuccess)
-    err = cudaMemcpy(base + table + phases + polls + mirror, &first_seq, sizeof(first_seq), cudaMemcpyHostToDevice);
+    err = cudaMemcpy(base + table + phases + polls + peers, &first_seq, sizeof(first_seq), cudaMemcpyHostToDevice);
   if (err != cudaSuccess) {
     cudaFree(mem);
+    cudaFree(mir);
     return set_status(MLI_ERR_CUDA, err);
   }
   mli_chain* c = new mli_chain;
@@ -1176,22 +1249,99 @@ int mli_chain_create(const mli_gemv_op* ops, int count, mli_chain** chain_out) {
   c->smem = p.smem;
   c->grid = p.grid;
   c->threads = threads;
+  c->world = world;
+  c->peers_ready = world == 1;
   c->kernel = kfn;
   c->args = p.args;
+  c->ops = p.ops;
   c->args.ops = reinterpret_cast<const chain::Op*>(base);
   c->args.phases = reinterpret_cast<const int*>(base + table);
   c->args.polls = reinterpret_cast<const int*>(base + table + phases);
-  c->args.mirror = reinterpret_cast<uint64_t*>(base + table + phases + polls);
-  c->args.seq = reinterpret_cast<unsigned*>(base + table + phases + polls + mirror);
+  c->args.peers = reinterpret_cast<uint64_t* const*>(base + table + phases + polls);
+  c->args.world = 1;  // rows are shared once every rank's mirror is known
+  c->args.mirror = static_cast<uint64_t*>(mir);
+  c->args.mirror_half = world > 1 ? static_cast<uint32_t>(half_words) : 0u;
+  c->args.seq = reinterpret_cast<unsigned*>(base + table + phases + polls + peers);
   c->args.finished = c->args.seq + 1;
   c->args.err = device_error_word();
   c->dev_mem = mem;
+  c->mirror_mem = mir;
+  c->mirror_bytes = mirror_bytes;
   *chain_out = c;
   return set_status(MLI_OK);
 }
 
+}  // namespace
+
+extern "C" {
+
+int mli_chain_create(const mli_gemv_op* ops, int count, mli_chain** chain_out) {
+  return chain_create(ops, nullptr, nullptr, count, 1, chain_out);
+}
+
+int mli_chain_create_sharded(const mli_gemv_op* ops, const int* row_offset, const int* d_total, int count,
+                             int world, mli_chain** chain_out) {
+  if (!row_offset || !d_total) {
+    if (chain_out) *chain_out = nullptr;
+    return set_status(MLI_ERR_INVALID_ARG);
+  }
+  return chain_create(ops, row_offset, d_total, count, world, chain_out);
+}
+
+int mli_chain_export(mli_chain* chain, unsigned char* ipc_handle) {
+  if (!chain || !ipc_handle) return set_status(MLI_ERR_INVALID_ARG);
+  cudaIpcMemHandle_t h;
+  const cudaError_t err = cudaIpcGetMemHandle(&h, chain->mirror_mem);
+  if (err != cudaSuccess) return set_status(MLI_ERR_CUDA, err);
+  static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+  std::memcpy(ipc_handle, &h, sizeof(h));
+  return set_status(MLI_OK);
+}
+
+int mli_chain_set_peers(mli_chain* chain, void* const* peer_mirrors, int rank) {
+  if (!chain || !peer_mirrors || rank < 0 || rank >= chain->world) return set_status(MLI_ERR_INVALID_ARG);
+  uint64_t* ptrs[chain::kMaxPeers] = {};
+  for (int r = 0; r < chain->world; ++r) {
+    ptrs[r] = r == rank ? static_cast<uint64_t*>(chain->mirror_mem) : static_cast<uint64_t*>(peer_mirrors[r]);
+    if (!ptrs[r]) return set_status(MLI_ERR_INVALID_ARG);
+  }
+  int cur = -1;
+  cudaError_t err = cudaGetDevice(&cur);
+  if (err == cudaSuccess && cur != chain->device) return set_status(MLI_ERR_INVALID_ARG);
+  if (err == cudaSuccess)
+    err = cudaMemcpy(const_cast<uint64_t**>(chain->args.peers), ptrs, sizeof(ptrs), cudaMemcpyHostToDevice);
+  if (err != cudaSuccess) return set_status(MLI_ERR_CUDA, err);
+  chain->args.world = chain->world;
+  chain->peers_ready = true;
+  return set_status(MLI_OK);
+}
+
+int mli_chain_rows(mli_chain* chain, int op, float* out, int* complete) {
+  if (!chain || !out || !complete || op < 0 || op >= static_cast<int>(chain->ops.size()))
+    return set_status(MLI_ERR_INVALID_ARG);
+  const chain::Op& o = chain->ops[op];
+  if (o.mirror < 0) return set_status(MLI_ERR_INVALID_ARG);
+  unsigned seq = 0;
+  cudaError_t err = cudaMemcpy(&seq, chain->args.seq, sizeof(seq), cudaMemcpyDeviceToHost);
+  if (err != cudaSuccess) return set_status(MLI_ERR_CUDA, err);
+  const unsigned last = seq == 1 ? chain::kSeqPeriod : seq - 1;  // the launch that ran last
+  const size_t off = ((last & 1u) ? chain->args.mirror_half : 0u) + static_cast<size_t>(o.mirror);
+  std::vector<uint64_t> w(static_cast<size_t>(o.d_total));
+  err = cudaMemcpy(w.data(), chain->args.mirror + off, sizeof(uint64_t) * w.size(), cudaMemcpyDeviceToHost);
+  if (err != cudaSuccess) return set_status(MLI_ERR_CUDA, err);
+  const uint32_t tag = chain::row_tag(last, op);
+  int ok = 1;
+  for (size_t i = 0; i < w.size(); ++i) {
+    ok &= static_cast<uint32_t>(w[i] >> 32) == tag;
+    const uint32_t bits = static_cast<uint32_t>(w[i]);
+    std::memcpy(out + i, &bits, sizeof(bits));
+  }
+  *complete = ok;
+  return set_status(MLI_OK);
+}
+
 int mli_chain_run(mli_chain* chain, void* stream) {
-  if (!chain) return set_status(MLI_ERR_INVALID_ARG);
+  if (!chain || !chain->peers_ready) return set_status(MLI_ERR_INVALID_ARG);
   int cur = -1;
   cudaError_t err = cudaGetDevice(&cur);
   if (err != cudaSuccess) return set_status(MLI_ERR_CUDA, err);
@@ -1211,7 +1361,9 @@ int mli_chain_run(mli_chain* chain, void* stream) {
 
 int mli_chain_destroy(mli_chain* chain) {
   if (!chain) return set_status(MLI_ERR_INVALID_ARG);
-  const cudaError_t err = cudaFree(chain->dev_mem);
+  cudaError_t err = cudaFree(chain->dev_mem);
+  const cudaError_t err2 = cudaFree(chain->mirror_mem);
+  if (err == cudaSuccess) err = err2;
   delete chain;
   return err == cudaSuccess ? set_status(MLI_OK) : set_status(MLI_ERR_CUDA, err);
 }
@@ -1220,7 +1372,7 @@ int mli_debug_plan_chain(const mli_gemv_op* ops, int count, int sm_count, int sm
                          int* out) {
   if (!out) return set_status(MLI_ERR_INVALID_ARG);
   chain::Plan p;
-  const int rc = chain::plan_chain(ops, count, sm_count, smem_optin + 1024, smem_optin, 0u, &p);
+  const int rc = chain::plan_chain(ops, count, sm_count, smem_optin + 1024, smem_optin, 0u, nullptr, nullptr, &p);
   if (rc != MLI_OK) return set_status(rc);
   out[0] = p.grid;
   out[1] = static_cast<int>(p.smem);

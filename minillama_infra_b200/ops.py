@@ -207,9 +207,17 @@ class GemvChain:
     earlier op takes that op's rows of the same launch; an "add" op adds into
     the latest earlier op's output of the same y.  The buffers must outlive
     the chain; the chain keeps references to the tensors given.
+
+    Row-sharded chains (mli_chain_create_sharded): every op dict may carry
+    "row_offset" and "d_total" (default 0 and d): the op computes rows
+    [row_offset, row_offset + d) of a GEMV of d_total rows, its y pointing at
+    the first of them, and an op whose x is the whole vector (the producer's
+    y - row_offset) reads every rank's rows.  `world` > 1 makes the chain
+    share its rows over NVLink: call export() on every rank, exchange the
+    handles, then set_peers(handles, rank) before the first run.
     """
 
-    def __init__(self, ops, group_size: int = 64):
+    def __init__(self, ops, group_size: int = 64, world: int = 1):
         arr = (GemvOp * len(ops))()
         self._keep = []
         for i, o in enumerate(ops):
@@ -223,8 +231,46 @@ class GemvChain:
                 if t is not None and not isinstance(t, int):
                     self._keep.append(t)
         self.count = len(ops)
+        self.world = world
+        self.d_total = [o.get("d_total", o["d"]) for o in ops]
+        self._peers = []
         self._h = ctypes.c_void_p()
-        check(lib().mli_chain_create(arr, len(ops), ctypes.byref(self._h)), "mli_chain_create")
+        sharded = world > 1 or any("row_offset" in o or "d_total" in o for o in ops)
+        if sharded:
+            roff = (ctypes.c_int * len(ops))(*[o.get("row_offset", 0) for o in ops])
+            dtot = (ctypes.c_int * len(ops))(*self.d_total)
+            check(lib().mli_chain_create_sharded(arr, roff, dtot, len(ops), world, ctypes.byref(self._h)),
+                  "mli_chain_create_sharded")
+        else:
+            check(lib().mli_chain_create(arr, len(ops), ctypes.byref(self._h)), "mli_chain_create")
+
+    def export(self) -> bytes:
+        """The 64-byte CUDA IPC handle of this rank's mirror block."""
+        buf = ctypes.create_string_buffer(64)
+        check(lib().mli_chain_export(self._h, buf), "mli_chain_export")
+        return buf.raw
+
+    def set_peers(self, handles, rank: int) -> None:
+        """handles[r]: rank r's export(); this rank's own entry is not opened."""
+        ptrs = (ctypes.c_void_p * self.world)()
+        for r, h in enumerate(handles):
+            if r == rank:
+                continue
+            p = ctypes.c_void_p()
+            check(lib().mli_peer_open(h, ctypes.byref(p)), "mli_peer_open")
+            self._peers.append(p)
+            ptrs[r] = p.value
+        check(lib().mli_chain_set_peers(self._h, ptrs, rank), "mli_chain_set_peers")
+
+    def rows(self, op: int):
+        """(whole rows of op `op` from the last run as a numpy float32 array,
+        True when every row carries that run's tag); synchronous."""
+        import numpy as np
+
+        out = np.empty(self.d_total[op], np.float32)
+        ok = ctypes.c_int(0)
+        check(lib().mli_chain_rows(self._h, op, out.ctypes.data, ctypes.byref(ok)), "mli_chain_rows")
+        return out, bool(ok.value)
 
     def run(self, stream=None):
         check(lib().mli_chain_run(self._h, _stream(stream)), "mli_chain_run")
@@ -233,6 +279,9 @@ class GemvChain:
         if self._h is not None and self._h.value:
             lib().mli_chain_destroy(self._h)
         self._h = None
+        for p in self._peers:
+            lib().mli_peer_close(p)
+        self._peers = []
         self._keep = []
 
     def __del__(self):

@@ -342,3 +342,80 @@ class ShardedFFN:
         if self._chain is not None:
             self._chain.close()
             self._chain = None
+
+
+class ChainShardedFFN:
+    """A stack of row-sharded Llama FFN blocks as ONE chained launch per step
+    on every rank, with the exchanges between ranks inside the kernel.
+
+    Per layer l (the reference's block, src/model_cuda_v2_shared.cu:408-412
+    W8A32, :551-558 W8A8): hb = silu(gate x) * (up x), x' = down hb, and the
+    next layer reads x'.  Rank r computes gate/up rows [r0, r1) of the hidden
+    dimension (one SwiGLU pair of the chain) and down rows [r0', r1') of the
+    model dimension.  Each rank stores every row it computes, tagged with the
+    launch, into every rank's copy of the vector over NVLink
+    (mli_chain_create_sharded), and the next op of every rank starts as soon
+    as the tagged rows it reads have arrived: no NCCL call, no host
+    synchronisation, no fence.  Every row is a full-K dot whose arithmetic
+    depends only on K, so every hb and x' is bit-identical to the same chain
+    on one GPU for any world size.
+
+    `layers`: this rank's shards, (gate_q, gate_s, up_q, up_s, down_q, down_s)
+    per layer; `x0`: the first layer's input (dim fp32, read at launch);
+    `exchange(bytes) -> list of bytes`: every rank's 64-byte handle, in rank
+    order (e.g. torch.distributed.all_gather_object).  Every rank must own
+    rows of both dimensions.  Close it on every rank only after all ranks'
+    last runs have finished (a barrier), since peers write into this rank's
+    buffers.
+    """
+
+    def __init__(self, layers, x0, dim: int, hidden: int, rank: int, world: int, form: str = "w8a32",
+                 exchange=None):
+        import torch
+
+        from . import ops
+
+        if form not in ("w8a32", "w8a8"):
+            raise ValueError(f"unknown form {form}")
+        self.hs = row_shard(hidden, world, rank)
+        self.ds = row_shard(dim, world, rank)
+        if self.hs.rows == 0 or self.ds.rows == 0:
+            raise ValueError("every rank must own rows of both dimensions")
+        self.dim, self.hidden, self.rank, self.world, self.form = dim, hidden, rank, world, form
+        dev = x0.device
+        self.hb = torch.zeros(self.hs.chunk * world, dtype=torch.float32, device=dev)
+        self.xb = torch.zeros(self.ds.chunk * world, dtype=torch.float32, device=dev)
+        self.x0 = x0
+        f = "w8a32" if form == "w8a32" else "w8a8_fused"
+        chain_ops = []
+        for l, (gq, gs, uq, us, dq, ds_) in enumerate(layers):
+            b = 3 * l
+            x = x0 if l == 0 else self.xb
+            common = dict(form=f, n=dim, d=self.hs.rows, wait=b, x=x, row_offset=self.hs.r0, d_total=hidden)
+            chain_ops.append(dict(common, y=self.hb[self.hs.r0:], w_q=gq, w_s=gs, epilogue="swiglu"))
+            chain_ops.append(dict(common, y=None, w_q=uq, w_s=us))
+            chain_ops.append(dict(form=f, n=hidden, d=self.ds.rows, wait=b + 2, x=self.hb, y=self.xb[self.ds.r0:],
+                                  w_q=dq, w_s=ds_, row_offset=self.ds.r0, d_total=dim))
+        self.layers = len(layers)
+        self.chain = ops.GemvChain(chain_ops, world=world)
+        if world > 1:
+            if exchange is None:
+                raise ValueError("a sharded chain over several ranks needs `exchange`")
+            self.chain.set_peers(exchange(self.chain.export()), rank)
+
+    def run(self, stream=None):
+        self.chain.run(stream)
+
+    def hidden_rows(self, layer: int):
+        """(hb of `layer` from the last run, every row tagged)."""
+        return self.chain.rows(3 * layer)
+
+    def output_rows(self, layer: int = -1):
+        """(x' of `layer` (default: the last) from the last run, every row tagged)."""
+        l = layer % self.layers
+        return self.chain.rows(3 * l + 2)
+
+    def close(self):
+        if self.chain is not None:
+            self.chain.close()
+            self.chain = None

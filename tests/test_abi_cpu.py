@@ -87,6 +87,10 @@ def test_launch_flags_roundtrip():
     lambda l: l.mli_gemv_f32(8, 8, 8, 0, 8, None),
     lambda l: l.mli_quantize_weights(8, 8, 8, 4, 100, 64, None),
     lambda l: l.mli_debug_group_dots(None, 8, 8, 64, 8, 64, None),
+    lambda l: l.mli_chain_create_sharded(None, None, None, 1, 2, None),
+    lambda l: l.mli_chain_export(None, None),
+    lambda l: l.mli_chain_set_peers(None, None, 0),
+    lambda l: l.mli_chain_rows(None, 0, None, None),
 ])
 def test_invalid_arguments_rejected_without_gpu(call):
     l = _lib.lib()

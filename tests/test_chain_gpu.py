@@ -321,3 +321,51 @@ def test_chain_rejects_reading_an_unawaited_producer():
     with pytest.raises(MliError):
         ops.GemvChain([dict(form="w8a32", n=256, d=256, wait=0, x=x, y=y, w_q=q, w_s=s),
                        dict(form="w8a32", n=256, d=256, wait=0, x=y, y=z, w_q=q, w_s=s)])
+
+
+def _ffn_layers(dim, hidden, layers, seed):
+    out = []
+    for l in range(layers):
+        g = weights(hidden, dim, seed + 10 * l)
+        u = weights(hidden, dim, seed + 10 * l + 1)
+        d = weights(dim, hidden, seed + 10 * l + 2)
+        out.append((g[0], g[1], u[0], u[1], d[0], d[1]))
+    return out
+
+
+@pytest.mark.parametrize("form", ["w8a32", "w8a8"])
+def test_sharded_chain_one_rank_matches_plain_chain(form):
+    """A row-sharded FFN stack (mli_chain_create_sharded) on one rank gives
+    the plain chain's hb and x' bit for bit, read back from its mirrors with
+    every row tagged, over several runs (both mirror halves in turn)."""
+    from minillama_infra_b200.shard import ChainShardedFFN
+
+    dim, hidden, L = 2048, 8192, 3
+    layers = _ffn_layers(dim, hidden, L, 500)
+    x0 = torch.from_numpy(synth.activation_np(dim, 77, outliers=form == "w8a8")).to(dev())
+    f = "w8a32" if form == "w8a32" else "w8a8_fused"
+    hb = torch.zeros(hidden, device=dev())
+    xb = torch.zeros(dim, device=dev())
+    plain_ops = []
+    for l, (gq, gs, uq, us, dq, ds_) in enumerate(layers):
+        x = x0 if l == 0 else xb
+        plain_ops += [dict(form=f, n=dim, d=hidden, wait=3 * l, x=x, y=hb, w_q=gq, w_s=gs, epilogue="swiglu"),
+                      dict(form=f, n=dim, d=hidden, wait=3 * l, x=x, y=None, w_q=uq, w_s=us),
+                      dict(form=f, n=hidden, d=dim, wait=3 * l + 2, x=hb, y=xb, w_q=dq, w_s=ds_)]
+    plain = ops.GemvChain(plain_ops)
+    plain.run()
+    torch.cuda.synchronize()
+    want_h, want_x = bits(hb), bits(xb)
+    sh = ChainShardedFFN(layers, x0, dim, hidden, 0, 1, form=form)
+    for rep in range(3):
+        sh.run()
+        torch.cuda.synchronize()
+        h, h_ok = sh.hidden_rows(L - 1)
+        x, x_ok = sh.output_rows()
+        assert h_ok and x_ok, rep
+        assert np.array_equal(h.view(np.uint32), want_h), rep
+        assert np.array_equal(x.view(np.uint32), want_x), rep
+        assert np.array_equal(bits(sh.xb[:dim]), want_x), rep  # the rank's own rows in its y
+    sh.close()
+    plain.close()
+    assert ops.device_error() == 0

@@ -201,3 +201,86 @@ def test_sharded_ffn_bit_exact_two_gpus(form):
     for rank, ok, err in results:
         assert ok, f"rank {rank}: gathered hb / xb differ from the single-GPU block"
         assert err == 0
+
+
+def _chain_ffn_worker(rank, world, port, form, q):
+    """The fused FFN stack over `world` ranks (peer stores inside one chained
+    launch per step) against the same stack on one GPU."""
+    from datetime import timedelta
+
+    import numpy as np
+    import torch.distributed as dist
+
+    from minillama_infra_b200 import ops, synth
+    from minillama_infra_b200.shard import ChainShardedFFN, row_shard
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    try:
+        dim, hidden, L = 2048, 8192, 4
+        full = []
+        for l in range(L):
+            g = synth.weights_gpu(hidden, dim, seed=600 + 10 * l, device=dev)
+            u = synth.weights_gpu(hidden, dim, seed=601 + 10 * l, device=dev)
+            d = synth.weights_gpu(dim, hidden, seed=602 + 10 * l, device=dev)
+            full.append((g[0], g[1], u[0], u[1], d[0], d[1]))
+        x0 = synth.activation_gpu(dim, 699, dev, outliers=(form == "w8a8"))
+        one = ChainShardedFFN(full, x0, dim, hidden, 0, 1, form=form)
+        one.run()
+        torch.cuda.synchronize()
+        want = [one.hidden_rows(l)[0].view(np.uint32) for l in range(L)] + [one.output_rows()[0].view(np.uint32)]
+        one.close()
+        hs, ds = row_shard(hidden, world, rank), row_shard(dim, world, rank)
+        mine = [(gq[hs.r0:hs.r1].clone(), gs[hs.r0:hs.r1].clone(), uq[hs.r0:hs.r1].clone(), us[hs.r0:hs.r1].clone(),
+                 dq[ds.r0:ds.r1].clone(), dss[ds.r0:ds.r1].clone()) for (gq, gs, uq, us, dq, dss) in full]
+
+        def exchange(h):
+            out = [None] * world
+            dist.all_gather_object(out, h)
+            return out
+
+        sh = ChainShardedFFN(mine, x0, dim, hidden, rank, world, form=form, exchange=exchange)
+        dist.barrier()
+        ok = True
+        for rep in range(5):  # both mirror halves, several times
+            sh.run()
+            torch.cuda.synchronize()
+            dist.barrier()  # every rank's rows of this run have landed everywhere
+            got = [sh.hidden_rows(l) for l in range(L)] + [sh.output_rows()]
+            for (v, tagged), w in zip(got, want):
+                ok = ok and tagged and bool(np.array_equal(v.view(np.uint32), w))
+            dist.barrier()
+        err = ops.device_error()
+        sh.close()
+        q.put((rank, ok, err))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("form", ["w8a32", "w8a8"])
+def test_chain_sharded_ffn_bit_exact_two_gpus(form):
+    """Four FFN blocks row-sharded over two GPUs in one chained launch per
+    step, the hb and x' rows exchanged by tagged peer stores inside the
+    kernel: every layer's hb and the last x' are bit-identical to one GPU on
+    both ranks, in five runs in a row."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_chain_ffn_worker, args=(r, world, port, form, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, ok, err in results:
+        assert ok, f"rank {rank}: sharded chain rows differ from one GPU (or were not tagged)"
+        assert err == 0
