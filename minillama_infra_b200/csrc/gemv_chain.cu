@@ -608,7 +608,9 @@ struct Role {
 
 // Warps 0 .. kW-1 consume (kRB rows per warp per stage), warp kW is the
 // producer (bulk copies).
-template <Form F, int kW, int kRB, bool kEpi>
+// kTags: some op reads another op's rows (mirrors, tags, polls, peers); a
+// chain without dependencies runs a kernel compiled without any of it.
+template <Form F, int kW, int kRB, bool kEpi, bool kTags>
 __global__ void __launch_bounds__((kW + 1) * 32, 1) gemv_chain_kernel(const Args a) {
   constexpr int kT = kW * 32;  // consumer threads
   extern __shared__ __align__(1024) unsigned char smem[];
@@ -691,7 +693,7 @@ __global__ void __launch_bounds__((kW + 1) * 32, 1) gemv_chain_kernel(const Args
         // once a wait has expired in this CTA, later ops wait for nothing
         // (their rows are not produced): the launch ends in bounded time
         const bool broken = *sm.broken != 0;
-        if (wait > known && op.poll_count > 0 && !broken) {
+        if (kTags && wait > known && op.poll_count > 0 && !broken) {
           // ops of the wait prefix that the activation's producer does not imply
           fail = !poll_ops<kT>(a, ops, polls, op.poll_first, op.poll_count, seq);
           fail = named_sync_or<kT>(fail);
@@ -710,7 +712,7 @@ __global__ void __launch_bounds__((kW + 1) * 32, 1) gemv_chain_kernel(const Args
           const int col0 = role.col0;
           // (a broken CTA reads the activation as it stands, without waiting)
           const uint64_t* src_m =
-              op.src >= 0 && !broken ? a.mirror + mirror_half(a, seq) + ops[op.src].mirror : nullptr;
+              kTags && op.src >= 0 && !broken ? a.mirror + mirror_half(a, seq) + ops[op.src].mirror : nullptr;
           const uint32_t src_tag = row_tag(seq, op.src);
           if constexpr (F == Form::kW8A8) {
             xscale = __ldcg(op.xs);
@@ -805,12 +807,12 @@ __global__ void __launch_bounds__((kW + 1) * 32, 1) gemv_chain_kernel(const Args
           const Op& op = ops[o];
           // rows r of the op are words row_off + r of its mirror (the whole GEMV's rows)
           const uint32_t half = mirror_half(a, seq);
-          const size_t my_off = op.mirror >= 0 ? half + op.mirror + op.row_off : 0;
-          const bool share = a.world > 1;
-          uint64_t* my_mirror = op.mirror >= 0 ? a.mirror + my_off : nullptr;
+          const size_t my_off = kTags && op.mirror >= 0 ? half + op.mirror + op.row_off : 0;
+          const bool share = kTags && a.world > 1;
+          uint64_t* my_mirror = kTags && op.mirror >= 0 ? a.mirror + my_off : nullptr;
           const uint32_t my_tag = row_tag(seq, o);
           const uint64_t* base_mirror =
-              op.base >= 0 ? a.mirror + half + ops[op.base].mirror + op.row_off : nullptr;
+              kTags && op.base >= 0 ? a.mirror + half + ops[op.base].mirror + op.row_off : nullptr;
           const uint32_t base_tag = row_tag(seq, op.base);
           bool late = false;
           const uint64_t t0 = global_timer_ns();
@@ -890,7 +892,8 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 // Kernel shape: consumer warps per CTA, rows per warp per stage, CTAs per SM.
 struct Variant {
   int warps, rb, per_sm;
-  bool epi;  // some op has a non-store epilogue: the kernel with epilogue code
+  bool epi;   // some op has a non-store epilogue: the kernel with epilogue code
+  bool tags;  // some op reads another op's rows: the kernel with mirror code
 };
 
 struct Plan {
@@ -916,8 +919,8 @@ bool overlaps(const void* a, size_t an, const void* b, size_t bn) {
 // comparisons).
 Variant pick_variant(int form, unsigned flags) {
   const bool a32 = form == 0;
-  if (flags & (1u << 8)) return {8, a32 ? 4 : 2, 1, false};
-  return {8, a32 ? 8 : 4, 1, false};
+  if (flags & (1u << 8)) return {8, a32 ? 4 : 2, 1, false, false};
+  return {8, a32 ? 8 : 4, 1, false, false};
 }
 
 // The activation held by the consumers (4 kT kPre columns) bounds ops that
@@ -1106,6 +1109,7 @@ int plan_chain(const mli_gemv_op* in, int count, int sm_count, int smem_per_sm, 
       if (mirror > (1u << 30)) return MLI_ERR_UNSUPPORTED;
     }
   p->mirror_words = mirror;
+  p->v.tags = mirror > 0 || !p->polls.empty() || row_offset != nullptr;
   Args& a = p->args;
   a.count = count;
   a.n_phases = static_cast<int>(p->phases.size()) - 1;
@@ -1144,17 +1148,20 @@ int plan_chain(const mli_gemv_op* in, int count, int sm_count, int smem_per_sm, 
 
 using KernelFn = void (*)(const Args);
 
-template <Form F, bool kEpi>
+template <Form F, bool kEpi, bool kTags>
 KernelFn kernel_shape(const Variant& v) {
   if constexpr (F == Form::kW8A32)
-    return v.rb == 8 ? gemv_chain_kernel<F, 8, 8, kEpi> : gemv_chain_kernel<F, 8, 4, kEpi>;
+    return v.rb == 8 ? gemv_chain_kernel<F, 8, 8, kEpi, kTags> : gemv_chain_kernel<F, 8, 4, kEpi, kTags>;
   else
-    return v.rb == 4 ? gemv_chain_kernel<F, 8, 4, kEpi> : gemv_chain_kernel<F, 8, 2, kEpi>;
+    return v.rb == 4 ? gemv_chain_kernel<F, 8, 4, kEpi, kTags> : gemv_chain_kernel<F, 8, 2, kEpi, kTags>;
 }
 
+// Three kernels per shape: no epilogue and no dependencies, dependencies
+// without epilogues, epilogues (with or without dependencies).
 template <Form F>
 KernelFn kernel_epi(const Variant& v) {
-  return v.epi ? kernel_shape<F, true>(v) : kernel_shape<F, false>(v);
+  if (v.epi) return kernel_shape<F, true, true>(v);
+  return v.tags ? kernel_shape<F, false, true>(v) : kernel_shape<F, false, false>(v);
 }
 
 KernelFn kernel_for(int form, const Variant& v) {
