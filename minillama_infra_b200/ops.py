@@ -262,6 +262,13 @@ class GemvChain:
             ptrs[r] = p.value
         check(lib().mli_chain_set_peers(self._h, ptrs, rank), "mli_chain_set_peers")
 
+    def set_peer_pointers(self, ptrs, rank: int) -> None:
+        """Every rank's mirror block as device pointers already mapped in this
+        process (ptrs[rank] is ignored): for frameworks that share memory
+        their own way."""
+        arr = (ctypes.c_void_p * self.world)(*[0 if r == rank else int(p) for r, p in enumerate(ptrs)])
+        check(lib().mli_chain_set_peers(self._h, arr, rank), "mli_chain_set_peers")
+
     def rows(self, op: int):
         """(whole rows of op `op` from the last run as a numpy float32 array,
         True when every row carries that run's tag); synchronous."""

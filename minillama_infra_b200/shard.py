@@ -363,7 +363,9 @@ class ChainShardedFFN:
     `layers`: this rank's shards, (gate_q, gate_s, up_q, up_s, down_q, down_s)
     per layer; `x0`: the first layer's input (dim fp32, read at launch);
     `exchange(bytes) -> list of bytes`: every rank's 64-byte handle, in rank
-    order (e.g. torch.distributed.all_gather_object).  Every rank must own
+    order (e.g. torch.distributed.all_gather_object); without it (world > 1)
+    the caller sets the peers itself (self.chain.set_peers /
+    set_peer_pointers) before the first run.  Every rank must own
     rows of both dimensions.  Close it on every rank only after all ranks'
     last runs have finished (a barrier), since peers write into this rank's
     buffers.
@@ -398,9 +400,7 @@ class ChainShardedFFN:
                                   w_q=dq, w_s=ds_, row_offset=self.ds.r0, d_total=dim))
         self.layers = len(layers)
         self.chain = ops.GemvChain(chain_ops, world=world)
-        if world > 1:
-            if exchange is None:
-                raise ValueError("a sharded chain over several ranks needs `exchange`")
+        if world > 1 and exchange is not None:
             self.chain.set_peers(exchange(self.chain.export()), rank)
 
     def run(self, stream=None):

@@ -369,3 +369,35 @@ def test_sharded_chain_one_rank_matches_plain_chain(form):
     sh.close()
     plain.close()
     assert ops.device_error() == 0
+
+
+def test_sharded_chain_times_out_when_a_rank_never_delivers():
+    """Rank 0 of a two-rank FFN layer whose partner never runs: its rows of hb
+    never arrive, so the down projection's bounded wait runs out -- the launch
+    ends with device error 4 instead of hanging, and the GPU stays usable.
+    The partner's mirror is stood in for by a zeroed buffer of this GPU.
+    Running before the peers are set is refused."""
+    from minillama_infra_b200.shard import ChainShardedFFN, row_shard
+
+    dim, hidden = 2048, 8192
+    (gq, gs, uq, us, dq, ds_), = _ffn_layers(dim, hidden, 1, 800)
+    hs, dsh = row_shard(hidden, 2, 0), row_shard(dim, 2, 0)
+    mine = [(gq[hs.r0:hs.r1].clone(), gs[hs.r0:hs.r1].clone(), uq[hs.r0:hs.r1].clone(), us[hs.r0:hs.r1].clone(),
+             dq[dsh.r0:dsh.r1].clone(), ds_[dsh.r0:dsh.r1].clone())]
+    x0 = torch.from_numpy(synth.activation_np(dim, 81)).to(dev())
+    sh = ChainShardedFFN(mine, x0, dim, hidden, 0, 2, form="w8a32")
+    with pytest.raises(MliError):
+        sh.run()  # no peers yet
+    assert ops.device_error() == 0
+    partner = torch.zeros(8 << 20, dtype=torch.uint8, device=dev())  # larger than the mirror block
+    sh.chain.set_peer_pointers([0, partner.data_ptr()], 0)
+    sh.run()
+    torch.cuda.synchronize()
+    assert ops.device_error() == 4
+    _, complete = sh.output_rows()
+    assert not complete
+    sh.close()
+    y = torch.empty(64, device=dev())  # the context still works
+    ops.matmul_int8(y, x0, gq[:64].contiguous(), gs[:64].contiguous(), dim, 64, 64)
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
