@@ -415,13 +415,24 @@ __device__ __forceinline__ void cta_rmsnorm(float4 (&v)[kPre], int n, const floa
 
 // W8A32 digit planes and group factors (digit_quad) of the held activation
 // into shared memory.
-template <int kT>
+// kUnroll: the held values stay in registers; rolled (the kernels with the
+// dependency code), they go through a per-thread local array instead, which
+// keeps the prologue's registers below the row loop's.
+template <int kT, bool kUnroll>
 __device__ __forceinline__ void cta_digits(const float4 (&v)[kPre], int n, int8_t* planes, float* fac) {
   const int lane = threadIdx.x & 31;
-#pragma unroll 1  // rolled: keeps the prologue's registers below the row loop's
-  for (int j = 0; j < kPre; ++j) {
-    const int c = 4 * kT * j + 4 * static_cast<int>(threadIdx.x);
-    if (4 * kT * j < n) digit_quad(v[j], c < n, c, n, planes, fac, lane);  // CTA-uniform
+  if constexpr (kUnroll) {
+#pragma unroll
+    for (int j = 0; j < kPre; ++j) {
+      const int c = 4 * kT * j + 4 * static_cast<int>(threadIdx.x);
+      if (4 * kT * j < n) digit_quad(v[j], c < n, c, n, planes, fac, lane);  // CTA-uniform
+    }
+  } else {
+#pragma unroll 1
+    for (int j = 0; j < kPre; ++j) {
+      const int c = 4 * kT * j + 4 * static_cast<int>(threadIdx.x);
+      if (4 * kT * j < n) digit_quad(v[j], c < n, c, n, planes, fac, lane);  // CTA-uniform
+    }
   }
 }
 
@@ -565,7 +576,7 @@ __device__ __forceinline__ void warp_digits(const float4 (&v)[kPre], unsigned vm
 // Shared preparation into shared memory: W8A32 digit planes + group factors,
 // or the fused W8A8 int8 copy (its scale into *xscale).  All consumer threads
 // call it.  False (on every thread) when an input row did not arrive in time.
-template <Form F, int kT>
+template <Form F, int kT, bool kUnroll>
 __device__ __forceinline__ bool prep_cta(const Op& op, const uint64_t* m, uint32_t tag, bool sys,
                                          unsigned char* xregion, float* red, float* red2, float* xscale) {
   float4 pre[kPre];
@@ -576,7 +587,7 @@ __device__ __forceinline__ bool prep_cta(const Op& op, const uint64_t* m, uint32
   if (op.norm_w != nullptr) cta_rmsnorm<kT>(pre, n, op.norm_w, red2);
   if constexpr (F == Form::kW8A32) {
     int8_t* planes = reinterpret_cast<int8_t*>(xregion);
-    cta_digits<kT>(pre, n, planes, reinterpret_cast<float*>(planes + 4 * n));
+    cta_digits<kT, kUnroll>(pre, n, planes, reinterpret_cast<float*>(planes + 4 * n));
   } else {
     *xscale = cta_quant<kT>(pre, op.x(), n, reinterpret_cast<int8_t*>(xregion), red);
   }
@@ -728,7 +739,7 @@ __global__ void __launch_bounds__((kW + 1) * 32, 1) gemv_chain_kernel(const Args
             if constexpr (F == Form::kW8A32) warp_digits(pre, vmask, xd, fac);
           } else {
             float t_scale = 0.f;
-            if (!prep_cta<F, kT>(op, src_m, src_tag, a.world > 1, smem + a.x_off, sm.red, sm.red2, &t_scale))
+            if (!prep_cta<F, kT, !kTags>(op, src_m, src_tag, a.world > 1, smem + a.x_off, sm.red, sm.red2, &t_scale))
               fail = true;
             xscale = t_scale;
             if constexpr (F == Form::kW8A32) {
