@@ -335,16 +335,16 @@ __device__ __forceinline__ bool poll_ops(const Args& a, const Op* ops, const int
 // ---------------------------------------------------------------------------
 constexpr int kPre = 8;  // float4 of activation held per consumer thread
 
-// Shared preparation: consumer thread t holds columns 4t + 4 kT j, j < kPre
+// Shared preparation: consumer thread t holds columns 4t + 4 kT j, j < J
 // (the whole activation for n <= 4 kT kPre).  False on a timeout.
-template <int kT>
+template <int kT, int J>
 __device__ __forceinline__ bool cta_x_load(const Op& op, const uint64_t* m, uint32_t tag, bool sys,
-                                           float4 (&v)[kPre]) {
+                                           float4 (&v)[J]) {
   const int t = static_cast<int>(threadIdx.x);
   const int n = op.n;
   if (m == nullptr) {
 #pragma unroll
-    for (int j = 0; j < kPre; ++j) {
+    for (int j = 0; j < J; ++j) {
       const int c = 4 * kT * j + 4 * t;
       v[j] = c < n ? __ldcg(reinterpret_cast<const float4*>(op.x() + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
@@ -354,7 +354,7 @@ __device__ __forceinline__ bool cta_x_load(const Op& op, const uint64_t* m, uint
   // few registers in flight, so the row loop around it keeps its own
   const uint64_t t0 = global_timer_ns();
 #pragma unroll
-  for (int j = 0; j < kPre; j += 2) {
+  for (int j = 0; j < J; j += 2) {
     v[j] = v[j + 1] = make_float4(0.f, 0.f, 0.f, 0.f);
     const int c0 = 4 * kT * j + 4 * t, c1 = c0 + 4 * kT;
     if (c0 >= n) continue;
@@ -384,13 +384,13 @@ __device__ __forceinline__ bool cta_x_load(const Op& op, const uint64_t* m, uint
 // src/model_cuda_v2_shared.cu:74-89): ss = 1 / sqrt(sum(x^2) / n + 1e-5),
 // x = weight * (ss * x).  The sum runs in one fixed order (per thread, the
 // warp butterfly, warps in order), so every CTA normalises identically.
-template <int kT>
-__device__ __forceinline__ void cta_rmsnorm(float4 (&v)[kPre], int n, const float* weight, float* red) {
+template <int kT, int J>
+__device__ __forceinline__ void cta_rmsnorm(float4 (&v)[J], int n, const float* weight, float* red) {
   constexpr int kW = kT / 32;
   const int t = static_cast<int>(threadIdx.x);
   float ssq = 0.f;
 #pragma unroll
-  for (int j = 0; j < kPre; ++j) {
+  for (int j = 0; j < J; ++j) {
     ssq = fmaf(v[j].x, v[j].x, ssq);
     ssq = fmaf(v[j].y, v[j].y, ssq);
     ssq = fmaf(v[j].z, v[j].z, ssq);
@@ -404,7 +404,7 @@ __device__ __forceinline__ void cta_rmsnorm(float4 (&v)[kPre], int n, const floa
   for (int w = 1; w < kW; ++w) sum += red[w];
   const float ss = 1.0f / sqrtf(sum / static_cast<float>(n) + 1e-5f);
 #pragma unroll
-  for (int j = 0; j < kPre; ++j) {
+  for (int j = 0; j < J; ++j) {
     const int c = 4 * kT * j + 4 * t;
     if (c < n) {
       const float4 g = __ldg(reinterpret_cast<const float4*>(weight + c));
@@ -418,18 +418,18 @@ __device__ __forceinline__ void cta_rmsnorm(float4 (&v)[kPre], int n, const floa
 // kUnroll: the held values stay in registers; rolled (the kernels with the
 // dependency code), they go through a per-thread local array instead, which
 // keeps the prologue's registers below the row loop's.
-template <int kT, bool kUnroll>
-__device__ __forceinline__ void cta_digits(const float4 (&v)[kPre], int n, int8_t* planes, float* fac) {
+template <int kT, bool kUnroll, int J>
+__device__ __forceinline__ void cta_digits(const float4 (&v)[J], int n, int8_t* planes, float* fac) {
   const int lane = threadIdx.x & 31;
   if constexpr (kUnroll) {
 #pragma unroll
-    for (int j = 0; j < kPre; ++j) {
+    for (int j = 0; j < J; ++j) {
       const int c = 4 * kT * j + 4 * static_cast<int>(threadIdx.x);
       if (4 * kT * j < n) digit_quad(v[j], c < n, c, n, planes, fac, lane);  // CTA-uniform
     }
   } else {
 #pragma unroll 1
-    for (int j = 0; j < kPre; ++j) {
+    for (int j = 0; j < J; ++j) {
       const int c = 4 * kT * j + 4 * static_cast<int>(threadIdx.x);
       if (4 * kT * j < n) digit_quad(v[j], c < n, c, n, planes, fac, lane);  // CTA-uniform
     }
@@ -439,16 +439,16 @@ __device__ __forceinline__ void cta_digits(const float4 (&v)[kPre], int n, int8_
 // Fused W8A8: the quantised activation into shared memory, bit-identical to
 // x_quant_prologue; from the held values when they cover n, else (an input
 // ready at launch, n > 4 kT kPre) read a second time.
-template <int kT>
-__device__ __forceinline__ float cta_quant(const float4 (&v)[kPre], const float* x, int n, int8_t* xq,
+template <int kT, int J>
+__device__ __forceinline__ float cta_quant(const float4 (&v)[J], const float* x, int n, int8_t* xq,
                                            float* red) {
   constexpr int kW = kT / 32;
   const int t = static_cast<int>(threadIdx.x);
-  const bool hold = n <= 4 * kT * kPre;
+  const bool hold = n <= 4 * kT * J;
   float m = 0.f;
   if (hold) {
 #pragma unroll
-    for (int j = 0; j < kPre; ++j)
+    for (int j = 0; j < J; ++j)
       m = fmaxf(m, fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w))));
   } else {
     for (int c = 4 * t; c < n; c += 4 * kT) {
@@ -466,7 +466,7 @@ __device__ __forceinline__ float cta_quant(const float4 (&v)[kPre], const float*
   const float inv = 1.0f / scale;
   if (hold) {
 #pragma unroll
-    for (int j = 0; j < kPre; ++j) {
+    for (int j = 0; j < J; ++j) {
       const int c = 4 * kT * j + 4 * t;
       if (c < n) *reinterpret_cast<uint32_t*>(xq + c) = quant_quad(v[j], inv);
     }
@@ -576,23 +576,37 @@ __device__ __forceinline__ void warp_digits(const float4 (&v)[kPre], unsigned vm
 // Shared preparation into shared memory: W8A32 digit planes + group factors,
 // or the fused W8A8 int8 copy (its scale into *xscale).  All consumer threads
 // call it.  False (on every thread) when an input row did not arrive in time.
-template <Form F, int kT, bool kUnroll>
-__device__ __forceinline__ bool prep_cta(const Op& op, const uint64_t* m, uint32_t tag, bool sys,
-                                         unsigned char* xregion, float* red, float* red2, float* xscale) {
-  float4 pre[kPre];
-  bool fail = !cta_x_load<kT>(op, m, tag, sys, pre);
+// J float4 of the activation per consumer thread (columns 4t + 4 kT j, j < J).
+template <Form F, int kT, bool kUnroll, int J>
+__device__ __forceinline__ bool prep_cta_j(const Op& op, const uint64_t* m, uint32_t tag, bool sys,
+                                           unsigned char* xregion, float* red, float* red2, float* xscale) {
+  float4 pre[J];
+  bool fail = !cta_x_load<kT, J>(op, m, tag, sys, pre);
   fail = named_sync_or<kT>(fail);  // also: every consumer is done reading the shared region
   if (fail) return false;
   const int n = op.n;
-  if (op.norm_w != nullptr) cta_rmsnorm<kT>(pre, n, op.norm_w, red2);
+  if (op.norm_w != nullptr) cta_rmsnorm<kT, J>(pre, n, op.norm_w, red2);
   if constexpr (F == Form::kW8A32) {
     int8_t* planes = reinterpret_cast<int8_t*>(xregion);
-    cta_digits<kT, kUnroll>(pre, n, planes, reinterpret_cast<float*>(planes + 4 * n));
+    cta_digits<kT, kUnroll || J <= 4, J>(pre, n, planes, reinterpret_cast<float*>(planes + 4 * n));
   } else {
-    *xscale = cta_quant<kT>(pre, op.x(), n, reinterpret_cast<int8_t*>(xregion), red);
+    *xscale = cta_quant<kT, J>(pre, op.x(), n, reinterpret_cast<int8_t*>(xregion), red);
   }
   named_sync<kT>();
   return true;
+}
+
+// W8A32 activations of up to 4 kT * 4 columns hold only as many float4 per
+// thread as they need, unrolled in registers; wider ones (and the kernels'
+// rolled loops) take the full kPre.
+template <Form F, int kT, bool kUnroll>
+__device__ __forceinline__ bool prep_cta(const Op& op, const uint64_t* m, uint32_t tag, bool sys,
+                                         unsigned char* xregion, float* red, float* red2, float* xscale) {
+  if constexpr (F == Form::kW8A32) {
+    if (op.n <= 4 * kT * 2) return prep_cta_j<F, kT, kUnroll, 2>(op, m, tag, sys, xregion, red, red2, xscale);
+    if (op.n <= 4 * kT * 4) return prep_cta_j<F, kT, kUnroll, 4>(op, m, tag, sys, xregion, red, red2, xscale);
+  }
+  return prep_cta_j<F, kT, kUnroll, kPre>(op, m, tag, sys, xregion, red, red2, xscale);
 }
 
 // A consumer warp's role in an op: its slice, its rows of a stage, and the
