@@ -6,30 +6,40 @@
 //
 // The reference decodes one token at a time (src/model_cuda_v2_shared.cu:
 // 465-501); with m >= 16 tokens the op is a real dense contraction and runs
-// here.  One CTA computes a tile of 128 weight rows x BN tokens over a range of
-// K:
+// here, in one of two kernels chosen per call:
+//
+// Split-K tiles (gemm_w8a8_tc_kernel<BN>, BN = 16..128 tokens).  One CTA
+// computes a tile of 128 weight rows x BN tokens over a range of K:
 //   * warp 0 streams 128-byte K chunks of the weight tile (128 x 128 B) and
 //     of the activation tile (BN x 128 B) with 2-D TMA loads (128-byte
 //     swizzle, the canonical K-major UMMA layout) into a ring of 6-10 stages;
 //   * warp 1 owns the tensor memory and issues the MMAs from one thread (two
 //     threads, warps 1 and 2 on alternate chunks, for tiles of 32 tokens or
-//     fewer): per K chunk, four K=32 MMAs (two per 64-column group) into a
-//     pair of int32 accumulator buffers, one commit for the pair and one for
-//     the stage;
-//   * warpgroups 1 and 2 are the epilogue, taking alternate chunks: each warp
-//     reads its 32 accumulator lanes over all BN token columns
-//     (tcgen05.ld), recovers the exact int32 group dot as a float (the
-//     accumulators start at a bias that makes the int32 result the bits of
-//     1.5 * 2^23 + I), adds ws[r][g] * I into fp32 registers (packed f32x2
-//     arithmetic) and refills the accumulator with the bias for its next
-//     use; the two warpgroups' sums are added in a fixed order at the end.
-// K is split over CTAs so a layer fills the GPU.  The splits of a tile run as
-// one thread-block cluster: each stages its partial tile in shared memory and
-// sums a share of the tile over the cluster's partials in split order
-// (deterministic), scales by xs[t] and writes Y.  Where clusters of the
-// wanted size do not fit the GPU at once, the splits may instead write their
-// partials into the caller's workspace, summed in split order by a second,
-// GPU-wide kernel.
+//     fewer): per 64-column group two K = 32 MMAs into an int32 accumulator
+//     buffer (128-token tiles first write the accumulator offset with one
+//     MMA of a constant unsigned tile), one commit per unit of buffers and
+//     one for the stage;
+//   * warpgroups 1 and 2 are the epilogue, taking alternate units: each warp
+//     reads its 32 accumulator lanes over all BN token columns (tcgen05.ld),
+//     recovers the exact int32 group dot as a float (the accumulator starts
+//     at an offset that makes its bits a float linear in the dot), adds
+//     ws[r][g] * I into fp32 registers (packed f32x2 arithmetic) and, for
+//     narrow tiles, refills the offset with tensor-memory stores; the two
+//     warpgroups' sums are added in a fixed order at the end.
+//   K is split over CTAs so a layer fills the GPU.  The splits of a tile run
+//   as one thread-block cluster: each stages its partial tile in shared memory
+//   and sums a share of the tile over the cluster's partials in split order
+//   (deterministic), scales by xs[t] and writes Y.  Where clusters of the
+//   wanted size do not fit the GPU at once, the splits may instead write their
+//   partials into the caller's workspace, summed in split order by a second,
+//   GPU-wide kernel.
+//
+// Persistent whole tiles (gemm_w8a8_persistent_kernel, more than 64 tokens,
+// problems with enough 128 x 128 tiles to keep every SM evenly busy): one CTA
+// per SM walks a host-made list of whole tiles, its TMA, MMA and epilogue
+// counters running on across tiles; the epilogue warpgroups split a tile by
+// token columns and store complete rows straight to Y (described at the
+// kernel).
 //
 // This file builds as a device module of its own (whole-program compilation,
 // no -rdc): only then does ptxas allocate the epilogue's registers up to its
