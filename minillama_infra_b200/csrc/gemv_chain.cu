@@ -47,6 +47,14 @@
 //  * Rows are computed exactly as in gemv_stream_kernel (same row kernels,
 //    same slice order), so an op without a norm prologue gives bit-identical
 //    output to the corresponding mli_gemv_* call.
+//  * Row-sharded chains (one process per GPU): an op computes a row range of a
+//    larger GEMV and stores each row, tagged, into every rank's mirror over
+//    NVLink (plain system-scope peer stores); a reader of the whole vector
+//    checks the tags of words other GPUs wrote.  Mirrors are kept twice,
+//    alternating by launch, so a rank one launch ahead never overwrites words
+//    another is still reading.
+//  * A chain in which no op reads another's rows runs a kernel compiled
+//    without any of the mirror, tag, poll or peer code.
 //  * Every CTA processes its units in chain order and a unit only waits for
 //    earlier ops, so the earliest unfinished op never waits: with all CTAs
 //    resident (cooperative launch) the chain cannot deadlock.  The last CTA to
