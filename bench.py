@@ -639,7 +639,7 @@ def classifier_measure(args, device, rank, world, form, allgather="p2p", sampler
 
     def forward(c=0):
         if fused:
-            idx.copy_(lins[c].forward(x))  # GEMV with peer stores + wait + argmax
+            lins[c].forward(x, out=idx)  # GEMV with peer stores + wait + argmax, one launch
             return None
         if lins is not None:
             logits = lins[c].forward(x)

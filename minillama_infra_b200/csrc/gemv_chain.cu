@@ -301,40 +301,66 @@ __device__ __forceinline__ void issue_unit(const Args& a, const Op* ops, unsigne
 __device__ __forceinline__ uint32_t mirror_half(const Args& a, unsigned seq) { return (seq & 1u) ? a.mirror_half : 0u; }
 
 // Consumer threads check, by their mirrors' tags, that every row of the ops
-// polls[first, first + count) was written in this launch.  False if a row did
-// not arrive in time.
+// polls[first, first + count) was written in this launch.  The polled ops'
+// rows form one index space; a thread's words of a round (up to 8) are all in
+// flight before the first is checked.  False if a row did not arrive in time.
 template <int kT>
 __device__ __forceinline__ bool poll_ops(const Args& a, const Op* ops, const int* polls, int first, int count,
                                          unsigned seq) {
   const uint64_t t0 = global_timer_ns();
-  for (int p = first; p < first + count; ++p) {
-    const int j = polls[p];
-    const Op& q = ops[j];
-    const uint32_t tag = row_tag(seq, j);
-    const uint64_t* m = a.mirror + mirror_half(a, seq) + q.mirror;
-    const bool sys = a.world > 1;
-    for (int r0 = threadIdx.x; r0 < q.d_total; r0 += 8 * kT) {
-      unsigned pending = 0;
+  const bool sys = a.world > 1;
+  const uint32_t half = mirror_half(a, seq);
+  int total = 0;
+  for (int p = first; p < first + count; ++p) total += ops[polls[p]].d_total;
+  int p = first, start = 0;  // op polls[p] holds rows [start, start + d_total) of the space
+  for (int r0 = threadIdx.x; r0 < total; r0 += 8 * kT) {
+    const uint64_t* addr[8];
+    uint32_t tags[8];
+    unsigned pending = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int i = r0 + k * kT;
+      addr[k] = a.mirror;
+      tags[k] = 0;
+      if (i < total) {
+        while (i >= start + ops[polls[p]].d_total) start += ops[polls[p++]].d_total;
+        const int j = polls[p];
+        addr[k] = a.mirror + half + ops[j].mirror + (i - start);
+        tags[k] = row_tag(seq, j);
+        pending |= 1u << k;
+      }
+    }
+    unsigned ns = 32;
+    while (true) {
+      uint64_t w[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) w[k] = ((pending >> k) & 1u) ? ld_relaxed_b64(addr[k], sys) : 0ull;
 #pragma unroll
       for (int k = 0; k < 8; ++k)
-        if (r0 + k * kT < q.d_total) pending |= 1u << k;
-      unsigned ns = 32;
-      while (true) {
-        uint64_t w[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k)
-          if ((pending >> k) & 1u) w[k] = ld_relaxed_b64(m + r0 + k * kT, sys);
-#pragma unroll
-        for (int k = 0; k < 8; ++k)
-          if (((pending >> k) & 1u) && has_tag(w[k], tag)) pending &= ~(1u << k);
-        if (pending == 0) break;
-        if (global_timer_ns() - t0 > kWaitLimitNs) return false;
-        poll_backoff(ns);
-      }
+        if (((pending >> k) & 1u) && has_tag(w[k], tags[k])) pending &= ~(1u << k);
+      if (pending == 0) break;
+      if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+      poll_backoff(ns);
     }
   }
   return true;
 }
+
+// Polls of the wait prefix, run by the activation loaders while their own
+// loads are in flight (nothing to poll: always true).
+struct NoPoll {
+  __device__ bool operator()() const { return true; }
+};
+template <int kT>
+struct PrefixPoll {
+  const Args& a;
+  const Op* ops;
+  const int* polls;
+  int first, count;
+  unsigned seq;
+  bool on;
+  __device__ bool operator()() const { return !on || poll_ops<kT>(a, ops, polls, first, count, seq); }
+};
 
 // ---------------------------------------------------------------------------
 // Activation preparation.  A produced activation is read from its producer's
@@ -343,11 +369,63 @@ __device__ __forceinline__ bool poll_ops(const Args& a, const Op* ops, const int
 // ---------------------------------------------------------------------------
 constexpr int kPre = 8;  // float4 of activation held per consumer thread
 
+// Float4 groups of tagged words (4 words each) a thread has in flight before it
+// checks the first: kBatch, or all kPre where the kernel's registers allow
+// (the shared preparation of the fused W8A8 kernels, the per-warp preparation
+// of the W8A32 kernels with 8 rows per warp).
+constexpr int kBatch = 4;
+
+// Loads groups [b, b + kB) of a thread's float4 groups of tagged words into
+// v, every load of the batch in flight before the first is checked, then
+// reloads the words without the tag until they carry it.  `addr(j)` is the
+// first word of group j (nullptr: outside the activation, v[j] = 0).
+// `between` runs once the batch's loads are issued (the wait prefix's polls).
+// False on a timeout or when `between` fails.
+template <int kB, int J, class Addr, class Between>
+__device__ __forceinline__ bool load_tagged_batch(int b, const Addr& addr, uint32_t tag, bool sys, uint64_t t0,
+                                                  float4 (&v)[J], const Between& between) {
+  uint64_t w[kB][4];
+  unsigned pending = 0;
+#pragma unroll
+  for (int j = 0; j < kB; ++j) {
+    v[b + j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    w[j][0] = w[j][1] = w[j][2] = w[j][3] = 0ull;
+    const uint64_t* p = addr(b + j);
+    if (p != nullptr) {
+      ld_relaxed_v2(p, w[j][0], w[j][1], sys);
+      ld_relaxed_v2(p + 2, w[j][2], w[j][3], sys);
+      pending |= 1u << j;
+    }
+  }
+  const bool ok = between();
+  unsigned ns = 32;
+  while (true) {
+#pragma unroll
+    for (int j = 0; j < kB; ++j)
+      if (((pending >> j) & 1u) && all_tagged4(w[j][0], w[j][1], w[j][2], w[j][3], tag)) {
+        v[b + j] = make_float4(word_value(w[j][0]), word_value(w[j][1]), word_value(w[j][2]), word_value(w[j][3]));
+        pending &= ~(1u << j);
+      }
+    if (pending == 0) return ok;
+    if (!ok || global_timer_ns() - t0 > kWaitLimitNs) return false;
+    poll_backoff(ns);
+#pragma unroll
+    for (int j = 0; j < kB; ++j)
+      if ((pending >> j) & 1u) {
+        const uint64_t* p = addr(b + j);
+        ld_relaxed_v2(p, w[j][0], w[j][1], sys);
+        ld_relaxed_v2(p + 2, w[j][2], w[j][3], sys);
+      }
+  }
+}
+
 // Shared preparation: consumer thread t holds columns 4t + 4 kT j, j < J
-// (the whole activation for n <= 4 kT kPre).  False on a timeout.
-template <int kT, int J>
+// (the whole activation for n <= 4 kT kPre), read in batches of kBatch groups
+// (load_tagged_batch); the wait prefix's polls run while the first batch is
+// in flight.  False on a timeout or when `between` fails.
+template <int kT, int J, int kMaxB, class Between>
 __device__ __forceinline__ bool cta_x_load(const Op& op, const uint64_t* m, uint32_t tag, bool sys,
-                                           float4 (&v)[J]) {
+                                           float4 (&v)[J], const Between& between) {
   const int t = static_cast<int>(threadIdx.x);
   const int n = op.n;
   if (m == nullptr) {
@@ -356,35 +434,18 @@ __device__ __forceinline__ bool cta_x_load(const Op& op, const uint64_t* m, uint
       const int c = 4 * kT * j + 4 * t;
       v[j] = c < n ? __ldcg(reinterpret_cast<const float4*>(op.x() + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    return true;
+    return between();
   }
-  // two groups (float4) at a time, both reloaded every round until tagged:
-  // few registers in flight, so the row loop around it keeps its own
   const uint64_t t0 = global_timer_ns();
+  const auto addr = [&](int j) -> const uint64_t* {
+    const int c = 4 * kT * j + 4 * t;
+    return c < n ? m + c : nullptr;
+  };
+  constexpr int kB = J < kMaxB ? J : kMaxB;
+  if (!load_tagged_batch<kB>(0, addr, tag, sys, t0, v, between)) return false;
 #pragma unroll
-  for (int j = 0; j < J; j += 2) {
-    v[j] = v[j + 1] = make_float4(0.f, 0.f, 0.f, 0.f);
-    const int c0 = 4 * kT * j + 4 * t, c1 = c0 + 4 * kT;
-    if (c0 >= n) continue;
-    const bool two = c1 < n;
-    unsigned ns = 32;
-    while (true) {
-      uint64_t a0, a1, a2, a3, b0 = 0, b1 = 0, b2 = 0, b3 = 0;
-      ld_relaxed_v2(m + c0, a0, a1, sys);
-      ld_relaxed_v2(m + c0 + 2, a2, a3, sys);
-      if (two) {
-        ld_relaxed_v2(m + c1, b0, b1, sys);
-        ld_relaxed_v2(m + c1 + 2, b2, b3, sys);
-      }
-      if (all_tagged4(a0, a1, a2, a3, tag) && (!two || all_tagged4(b0, b1, b2, b3, tag))) {
-        v[j] = make_float4(word_value(a0), word_value(a1), word_value(a2), word_value(a3));
-        if (two) v[j + 1] = make_float4(word_value(b0), word_value(b1), word_value(b2), word_value(b3));
-        break;
-      }
-      if (global_timer_ns() - t0 > kWaitLimitNs) return false;
-      poll_backoff(ns);
-    }
-  }
+  for (int b = kB; b < J; b += kB)
+    if (4 * kT * b < n && !load_tagged_batch<kB>(b, addr, tag, sys, t0, v, NoPoll{})) return false;
   return true;
 }
 
@@ -487,9 +548,12 @@ __device__ __forceinline__ float cta_quant(const float4 (&v)[J], const float* x,
 
 // Per-warp preparation (W8A32, when no two warps share a slice): the lane's
 // chunks k = 0, 1 of its slice, 16 columns each at col0 + 512k, as
-// v[4k + j] = columns col0 + 512k + 4j .. + 3.  False on a timeout.
+// v[4k + j] = columns col0 + 512k + 4j .. + 3, in batches of kB groups
+// (load_tagged_batch); the wait prefix's polls run while the first is in
+// flight.  False on a timeout or when `between` fails.
+template <int kB, class Between>
 __device__ __forceinline__ bool warp_x_load(const Op& op, const uint64_t* m, uint32_t tag, bool sys, int col0,
-                                            unsigned vmask, float4 (&v)[kPre]) {
+                                            unsigned vmask, float4 (&v)[kPre], const Between& between) {
   if (m == nullptr) {
 #pragma unroll
     for (int k = 0; k < 2; ++k)
@@ -498,33 +562,17 @@ __device__ __forceinline__ bool warp_x_load(const Op& op, const uint64_t* m, uin
         v[4 * k + j] = ((vmask >> k) & 1u)
                            ? __ldcg(reinterpret_cast<const float4*>(op.x() + col0 + 512 * k + 4 * j))
                            : make_float4(0.f, 0.f, 0.f, 0.f);
-    return true;
+    return between();
   }
-  // two groups (float4) at a time, both reloaded every round until tagged:
-  // few registers in flight, so the row loop around it keeps its own
   const uint64_t t0 = global_timer_ns();
+  const auto addr = [&](int q) -> const uint64_t* {
+    return ((vmask >> (q >> 2)) & 1u) ? m + col0 + 512 * (q >> 2) + 4 * (q & 3) : nullptr;
+  };
+  static_assert(kPre % kB == 0, "whole batches");
+  if (!load_tagged_batch<kB>(0, addr, tag, sys, t0, v, between)) return false;
 #pragma unroll
-  for (int q = 0; q < kPre; q += 2) {
-    v[q] = v[q + 1] = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (!((vmask >> (q >> 2)) & 1u)) continue;
-    const uint64_t* p0 = m + col0 + 512 * (q >> 2) + 4 * (q & 3);
-    const uint64_t* p1 = p0 + 4;
-    unsigned ns = 32;
-    while (true) {
-      uint64_t a0, a1, a2, a3, b0, b1, b2, b3;
-      ld_relaxed_v2(p0, a0, a1, sys);
-      ld_relaxed_v2(p0 + 2, a2, a3, sys);
-      ld_relaxed_v2(p1, b0, b1, sys);
-      ld_relaxed_v2(p1 + 2, b2, b3, sys);
-      if (all_tagged4(a0, a1, a2, a3, tag) && all_tagged4(b0, b1, b2, b3, tag)) {
-        v[q] = make_float4(word_value(a0), word_value(a1), word_value(a2), word_value(a3));
-        v[q + 1] = make_float4(word_value(b0), word_value(b1), word_value(b2), word_value(b3));
-        break;
-      }
-      if (global_timer_ns() - t0 > kWaitLimitNs) return false;
-      poll_backoff(ns);
-    }
-  }
+  for (int b = kB; b < kPre; b += kB)
+    if (!load_tagged_batch<kB>(b, addr, tag, sys, t0, v, NoPoll{})) return false;
   return true;
 }
 
@@ -585,11 +633,12 @@ __device__ __forceinline__ void warp_digits(const float4 (&v)[kPre], unsigned vm
 // or the fused W8A8 int8 copy (its scale into *xscale).  All consumer threads
 // call it.  False (on every thread) when an input row did not arrive in time.
 // J float4 of the activation per consumer thread (columns 4t + 4 kT j, j < J).
-template <Form F, int kT, bool kUnroll, int J>
+template <Form F, int kT, bool kUnroll, int J, class Between>
 __device__ __forceinline__ bool prep_cta_j(const Op& op, const uint64_t* m, uint32_t tag, bool sys,
-                                           unsigned char* xregion, float* red, float* red2, float* xscale) {
+                                           unsigned char* xregion, float* red, float* red2, float* xscale,
+                                           const Between& between) {
   float4 pre[J];
-  bool fail = !cta_x_load<kT, J>(op, m, tag, sys, pre);
+  bool fail = !cta_x_load<kT, J, F == Form::kW8A8Fused ? kPre : kBatch>(op, m, tag, sys, pre, between);
   fail = named_sync_or<kT>(fail);  // also: every consumer is done reading the shared region
   if (fail) return false;
   const int n = op.n;
@@ -607,14 +656,17 @@ __device__ __forceinline__ bool prep_cta_j(const Op& op, const uint64_t* m, uint
 // W8A32 activations of up to 4 kT * 4 columns hold only as many float4 per
 // thread as they need, unrolled in registers; wider ones (and the kernels'
 // rolled loops) take the full kPre.
-template <Form F, int kT, bool kUnroll>
+template <Form F, int kT, bool kUnroll, class Between>
 __device__ __forceinline__ bool prep_cta(const Op& op, const uint64_t* m, uint32_t tag, bool sys,
-                                         unsigned char* xregion, float* red, float* red2, float* xscale) {
+                                         unsigned char* xregion, float* red, float* red2, float* xscale,
+                                         const Between& between) {
   if constexpr (F == Form::kW8A32) {
-    if (op.n <= 4 * kT * 2) return prep_cta_j<F, kT, kUnroll, 2>(op, m, tag, sys, xregion, red, red2, xscale);
-    if (op.n <= 4 * kT * 4) return prep_cta_j<F, kT, kUnroll, 4>(op, m, tag, sys, xregion, red, red2, xscale);
+    if (op.n <= 4 * kT * 2)
+      return prep_cta_j<F, kT, kUnroll, 2>(op, m, tag, sys, xregion, red, red2, xscale, between);
+    if (op.n <= 4 * kT * 4)
+      return prep_cta_j<F, kT, kUnroll, 4>(op, m, tag, sys, xregion, red, red2, xscale, between);
   }
-  return prep_cta_j<F, kT, kUnroll, kPre>(op, m, tag, sys, xregion, red, red2, xscale);
+  return prep_cta_j<F, kT, kUnroll, kPre>(op, m, tag, sys, xregion, red, red2, xscale, between);
 }
 
 // A consumer warp's role in an op: its slice, its rows of a stage, and the
@@ -726,11 +778,12 @@ __global__ void __launch_bounds__((kW + 1) * 32, 1) gemv_chain_kernel(const Args
         // once a wait has expired in this CTA, later ops wait for nothing
         // (their rows are not produced): the launch ends in bounded time
         const bool broken = *sm.broken != 0;
-        if (kTags && wait > known && op.poll_count > 0 && !broken) {
-          // ops of the wait prefix that the activation's producer does not imply
-          fail = !poll_ops<kT>(a, ops, polls, op.poll_first, op.poll_count, seq);
-          fail = named_sync_or<kT>(fail);
-        }
+        // ops of the wait prefix that the activation's producer does not imply;
+        // polled while the activation's own loads are in flight when it changes
+        const bool need_poll = kTags && wait > known && op.poll_count > 0;  // CTA-uniform
+        const bool do_poll = need_poll && !broken;
+        const PrefixPoll<kT> prefix{a, ops, polls, op.poll_first, op.poll_count, seq, do_poll};
+        bool polled = false;
         n = op.n; d = op.d; Gr = op.G(); R = op.R; base = op.unit_base; y = op.y;
         if constexpr (kEpi) {
           Ru = op.Ru();
@@ -747,6 +800,12 @@ __global__ void __launch_bounds__((kW + 1) * 32, 1) gemv_chain_kernel(const Args
           const uint64_t* src_m =
               kTags && op.src >= 0 && !broken ? a.mirror + mirror_half(a, seq) + ops[op.src].mirror : nullptr;
           const uint32_t src_tag = row_tag(seq, op.src);
+          // No warp polls while another still computes on this SM: the
+          // consumers first finish their units of the previous phase (the
+          // activation needs their rows anyway), and they start the new op
+          // together once it has arrived.
+          const bool gate = kTags && (op.src >= 0 || need_poll);  // CTA-uniform
+          if (gate) named_sync<kT>();
           if constexpr (F == Form::kW8A8) {
             xscale = __ldcg(op.xs);
 #pragma unroll
@@ -757,12 +816,19 @@ __global__ void __launch_bounds__((kW + 1) * 32, 1) gemv_chain_kernel(const Args
           } else if (F == Form::kW8A32 && op.S == kW && op.norm_w == nullptr) {
             // every warp owns its slice: prepare it in registers, no barrier
             float4 pre[kPre];
-            if (!warp_x_load(op, src_m, src_tag, a.world > 1, col0, vmask, pre)) fail = true;
+            // (one batch of loads, except in the narrow-row kernels, whose
+            // registers leave room for half of it)
+            if (!warp_x_load<kRB == 8 ? kPre : kBatch>(op, src_m, src_tag, a.world > 1, col0, vmask, pre, prefix))
+              fail = true;
+            if (gate) fail = named_sync_or<kT>(fail);
+            polled = true;
             if constexpr (F == Form::kW8A32) warp_digits(pre, vmask, xd, fac);
           } else {
             float t_scale = 0.f;
-            if (!prep_cta<F, kT, !kTags>(op, src_m, src_tag, a.world > 1, smem + a.x_off, sm.red, sm.red2, &t_scale))
+            if (!prep_cta<F, kT, !kTags>(op, src_m, src_tag, a.world > 1, smem + a.x_off, sm.red, sm.red2, &t_scale,
+                                         prefix))
               fail = true;
+            polled = true;
             xscale = t_scale;
             if constexpr (F == Form::kW8A32) {
               const int8_t* planes = reinterpret_cast<const int8_t*>(smem + a.x_off);
@@ -784,6 +850,10 @@ __global__ void __launch_bounds__((kW + 1) * 32, 1) gemv_chain_kernel(const Args
                                             : make_uint4(0, 0, 0, 0);
             }
           }
+        }
+        if (need_poll && !polled) {
+          if (do_poll) fail = !poll_ops<kT>(a, ops, polls, op.poll_first, op.poll_count, seq) || fail;
+          fail = named_sync_or<kT>(fail);
         }
         if (fail) {
           record_error(a, kDevChainTimeout);

@@ -197,19 +197,24 @@ class PeerShardedLinear:
         rank must have finished that step."""
         return read_tagged_logits(self.base + self.HEADER, self.d, step & 1, step)
 
-    def forward(self, x, stream=None, fused: bool = True):
+    def forward(self, x, stream=None, fused: bool = True, out=None):
         """One step: this rank's rows to every rank, then the argmax into
-        self.out -- one launch (fused) or the GEMV and the wait kernel."""
+        `out` (an int64 device scalar; default self.out) -- one launch (fused)
+        or the GEMV and the wait kernel.  Returns the tensor written."""
         import torch
 
         from ._lib import check
 
         st = torch.cuda.current_stream().cuda_stream if stream is None else stream
+        if out is None:
+            out = self.out
+        elif out.dtype != torch.int64 or out.numel() != 1 or out.device != self.out.device:
+            raise ValueError("out must be one int64 element on this rank's device")
         if fused:
             check(self.lib.mli_gemv_rowshard_argmax(
                 self.form_code, self._peer_logits, self.base, x.data_ptr(), self.w_q.data_ptr(),
                 self.w_s.data_ptr(), self.n, self.shard.rows, self.shard.r0, self.d, self.rank, self.world, 64,
-                self._shard_rows, self.out.data_ptr(), self.timeout_us, st), "mli_gemv_rowshard_argmax")
+                self._shard_rows, out.data_ptr(), self.timeout_us, st), "mli_gemv_rowshard_argmax")
         else:
             check(self.lib.mli_gemv_rowshard(self.form_code, self._peer_logits, self.base + 128, x.data_ptr(),
                                              self.w_q.data_ptr(), self.w_s.data_ptr(), self.n, self.shard.rows,
@@ -217,10 +222,10 @@ class PeerShardedLinear:
                   "mli_gemv_rowshard")
             check(self.lib.mli_rowshard_wait_argmax(self.form_code, self.n, self.base + self.HEADER,
                                                     self.base + 128, self._shard_rows, self.world, self.d,
-                                                    self.out.data_ptr(), self.timeout_us, st),
+                                                    out.data_ptr(), self.timeout_us, st),
                   "mli_rowshard_wait_argmax")
         self.steps += 1
-        return self.out
+        return out
 
     def close(self):
         import torch
