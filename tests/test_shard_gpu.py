@@ -52,19 +52,54 @@ def _worker(rank, world, port, d, n, form, q, fused=False):
                                     form=form)
             same, arg = True, True
             full_bits = full.cpu().numpy().view("uint32")
+            given = torch.full((), -1, dtype=torch.int64, device=dev)
             for step in range(5):  # both logits halves, several times
-                out = lin.forward(x)
+                # odd steps write the argmax into a tensor of the caller's
+                out = lin.forward(x, out=given) if step % 2 else lin.forward(x)
                 torch.cuda.synchronize()
                 dist.barrier()  # every rank's words of this step have landed
                 got = lin.read_logits(step)  # also checks every word's step tag
                 same = same and bool((got.view("uint32") == full_bits).all())
-                arg = arg and int(out.item()) == want
+                arg = arg and int(out.item()) == want and (out is given) == (step % 2 == 1)
                 dist.barrier()
             lin.close()
         q.put((rank, same, arg, ops.device_error()))
         dist.barrier()
     finally:
         dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("form", ["w8a32", "w8a8"])
+def test_peer_sharded_classifier_one_gpu(form):
+    """world == 1: the fused GEMV + argmax without a process group, the argmax
+    written into the tensor given to forward() and the logits bit-exact."""
+    from minillama_infra_b200 import ops, synth
+    from minillama_infra_b200.shard import PeerShardedLinear
+
+    dev = torch.device("cuda", 0)
+    d, n = 128256 // 8 + 3, 2048
+    w_q, w_s = synth.weights_gpu(d, n, seed=99, device=dev)
+    x = synth.activation_gpu(n, 7, dev, outliers=(form == "w8a8"))
+    full = torch.empty(d, dtype=torch.float32, device=dev)
+    if form == "w8a32":
+        ops.matmul_int8(full, x, w_q, w_s, n, d, 64)
+    else:
+        ops.matmul_dp4a_fused(full, x, w_q, w_s, n, d, 64)
+    want = int(torch.argmax(full).item())
+    lin = PeerShardedLinear(w_q, w_s, d, n, 0, 1, form=form)
+    given = torch.full((), -1, dtype=torch.int64, device=dev)
+    try:
+        for step in range(3):
+            out = lin.forward(x, out=given)
+            torch.cuda.synchronize()
+            assert out is given and int(given.item()) == want
+            got = lin.read_logits(step)
+            assert (got.view("uint32") == full.cpu().numpy().view("uint32")).all()
+        with pytest.raises(ValueError):
+            lin.forward(x, out=torch.zeros(2, dtype=torch.int64, device=dev))
+        assert ops.device_error() == 0
+    finally:
+        lin.close()
 
 
 @pytest.mark.parametrize("fused", [False, True], ids=["nccl", "p2p"])
