@@ -302,7 +302,7 @@ __device__ __forceinline__ uint32_t mirror_half(const Args& a, unsigned seq) { r
 
 // Consumer threads check, by their mirrors' tags, that every row of the ops
 // polls[first, first + count) was written in this launch.  The polled ops'
-// rows form one index space; a thread's words of a round (up to 8) are all in
+// rows form one index space; a thread's words of one pass (up to 8) are all in
 // flight before the first is checked.  False if a row did not arrive in time.
 template <int kT>
 __device__ __forceinline__ bool poll_ops(const Args& a, const Op* ops, const int* polls, int first, int count,
