@@ -36,7 +36,7 @@
 //    prepare it: an optional RMSNorm (weight * (x / sqrt(mean(x^2) + 1e-5)),
 //    the reference's rmsnorm_cuda / fused_add_rmsnorm_cuda before the q/k/v
 //    and gate/up projections, recomputed by every CTA from the whole vector),
-//    then W8A32 digit planes (digit_quad) or the fused W8A8 quantisation
+//    then W8A32 digit-pair planes (digit_quad) or the fused W8A8 quantisation
 //    (quant_quad) -- once per CTA into shared memory, or, when every warp owns
 //    its own slice of the row (W8A32 with n = 8192, no norm), by each warp in
 //    registers without a barrier.
@@ -482,7 +482,7 @@ __device__ __forceinline__ void cta_rmsnorm(float4 (&v)[J], int n, const float* 
   }
 }
 
-// W8A32 digit planes and group factors (digit_quad) of the held activation
+// W8A32 digit-pair planes and group factors (digit_quad) of the held activation
 // into shared memory.
 // kUnroll: the held values stay in registers; rolled (the kernels with the
 // dependency code), they go through a per-thread local array instead, which
@@ -576,7 +576,8 @@ __device__ __forceinline__ bool warp_x_load(const Op& op, const uint64_t* m, uin
   return true;
 }
 
-// The lane's digit planes of chunks 0, 1 in registers.  The quad of lanes
+// The lane's digit pairs of chunks 0, 1 in registers (xd as load_digit_chunk
+// lays them out).  The quad of lanes
 // holding a group (group lane/4 + 8k of the slice) finds the group's max
 // together, so digits and factors are exactly those of digit_quad.
 __device__ __forceinline__ void warp_digits(const float4 (&v)[kPre], unsigned vmask, uint4 (&xd)[2][4],
@@ -603,33 +604,36 @@ __device__ __forceinline__ void warp_digits(const float4 (&v)[kPre], unsigned vm
       scale_up = 0.f;
       factor = 0.f;
     }
-    uint32_t words[4][4];  // [plane][word]
+    // words[pair][w]: the pair plane's int16 values of columns 2w, 2w + 1
+    uint32_t words[2][8];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float4 q = v[4 * k + j];
-      uint32_t t0[4], t1[4], t2[4], t3[4];
-      digits4(q.x * scale_up, t0);
-      digits4(q.y * scale_up, t1);
-      digits4(q.z * scale_up, t2);
-      digits4(q.w * scale_up, t3);
-#pragma unroll
-      for (int p = 0; p < 4; ++p) {
-        const uint32_t lo = __byte_perm(t0[p], t1[p], 0x0040);
-        const uint32_t hi = __byte_perm(t2[p], t3[p], 0x0040);
-        words[p][j] = __byte_perm(lo, hi, 0x5410);
-      }
+      int a1, a2, b1, b2, c1, c2, d1, d2;
+      digit_pairs(q.x * scale_up, a1, a2);
+      digit_pairs(q.y * scale_up, b1, b2);
+      digit_pairs(q.z * scale_up, c1, c2);
+      digit_pairs(q.w * scale_up, d1, d2);
+      words[0][2 * j] = pack16(a1, b1);
+      words[0][2 * j + 1] = pack16(c1, d1);
+      words[1][2 * j] = pack16(a2, b2);
+      words[1][2 * j + 1] = pack16(c2, d2);
     }
     const bool valid = (vmask >> k) & 1u;
 #pragma unroll
-    for (int p = 0; p < 4; ++p)
-      xd[k][p] = valid ? make_uint4(words[p][0], words[p][1], words[p][2], words[p][3]) : make_uint4(0, 0, 0, 0);
+    for (int p = 0; p < 2; ++p)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t* w = words[p] + 4 * h;
+        xd[k][2 * p + h] = valid ? make_uint4(w[0], w[1], w[2], w[3]) : make_uint4(0, 0, 0, 0);
+      }
     fac[k] = valid ? factor : 0.f;
   }
 }
 
 // The activation prologue runs once per activation change.
 
-// Shared preparation into shared memory: W8A32 digit planes + group factors,
+// Shared preparation into shared memory: W8A32 digit-pair planes + group factors,
 // or the fused W8A8 int8 copy (its scale into *xscale).  All consumer threads
 // call it.  False (on every thread) when an input row did not arrive in time.
 // J float4 of the activation per consumer thread (columns 4t + 4 kT j, j < J).
@@ -763,7 +767,7 @@ __global__ void __launch_bounds__((kW + 1) * 32, 1) gemv_chain_kernel(const Args
     bool warp_on = false;
     unsigned vmask = 0;
     float xscale = 0.f;
-    uint4 xd[2][4];  // W8A32 digit planes of chunks 0, 1
+    uint4 xd[2][4];  // W8A32 digit pairs of chunks 0, 1 (load_digit_chunk)
     float fac[2];
     uint4 xv[4];     // W8A8 int8 chunks 0..3
 
@@ -836,10 +840,12 @@ __global__ void __launch_bounds__((kW + 1) * 32, 1) gemv_chain_kernel(const Args
 #pragma unroll
               for (int k = 0; k < 2; ++k) {
                 const bool v = (vmask >> k) & 1u;
+                if (v) {
+                  load_digit_chunk(planes, n, col0 + 512 * k, xd[k]);
+                } else {
 #pragma unroll
-                for (int p = 0; p < 4; ++p)
-                  xd[k][p] = v ? *reinterpret_cast<const uint4*>(planes + p * n + col0 + 512 * k)
-                               : make_uint4(0, 0, 0, 0);
+                  for (int p = 0; p < 4; ++p) xd[k][p] = make_uint4(0, 0, 0, 0);
+                }
                 fac[k] = v ? facs[(col0 + 512 * k) >> 6] : 0.f;
               }
             } else {

@@ -29,9 +29,9 @@
 //  * The activation is read only after griddepcontrol.wait, straight from
 //    global memory (it was just written, so it sits in L2), and prepared once
 //    per CTA in shared memory:
-//      W8A32: split exactly enough for fp32 parity into four int8 digit planes
-//      under a per-group power of two (see x_digits_prologue), so every
-//      weight chunk is 16 dp4a of exact int32 partials plus three fp32 ops
+//      W8A32: split exactly enough for fp32 parity into two int16 planes of
+//      digit pairs under a per-group power of two (see x_digits_prologue), so
+//      every weight chunk is 16 dp2a of exact int32 sums plus a few fp32 ops
 //      instead of 16 int8->fp32 conversions and 16 FMAs;
 //      W8A8 fused: quantised in the prologue, bit-identical to
 //      quantize_activation.
@@ -210,7 +210,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_stream_kernel(const StreamAr
   float* staged = reinterpret_cast<float*>(smem + a.out_off);
   const int cta_row0 = begin * a.R;
   float xscale = 0.f;
-  uint4 xd[2][4];  // W8A32 digit planes of chunks 0, 1
+  uint4 xd[2][4];  // W8A32 digit pairs of chunks 0, 1 (load_digit_chunk)
   float fac[2];
   uint4 xv[4];     // W8A8 int8 chunks 0..3
   if constexpr (F == Form::kW8A32) {
@@ -221,10 +221,12 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_stream_kernel(const StreamAr
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
       const bool v = (vmask >> k) & 1u;
+      if (v) {
+        load_digit_chunk(planes, a.n, col0 + 512 * k, xd[k]);
+      } else {
 #pragma unroll
-      for (int p = 0; p < 4; ++p)
-        xd[k][p] = v ? *reinterpret_cast<const uint4*>(planes + p * a.n + col0 + 512 * k)
-                     : make_uint4(0, 0, 0, 0);
+        for (int p = 0; p < 4; ++p) xd[k][p] = make_uint4(0, 0, 0, 0);
+      }
       fac[k] = v ? facs[(col0 + 512 * k) >> 6] : 0.f;
     }
   } else if constexpr (F == Form::kW8A8Fused) {
@@ -451,7 +453,7 @@ bool plan_stream(Form f, const DeviceInfo& dev, int n, int d, bool peer, StreamA
   a->R = R;
   a->n_stages = (d + R - 1) / R;
   a->stage_bytes = static_cast<uint32_t>(R) * n + static_cast<uint32_t>(R) * a->G * 4u;
-  // W8A32: four digit planes + per-group factors; fused W8A8: the int8 x.
+  // W8A32: two digit-pair planes + per-group factors; fused W8A8: the int8 x.
   size_t xbytes =
       (f == Form::kW8A32) ? 4u * n + (n / kGroup) * 4u : (f == Form::kW8A8 ? 0u : static_cast<size_t>(n));
   // Row-sharded launches stage a CTA's output rows (at most

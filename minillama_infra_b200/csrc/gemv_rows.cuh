@@ -2,9 +2,9 @@
 // shared by the single-GEMV streaming kernel (gemv_g64.cu) and the chained
 // kernel (gemv_chain.cu), so that both give bit-identical rows.
 //
-//  * Activation prologues: the fp32 activation as four int8 digit planes
-//    (W8A32) or quantised per token (fused W8A8), written once per CTA into
-//    shared memory.
+//  * Activation prologues: the fp32 activation as two int16 planes of 7-bit
+//    digit pairs (W8A32) or quantised per token (fused W8A8), written once per
+//    CTA into shared memory.
 //  * Row kernels: one warp computes RB consecutive rows of one slice of a
 //    stage held in shared memory.
 #pragma once
@@ -41,26 +41,50 @@ __device__ __forceinline__ float4 load_x4(const float* p) {
 // Activation prologues (consumer threads, once per CTA)
 // ---------------------------------------------------------------------------
 // W8A32 represents each 64-column group of the fp32 activation exactly enough
-// for fp32 parity as four signed 7-bit int8 "digit planes" under a per-group
-// power of two:  x~ = 2^-E (d1 + d2 2^-7 + d3 2^-14 + d4 2^-21),
+// for fp32 parity as four signed 7-bit digits under a per-group power of two:
+//   x~ = 2^-E (d1 + d2 2^-7 + d3 2^-14 + d4 2^-21),
 // with E chosen so that max|x_g| * 2^E lies in [32, 64).  Every digit is in
 // [-64, 64] and |x - x~| <= 2^-27 max|x_g| (well below the fp32 rounding of
-// the dot product itself).  A weight chunk then costs 16 dp4a of exact int32
-// partials P1..P4, combined as Q = 128 P1 + P2 and R = 128 P3 + P4 (both
-// below 2^24, so exact in fp32):  sum_j w_j x~_j = 2^-(E+7) (Q + 2^-14 R).
+// the dot product itself).  The digits are kept in pairs, as two signed 14-bit
+// planes C1 = 128 d1 + d2 and C2 = 128 d3 + d4 (int16, |C| <= 8256): a weight
+// chunk of 16 columns costs 16 dp2a (int16 x int8 pairs) of exact int32 sums
+//   Q = sum w C1 = 128 P1 + P2,  R = sum w C2 = 128 P3 + P4
+// (P the four digit-plane dots; both below 2^24, so exact in fp32):
+//   sum_j w_j x~_j = 2^-(E+7) (Q + 2^-14 R).
+// With u = x 2^E: C1 = rint(128 u) and C2 = rint((128 u - C1) 2^14), ties to
+// even -- the same integers as the four digits taken one at a time (each
+// digit's remainder is exact, and adding 128 d1, an even integer, leaves a
+// tie's rounding unchanged).
 //
-// rint(u) for |u| <= 64 is (u + 1.5*2^23) - 1.5*2^23 (ties to even), and the
-// low byte of the bits of u + 1.5*2^23 is the digit's two's-complement byte.
+// rint(s) for |s| < 2^22 is (s + 1.5*2^23) - 1.5*2^23 (ties to even), and the
+// bits of s + 1.5*2^23 minus those of 1.5*2^23 are rint(s) as an integer.
 constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
 
-// Digit bytes of one value; `u` is the value already scaled by 2^E.
-__device__ __forceinline__ void digits4(float u, uint32_t (&t)[4]) {
-#pragma unroll
-  for (int p = 0; p < 4; ++p) {
-    const float r = u + kRoundMagic;
-    t[p] = __float_as_uint(r);
-    if (p < 3) u = (u - (r - kRoundMagic)) * 128.0f;
-  }
+// The two 14-bit digit pairs of one value; `u` is the value already scaled
+// by 2^E.
+__device__ __forceinline__ void digit_pairs(float u, int& c1, int& c2) {
+  const float s = u * 128.0f;
+  const float r = s + kRoundMagic;
+  c1 = __float_as_int(r) - __float_as_int(kRoundMagic);
+  const float t = (s - (r - kRoundMagic)) * 16384.0f;
+  c2 = __float_as_int(t + kRoundMagic) - __float_as_int(kRoundMagic);
+}
+
+// Two int16 (low halves of a, b) as one word: a in the low half.
+__device__ __forceinline__ uint32_t pack16(int a, int b) {
+  return __byte_perm(static_cast<uint32_t>(a), static_cast<uint32_t>(b), 0x5410);
+}
+
+// Shared-memory digit planes: [2][n] int16 (C1 then C2), then the group
+// factors.  A lane's 16 columns cc .. cc+15 (cc a multiple of 16) as
+// xd[0..1] = C1 of columns cc..cc+7, cc+8..cc+15 and xd[2..3] = C2 likewise.
+__device__ __forceinline__ void load_digit_chunk(const int8_t* planes, int n, int cc, uint4 (&xd)[4]) {
+  const uint4* p1 = reinterpret_cast<const uint4*>(planes + 2 * cc);
+  const uint4* p2 = reinterpret_cast<const uint4*>(planes + 2 * n + 2 * cc);
+  xd[0] = p1[0];
+  xd[1] = p1[1];
+  xd[2] = p2[0];
+  xd[3] = p2[1];
 }
 
 // Digit planes and group factor of the four columns c..c+3 of x held by this
@@ -83,25 +107,22 @@ __device__ __forceinline__ void digit_quad(const float4 v, bool valid, int c, in
     scale_up = 0.f;
     factor = 0.f;
   }
-  uint32_t t0[4], t1[4], t2[4], t3[4];
-  digits4(v.x * scale_up, t0);
-  digits4(v.y * scale_up, t1);
-  digits4(v.z * scale_up, t2);
-  digits4(v.w * scale_up, t3);
+  int a1, a2, b1, b2, c1, c2, d1, d2;
+  digit_pairs(v.x * scale_up, a1, a2);
+  digit_pairs(v.y * scale_up, b1, b2);
+  digit_pairs(v.z * scale_up, c1, c2);
+  digit_pairs(v.w * scale_up, d1, d2);
   if (valid) {
-#pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      const uint32_t lo = __byte_perm(t0[p], t1[p], 0x0040);
-      const uint32_t hi = __byte_perm(t2[p], t3[p], 0x0040);
-      *reinterpret_cast<uint32_t*>(planes + p * n + c) = __byte_perm(lo, hi, 0x5410);
-    }
+    *reinterpret_cast<uint2*>(planes + 2 * c) = make_uint2(pack16(a1, b1), pack16(c1, d1));
+    *reinterpret_cast<uint2*>(planes + 2 * n + 2 * c) = make_uint2(pack16(a2, b2), pack16(c2, d2));
     if ((lane & 15) == 0) fac[c >> 6] = factor;
   }
 }
 
-// Writes the digit planes [4][n] int8 and the per-group factors 2^-(E+7)
-// [n/64] of x into shared memory.  Thread t handles columns 4t + 1024j, so
-// each half-warp holds one whole 64-column group.
+// Writes the digit planes [2][n] int16 and the per-group factors 2^-(E+7)
+// [n/64] of x into shared memory (4n bytes, then the factors).  Thread t
+// handles columns 4t + 1024j, so each half-warp holds one whole 64-column
+// group.
 template <bool kL2 = false>
 __device__ __forceinline__ void x_digits_prologue(const float* x, int n, int8_t* planes,
                                                   float* fac) {
@@ -158,6 +179,20 @@ __device__ __forceinline__ float x_quant_prologue(const float* x, int n, int8_t*
 // ---------------------------------------------------------------------------
 // Consumer row kernels (one warp, one slice of RB consecutive rows)
 // ---------------------------------------------------------------------------
+// Sum over the 16 columns of a weight chunk of w * C, C the int16 digit pairs
+// of columns 0..7 (lo) and 8..15 (hi).
+__device__ __forceinline__ int dp2a_chunk(const uint4 w, const uint4 lo, const uint4 hi) {
+  int acc = __dp2a_lo(static_cast<int>(lo.x), static_cast<int>(w.x), 0);
+  acc = __dp2a_hi(static_cast<int>(lo.y), static_cast<int>(w.x), acc);
+  acc = __dp2a_lo(static_cast<int>(lo.z), static_cast<int>(w.y), acc);
+  acc = __dp2a_hi(static_cast<int>(lo.w), static_cast<int>(w.y), acc);
+  acc = __dp2a_lo(static_cast<int>(hi.x), static_cast<int>(w.z), acc);
+  acc = __dp2a_hi(static_cast<int>(hi.y), static_cast<int>(w.z), acc);
+  acc = __dp2a_lo(static_cast<int>(hi.z), static_cast<int>(w.w), acc);
+  acc = __dp2a_hi(static_cast<int>(hi.w), static_cast<int>(w.w), acc);
+  return acc;
+}
+
 __device__ __forceinline__ int dp4a_chunk(const uint4 w, const uint4 x) {
   int acc = __dp4a(static_cast<int>(w.x), static_cast<int>(x.x), 0);
   acc = __dp4a(static_cast<int>(w.y), static_cast<int>(x.y), acc);
@@ -168,8 +203,8 @@ __device__ __forceinline__ int dp4a_chunk(const uint4 w, const uint4 x) {
 
 // Per-lane W8A32 partials of RB consecutive rows (row stride n bytes in the
 // stage, scale-row stride G floats).  Per 16-byte chunk k (group lane/4 + 8k):
-// four digit-plane dots, combined exactly into Q, R, then one rounding into
-// fp32 and one FMA with the group scale; chunks in order k = 0, 1.
+// the two digit-pair dots Q, R (exact int32), then one rounding into fp32
+// and one FMA with the group scale; chunks in order k = 0, 1.
 template <int RB>
 __device__ __forceinline__ void rows_w8a32(const int8_t* wr, const float* sr, int n, int G,
                                            int nvalid, const uint4 (&xd)[2][4],
@@ -192,8 +227,8 @@ __device__ __forceinline__ void rows_w8a32(const int8_t* wr, const float* sr, in
     float acc = 0.f;
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
-      const int q = dp4a_chunk(w[r][k], xd[k][0]) * 128 + dp4a_chunk(w[r][k], xd[k][1]);
-      const int rr = dp4a_chunk(w[r][k], xd[k][2]) * 128 + dp4a_chunk(w[r][k], xd[k][3]);
+      const int q = dp2a_chunk(w[r][k], xd[k][0], xd[k][1]);
+      const int rr = dp2a_chunk(w[r][k], xd[k][2], xd[k][3]);
       const float v = fmaf(static_cast<float>(rr), 0x1p-14f, static_cast<float>(q));
       acc = fmaf(v * fac[k], sc[r][k], acc);
     }
